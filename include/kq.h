@@ -1,0 +1,216 @@
+/*
+ * kq.h -- C ABI of the B200 quantized routed-expert engine (libkq.so).
+ *
+ * Two families of entry points live here.
+ *
+ * 1. Reference-compatible symbols (bakan_cpu_expert_*).  Same names, argument
+ *    meaning, host-pointer I/O and return convention (0 = OK, -1 = error with a
+ *    "[kandiga] ..." line on stderr) as the reference's native expert library,
+ *    so the reference's own ctypes binding (_CPUExpertLib) can load libkq.so
+ *    unchanged.  Expert weights are read once from the BKEX layer files at init
+ *    and kept resident in HBM; each call copies x to the device, runs the
+ *    sm_100a kernels and copies the result back (synchronous, like the
+ *    reference).
+ *
+ * 2. Device-pointer entry points (kq_*).  All pointers are device pointers
+ *    unless stated otherwise, every call takes a cudaStream_t (passed as void*)
+ *    and is asynchronous.  Return value: 0 OK, >0 argument/setup error
+ *    (KQ_ERR_*); kernel-side conditions (bad expert id, wait timeout) are
+ *    latched in a device status word read with kq_status_read().  No call on
+ *    the hot path allocates memory: scratch comes from a caller-provided
+ *    workspace whose size is queried up front.
+ *
+ * Reference interfaces replaced (paths relative to the kandiga project root)
+ * are cited beside each declaration.
+ */
+#ifndef KQ_H
+#define KQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- codes ----------------------------------------------------------------- */
+#define KQ_OK 0
+#define KQ_ERR_ARG 1
+#define KQ_ERR_CUDA 2
+#define KQ_ERR_ALLOC 3
+#define KQ_ERR_IO 4
+#define KQ_ERR_FORMAT 5
+#define KQ_ERR_UNSUPPORTED 6
+#define KQ_ERR_WORKSPACE 7
+
+/* device status bits (kq_status_read) */
+#define KQ_DEV_BAD_EXPERT 1u  /* an expert id outside [0, num_experts): output rows zeroed */
+#define KQ_DEV_WAIT_TIMEOUT 2u /* a bounded device-side wait gave up */
+#define KQ_DEV_BAD_INDEX 4u   /* a token/slot index outside its range */
+
+/* element types */
+#define KQ_DT_F16 0
+#define KQ_DT_BF16 1
+#define KQ_DT_F32 2
+
+/* activations */
+#define KQ_ACT_SILU 0      /* silu(g) * u  (kandiga/metal/kandiga_cpu_expert.m:384-394) */
+#define KQ_ACT_GELU_TANH 1 /* gelu_tanh(g) * u (kandiga/metal/kandiga_cpu_expert_lg.m:237-250) */
+
+/* ---- 1. reference-compatible ABI ------------------------------------------- */
+
+/* replaces kandiga/metal/kandiga_cpu_expert.h:40 (bakan_cpu_expert_init).
+ * Reads packed_dir/layer_XX.bin (BKEX, kandiga/_pack_experts.py:95-132) for
+ * XX in [0, num_layers), takes hidden/inter/bits from the header the way
+ * kandiga/metal/kandiga_cpu_expert_lg.m:67-117 does, repacks every expert into
+ * the HBM table.  Returns NULL on failure. */
+void* bakan_cpu_expert_init(const char* packed_dir, int num_layers);
+
+/* replaces kandiga/metal/kandiga_cpu_expert.h:51 (fp32 host in/out).
+ * output_f32 [num_experts][hidden], unweighted per-expert outputs. */
+int bakan_cpu_expert_mlp(void* engine, int layer_idx, const float* x_f32,
+                         const int32_t* expert_indices, int num_experts, float* output_f32);
+
+/* replaces kandiga/metal/kandiga_cpu_expert.h:65 (fp16 host in/out). */
+int bakan_cpu_expert_mlp_f16(void* engine, int layer_idx, const void* x_f16,
+                             const int32_t* expert_indices, int num_experts, void* output_f16);
+
+/* replaces kandiga/metal/kandiga_cpu_expert.h:79 (bf16 host in, fp16 host out). */
+int bakan_cpu_expert_mlp_bf16(void* engine, int layer_idx, const void* x_bf16,
+                              const int32_t* expert_indices, int num_experts, void* output_f16);
+
+/* replaces kandiga/metal/kandiga_cpu_expert.m:564 (bakan_cpu_expert_mlp_batch_f16):
+ * x [num_tokens][hidden] fp16, indices [num_tokens][K], output [num_tokens][K][hidden] fp16. */
+int bakan_cpu_expert_mlp_batch_f16(void* engine, int layer_idx, const void* x_f16_batch,
+                                   const int32_t* indices_batch, int num_tokens, int K,
+                                   void* output_f16_batch);
+
+/* replaces kandiga/metal/kandiga_cpu_expert.m:773 (bakan_cpu_expert_mlp_prefill_f16).
+ * CSR-grouped prefill: the groups describe which (token, k) pairs use which
+ * expert; output [num_tokens][K][hidden] fp16 at (token, k_pos). */
+int bakan_cpu_expert_mlp_prefill_f16(void* engine, int layer_idx, const void* x_f16,
+                                     int num_tokens, int K, int hidden_size,
+                                     const int32_t* sorted_token_indices,
+                                     const int32_t* sorted_expert_indices,
+                                     const int32_t* sorted_k_positions,
+                                     const int32_t* group_starts, const int32_t* unique_experts,
+                                     int num_unique_experts, void* output_f16);
+
+/* replaces kandiga/metal/kandiga_cpu_expert.m:847 (bakan_cpu_expert_pread_batch):
+ * copies the raw BKEX bytes of the listed experts into a caller host buffer
+ * (num_experts_to_read * expert_size bytes), reconstructed from the HBM table. */
+int bakan_cpu_expert_pread_batch(void* engine, int layer_idx, const int32_t* expert_ids,
+                                 int num_experts_to_read, void* output_buffer);
+
+/* replaces kandiga/metal/kandiga_cpu_expert.h:91 */
+void bakan_cpu_expert_destroy(void* engine);
+
+/* replaces kandiga/metal/kandiga_cpu_expert.h:96 */
+int bakan_cpu_expert_num_layers(void* engine);
+
+/* ---- 2. device ABI ------------------------------------------------------------ */
+
+typedef struct kq_table kq_table; /* HBM-resident routed-expert table (all layers) */
+typedef struct kq_qmat kq_qmat;   /* HBM-resident dense quantized matrix */
+
+typedef struct {
+    int32_t num_layers;
+    int32_t num_experts;
+    int32_t hidden;     /* H: gate/up input, down output */
+    int32_t inter;      /* I: moe_intermediate */
+    int32_t bits;       /* 3 or 4 */
+    int32_t group_size; /* 64 */
+    int32_t sb_dtype;   /* KQ_DT_F16 or KQ_DT_BF16: per-group scale/bias storage */
+    int32_t activation; /* KQ_ACT_* */
+} kq_table_desc;
+
+/* One MLX-layout quantized matrix, optionally stacked over experts.
+ * weight: 3-bit -> bytes [rows][cols*3/8] (== MLX uint32 [rows][cols*3/32]),
+ *         4-bit -> uint32 [rows][cols/8]; nibble / 3-bit field j at bit bits*j,
+ *         LSB first (kandiga/metal/kandiga_cpu_expert.m:194-201,285-291).
+ * scales, biases: 16-bit [rows][cols/group_size].
+ * *_stride: bytes between consecutive experts (0 for a single matrix). */
+typedef struct {
+    const void* weight;
+    const void* scales;
+    const void* biases;
+    int64_t weight_stride;
+    int64_t sb_stride;
+} kq_mlx_matrix;
+
+/* Table lifetime.  The table owns its HBM; size = layers * experts * expert bytes. */
+int kq_table_create(const kq_table_desc* desc, kq_table** out);
+int kq_table_destroy(kq_table* t);
+int kq_table_desc_get(const kq_table* t, kq_table_desc* desc);
+size_t kq_table_bytes(const kq_table* t);
+/* bytes one expert occupies in HBM (equal to the MLX/BKEX expert size) */
+size_t kq_table_expert_bytes(const kq_table* t);
+
+/* Repack experts [expert_begin, expert_begin + num_experts) of `layer` from
+ * device MLX-layout arrays into the table (replaces the pread path of
+ * kandiga/metal/kandiga_cpu_expert.m:495-515: weights are made resident once). */
+int kq_table_load_mlx(kq_table* t, int layer, int expert_begin, int num_experts,
+                      const kq_mlx_matrix* gate, const kq_mlx_matrix* up,
+                      const kq_mlx_matrix* down, void* stream);
+
+/* Load one BKEX layer file image (header + payload) that the caller has in
+ * host memory.  The header must match the table's desc. */
+int kq_table_load_bkex(kq_table* t, int layer, const void* file_bytes, size_t nbytes, void* stream);
+
+/* Unpack one matrix (0 gate, 1 up, 2 down) of one expert back to MLX layout
+ * (device buffers sized as for kq_mlx_matrix).  Bit-exact inverse of the load. */
+int kq_table_unpack_mlx(const kq_table* t, int layer, int expert, int matrix, void* weight,
+                        void* scales, void* biases, void* stream);
+
+/* Scratch for kq_moe_*: query, allocate (device), zero once with kq_workspace_init. */
+size_t kq_moe_workspace_size(const kq_table* t, int max_tokens, int top_k);
+int kq_workspace_init(void* workspace, size_t bytes, void* stream);
+
+/* Router: softmax over E logits, top-K (strict '>', lowest index wins ties),
+ * renormalised weights.  replaces kandiga/metal/moe_block.metal:419-505.
+ * logits [T][E] fp32 -> idx [T][K] int32, weights [T][K] fp32. */
+int kq_router_topk(const float* logits, int T, int E, int K, int32_t* idx, float* weights,
+                   void* stream);
+
+/* Routed-expert MLP for T tokens (decode-shaped: every (token, k) pair runs
+ * its own expert).  replaces _CPUSwitchGLU.__call__ (kandiga/engine.py:670-739)
+ * and bakan_cpu_expert_mlp_f16/bf16 (kandiga/metal/kandiga_cpu_expert.m:662-719).
+ *   x          [T][H] in x_dtype (f16, bf16 or f32)
+ *   logits     [T][E] fp32 or NULL.  If given, routing runs first and idx /
+ *              weights are OUTPUTS; if NULL they are INPUTS.
+ *   idx        [T][K] int32;  weights [T][K] fp32 (may be NULL when out is NULL)
+ *   out_per_k  [T][K][H] out_dtype, unweighted per-expert outputs, or NULL
+ *   out        [T][H] out_dtype: residual + sum_k w_k y_k
+ *              (kandiga/metal/moe_block.metal:515-584), or NULL
+ *   residual   [T][H] out_dtype or NULL */
+int kq_moe_decode(const kq_table* t, int layer, const void* x, int x_dtype, int T,
+                  const float* logits, int32_t* idx, float* weights, int K, void* out_per_k,
+                  void* out, int out_dtype, const void* residual, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* Read and clear the device status word of a workspace (synchronises `stream`). */
+int kq_status_read(void* workspace, uint32_t* status, void* stream);
+
+/* ---- dense quantized GEMV (tq3 / shared-layer path) -------------------------- */
+
+/* Dense MLX-affine matrix [rows][cols].  With `pair` set, two matrices of the
+ * same shape (gate, up) are interleaved so one pass yields act(gate x) * (up x). */
+int kq_qmat_create(int rows, int cols, int bits, int sb_dtype, int pair, kq_qmat** out);
+int kq_qmat_destroy(kq_qmat* m);
+int kq_qmat_load_mlx(kq_qmat* m, const kq_mlx_matrix* a, const kq_mlx_matrix* b, void* stream);
+/* Unpack matrix `which` (0 = a / gate, 1 = b / up) back to MLX layout, bit-exact. */
+int kq_qmat_unpack_mlx(const kq_qmat* m, int which, void* weight, void* scales, void* biases,
+                       void* stream);
+
+/* y[t] = W x[t] (pair: y = act(Wg x) * (Wu x), activation KQ_ACT_*).
+ * Optional RMSNorm prologue: x <- x * rsqrt(mean(x^2) + eps) * norm_w
+ * (kandiga/metal/attention.metal:530-675), norm_w in x_dtype or NULL.
+ * replaces the MLX QuantizedLinear(bits=3) path loaded at kandiga/engine.py:928-989. */
+int kq_dense_gemv(const kq_qmat* m, const void* x, int x_dtype, int T, const void* norm_w,
+                  float eps, int activation, void* y, int y_dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KQ_H */

@@ -1,0 +1,100 @@
+"""ctypes binding of libkq.so (include/kq.h).
+
+The library is built in-tree by kandiga_b200/build.py.  There is no fallback:
+if the shared object is missing or does not load, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+from .build import LIB
+
+c_int, c_size_t, c_float, c_void_p = ctypes.c_int, ctypes.c_size_t, ctypes.c_float, ctypes.c_void_p
+c_i32p = ctypes.POINTER(ctypes.c_int32)
+c_u32p = ctypes.POINTER(ctypes.c_uint32)
+
+KQ_OK = 0
+ERRORS = {1: "KQ_ERR_ARG", 2: "KQ_ERR_CUDA", 3: "KQ_ERR_ALLOC", 4: "KQ_ERR_IO", 5: "KQ_ERR_FORMAT",
+          6: "KQ_ERR_UNSUPPORTED", 7: "KQ_ERR_WORKSPACE"}
+DT_F16, DT_BF16, DT_F32 = 0, 1, 2
+ACT_SILU, ACT_GELU_TANH = 0, 1
+DEV_BAD_EXPERT, DEV_WAIT_TIMEOUT, DEV_BAD_INDEX = 1, 2, 4
+
+
+class KQError(RuntimeError):
+    pass
+
+
+class kq_table_desc(ctypes.Structure):
+    _fields_ = [("num_layers", ctypes.c_int32), ("num_experts", ctypes.c_int32),
+                ("hidden", ctypes.c_int32), ("inter", ctypes.c_int32), ("bits", ctypes.c_int32),
+                ("group_size", ctypes.c_int32), ("sb_dtype", ctypes.c_int32),
+                ("activation", ctypes.c_int32)]
+
+
+class kq_mlx_matrix(ctypes.Structure):
+    _fields_ = [("weight", c_void_p), ("scales", c_void_p), ("biases", c_void_p),
+                ("weight_stride", ctypes.c_int64), ("sb_stride", ctypes.c_int64)]
+
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    # reference-compatible host ABI
+    "bakan_cpu_expert_init": (c_void_p, [ctypes.c_char_p, c_int]),
+    "bakan_cpu_expert_mlp": (c_int, [c_void_p, c_int, c_void_p, c_i32p, c_int, c_void_p]),
+    "bakan_cpu_expert_mlp_f16": (c_int, [c_void_p, c_int, c_void_p, c_i32p, c_int, c_void_p]),
+    "bakan_cpu_expert_mlp_bf16": (c_int, [c_void_p, c_int, c_void_p, c_i32p, c_int, c_void_p]),
+    "bakan_cpu_expert_mlp_batch_f16": (c_int, [c_void_p, c_int, c_void_p, c_i32p, c_int, c_int, c_void_p]),
+    "bakan_cpu_expert_mlp_prefill_f16": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_i32p,
+                                                 c_i32p, c_i32p, c_i32p, c_i32p, c_int, c_void_p]),
+    "bakan_cpu_expert_pread_batch": (c_int, [c_void_p, c_int, c_i32p, c_int, c_void_p]),
+    "bakan_cpu_expert_destroy": (None, [c_void_p]),
+    "bakan_cpu_expert_num_layers": (c_int, [c_void_p]),
+    # device ABI
+    "kq_table_create": (c_int, [ctypes.POINTER(kq_table_desc), ctypes.POINTER(c_void_p)]),
+    "kq_table_destroy": (c_int, [c_void_p]),
+    "kq_table_desc_get": (c_int, [c_void_p, ctypes.POINTER(kq_table_desc)]),
+    "kq_table_bytes": (c_size_t, [c_void_p]),
+    "kq_table_expert_bytes": (c_size_t, [c_void_p]),
+    "kq_table_load_mlx": (c_int, [c_void_p, c_int, c_int, c_int, ctypes.POINTER(kq_mlx_matrix),
+                                  ctypes.POINTER(kq_mlx_matrix), ctypes.POINTER(kq_mlx_matrix), c_void_p]),
+    "kq_table_load_bkex": (c_int, [c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "kq_table_unpack_mlx": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "kq_moe_workspace_size": (c_size_t, [c_void_p, c_int, c_int]),
+    "kq_workspace_init": (c_int, [c_void_p, c_size_t, c_void_p]),
+    "kq_router_topk": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "kq_moe_decode": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int,
+                              c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "kq_status_read": (c_int, [c_void_p, c_u32p, c_void_p]),
+    "kq_qmat_create": (c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_void_p)]),
+    "kq_qmat_destroy": (c_int, [c_void_p]),
+    "kq_qmat_load_mlx": (c_int, [c_void_p, ctypes.POINTER(kq_mlx_matrix), ctypes.POINTER(kq_mlx_matrix),
+                                 c_void_p]),
+    "kq_qmat_unpack_mlx": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "kq_dense_gemv": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_float, c_int, c_void_p, c_int,
+                              c_void_p]),
+}
+
+_lib = None
+
+
+def load(path: str = LIB):
+    """Load libkq.so; raises if it is missing (there is no CPU fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise KQError(f"libkq.so not found at {path}; build it with `python -m kandiga_b200.build`")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(rc: int, what: str):
+    if rc != KQ_OK:
+        raise KQError(f"{what} failed: {ERRORS.get(rc, rc)}")

@@ -1,0 +1,335 @@
+// kq_bakan.cu -- reference-compatible host ABI (bakan_cpu_expert_*).
+//
+// The reference's native library (kandiga/metal/kandiga_cpu_expert.m) preads K
+// experts from the BKEX layer files on every call and computes them on CPU
+// cores.  Here init reads every layer file once into the HBM table, and each
+// call is: host -> device copy of x and the expert ids, the sm_100a decode
+// kernels, device -> host copy of the per-expert outputs.  Calls are
+// synchronous and, like the reference, not re-entrant per engine.
+// Errors: -1 with a "[kandiga] ERROR: ..." line on stderr, as the reference.
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "kq_internal.h"
+
+using namespace kq;
+
+namespace {
+
+constexpr int kMaxExperts = 16;  // MAX_EXPERTS, kandiga/metal/kandiga_cpu_expert.m:37
+
+struct Engine {
+    kq_table* table = nullptr;
+    BkexInfo info{};
+    int num_layers = 0;
+    cudaStream_t stream = nullptr;
+    // device scratch, grown on demand (never on the single-token path after init)
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    int ws_tokens = 0;
+    void* dx = nullptr;
+    size_t dx_bytes = 0;
+    void* dout = nullptr;
+    size_t dout_bytes = 0;
+    int32_t* didx = nullptr;
+    size_t didx_bytes = 0;
+    std::vector<uint8_t> host_stage;
+};
+
+bool grow(void** p, size_t* have, size_t need) {
+    if (*have >= need) return true;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *have = 0;
+    if (cudaMalloc(p, need) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    *have = need;
+    return true;
+}
+
+bool ensure(Engine* e, int T, int K) {
+    const int H = e->info.hidden;
+    if (!grow(&e->dx, &e->dx_bytes, (size_t)T * H * 4)) return false;
+    if (!grow(&e->dout, &e->dout_bytes, (size_t)T * K * H * 4)) return false;
+    if (!grow(reinterpret_cast<void**>(&e->didx), &e->didx_bytes, (size_t)T * K * 4)) return false;
+    if (T > e->ws_tokens || e->ws_bytes < kq_moe_workspace_size(e->table, T, K)) {
+        size_t need = kq_moe_workspace_size(e->table, std::max(T, e->ws_tokens), kMaxExperts);
+        if (e->ws) cudaFree(e->ws);
+        e->ws = nullptr;
+        e->ws_bytes = 0;
+        if (cudaMalloc(&e->ws, need) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        e->ws_bytes = need;
+        e->ws_tokens = std::max(T, e->ws_tokens);
+        if (kq_workspace_init(e->ws, need, e->stream) != KQ_OK) return false;
+    }
+    return true;
+}
+
+int check_call(Engine* e, int layer, const int32_t* idx, int n, int K) {
+    if (!e) return -1;
+    if (layer < 0 || layer >= e->num_layers) {
+        fprintf(stderr, "[kandiga] ERROR: layer_idx %d out of range [0, %d)\n", layer, e->num_layers);
+        return -1;
+    }
+    if (K <= 0 || K > kMaxExperts) {
+        fprintf(stderr, "[kandiga] ERROR: num_experts %d out of range [1, %d]\n", K, kMaxExperts);
+        return -1;
+    }
+    for (int i = 0; i < n; ++i)
+        if (idx[i] < 0 || idx[i] >= e->info.num_experts) {
+            fprintf(stderr, "[kandiga] ERROR: expert index %d out of range [0, %d)\n", idx[i],
+                    e->info.num_experts);
+            return -1;
+        }
+    return 0;
+}
+
+// Run T tokens x K experts: x host [T][H] in x_dtype -> out host [T][K][H] in out_dtype.
+int run(Engine* e, int layer, const void* x, int x_dtype, const int32_t* idx, int T, int K,
+        void* out, int out_dtype) {
+    if (!ensure(e, T, K)) {
+        fprintf(stderr, "[kandiga] ERROR: device allocation failed\n");
+        return -1;
+    }
+    const int H = e->info.hidden;
+    const size_t xb = (size_t)T * H * (x_dtype == KQ_DT_F32 ? 4 : 2);
+    const size_t ob = (size_t)T * K * H * (out_dtype == KQ_DT_F32 ? 4 : 2);
+    cudaStream_t s = e->stream;
+    if (cudaMemcpyAsync(e->dx, x, xb, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(e->didx, idx, (size_t)T * K * 4, cudaMemcpyHostToDevice, s) != cudaSuccess) {
+        fprintf(stderr, "[kandiga] ERROR: host->device copy failed for layer %d\n", layer);
+        return -1;
+    }
+    int rc = kq_moe_decode(e->table, layer, e->dx, x_dtype, T, nullptr, e->didx, nullptr, K, e->dout,
+                           nullptr, out_dtype, nullptr, e->ws, e->ws_bytes, s);
+    if (rc != KQ_OK) {
+        fprintf(stderr, "[kandiga] ERROR: expert kernels failed for layer %d (code %d)\n", layer, rc);
+        return -1;
+    }
+    if (cudaMemcpyAsync(out, e->dout, ob, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess) {
+        fprintf(stderr, "[kandiga] ERROR: Expert computation failed for layer %d\n", layer);
+        return -1;
+    }
+    uint32_t st = 0;
+    if (kq_status_read(e->ws, &st, s) != KQ_OK || st != 0) {
+        fprintf(stderr, "[kandiga] ERROR: device status 0x%x for layer %d\n", st, layer);
+        return -1;
+    }
+    return 0;
+}
+
+}  // namespace
+
+extern "C" void bakan_cpu_expert_destroy(void* engine_ptr);
+
+extern "C" void* bakan_cpu_expert_init(const char* packed_dir, int num_layers) {
+    if (!packed_dir || num_layers <= 0) {
+        fprintf(stderr, "[kandiga] ERROR: bad arguments to init\n");
+        return nullptr;
+    }
+    Engine* e = new (std::nothrow) Engine();
+    if (!e) {
+        fprintf(stderr, "[kandiga] ERROR: Failed to allocate engine\n");
+        return nullptr;
+    }
+    e->num_layers = num_layers;
+    if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        fprintf(stderr, "[kandiga] ERROR: no CUDA device\n");
+        delete e;
+        return nullptr;
+    }
+    std::vector<uint8_t> file;
+    for (int l = 0; l < num_layers; ++l) {
+        char path[1024];
+        snprintf(path, sizeof(path), "%s/layer_%02d.bin", packed_dir, l);
+        FILE* f = fopen(path, "rb");
+        if (!f) {
+            fprintf(stderr, "[kandiga] ERROR: Cannot open %s\n", path);
+            bakan_cpu_expert_destroy(e);
+            return nullptr;
+        }
+        fseek(f, 0, SEEK_END);
+        const long n = ftell(f);
+        fseek(f, 0, SEEK_SET);
+        file.resize(n > 0 ? (size_t)n : 0);
+        const size_t got = n > 0 ? fread(file.data(), 1, (size_t)n, f) : 0;
+        fclose(f);
+        if (n <= 0 || got != (size_t)n) {
+            fprintf(stderr, "[kandiga] ERROR: read failed for %s\n", path);
+            bakan_cpu_expert_destroy(e);
+            return nullptr;
+        }
+        if (l == 0) {
+            if (bkex_parse(file.data(), file.size(), &e->info) != KQ_OK) {
+                fprintf(stderr, "[kandiga] ERROR: %s is not a BKEX layer file\n", path);
+                bakan_cpu_expert_destroy(e);
+                return nullptr;
+            }
+            kq_table_desc d{};
+            d.num_layers = num_layers;
+            d.num_experts = e->info.num_experts;
+            d.hidden = e->info.hidden;
+            d.inter = e->info.inter;
+            d.bits = e->info.bits;
+            d.group_size = 64;
+            d.sb_dtype = e->info.sb_dtype;
+            d.activation = e->info.activation;
+            if (kq_table_create(&d, &e->table) != KQ_OK) {
+                fprintf(stderr, "[kandiga] ERROR: cannot create the HBM expert table\n");
+                bakan_cpu_expert_destroy(e);
+                return nullptr;
+            }
+        }
+        if (kq_table_load_bkex(e->table, l, file.data(), file.size(), e->stream) != KQ_OK) {
+            fprintf(stderr, "[kandiga] ERROR: cannot load %s\n", path);
+            bakan_cpu_expert_destroy(e);
+            return nullptr;
+        }
+    }
+    if (!ensure(e, 1, kMaxExperts)) {
+        fprintf(stderr, "[kandiga] ERROR: device allocation failed\n");
+        bakan_cpu_expert_destroy(e);
+        return nullptr;
+    }
+    fprintf(stderr, "[kandiga] Initialized: %d layers, %d experts (%zu KB each), %d-bit, HBM-resident\n",
+            num_layers, e->info.num_experts, (size_t)e->info.expert_size / 1024, e->info.bits);
+    return e;
+}
+
+extern "C" int bakan_cpu_expert_mlp(void* engine, int layer_idx, const float* x_f32,
+                                    const int32_t* expert_indices, int num_experts, float* output_f32) {
+    Engine* e = static_cast<Engine*>(engine);
+    if (check_call(e, layer_idx, expert_indices, num_experts, num_experts)) return -1;
+    return run(e, layer_idx, x_f32, KQ_DT_F32, expert_indices, 1, num_experts, output_f32, KQ_DT_F32);
+}
+
+extern "C" int bakan_cpu_expert_mlp_f16(void* engine, int layer_idx, const void* x_f16,
+                                        const int32_t* expert_indices, int num_experts,
+                                        void* output_f16) {
+    Engine* e = static_cast<Engine*>(engine);
+    if (check_call(e, layer_idx, expert_indices, num_experts, num_experts)) return -1;
+    return run(e, layer_idx, x_f16, KQ_DT_F16, expert_indices, 1, num_experts, output_f16, KQ_DT_F16);
+}
+
+extern "C" int bakan_cpu_expert_mlp_bf16(void* engine, int layer_idx, const void* x_bf16,
+                                         const int32_t* expert_indices, int num_experts,
+                                         void* output_f16) {
+    Engine* e = static_cast<Engine*>(engine);
+    if (check_call(e, layer_idx, expert_indices, num_experts, num_experts)) return -1;
+    return run(e, layer_idx, x_bf16, KQ_DT_BF16, expert_indices, 1, num_experts, output_f16, KQ_DT_F16);
+}
+
+extern "C" int bakan_cpu_expert_mlp_batch_f16(void* engine, int layer_idx, const void* x_f16_batch,
+                                              const int32_t* indices_batch, int num_tokens, int K,
+                                              void* output_f16_batch) {
+    Engine* e = static_cast<Engine*>(engine);
+    if (!e || num_tokens <= 0) return -1;
+    if (check_call(e, layer_idx, indices_batch, num_tokens * K, K)) return -1;
+    return run(e, layer_idx, x_f16_batch, KQ_DT_F16, indices_batch, num_tokens, K, output_f16_batch,
+               KQ_DT_F16);
+}
+
+extern "C" int bakan_cpu_expert_mlp_prefill_f16(void* engine, int layer_idx, const void* x_f16,
+                                                int num_tokens, int K, int hidden_size,
+                                                const int32_t* sorted_token_indices,
+                                                const int32_t* sorted_expert_indices,
+                                                const int32_t* sorted_k_positions,
+                                                const int32_t* group_starts,
+                                                const int32_t* unique_experts,
+                                                int num_unique_experts, void* output_f16) {
+    Engine* e = static_cast<Engine*>(engine);
+    if (!e || layer_idx < 0 || layer_idx >= e->num_layers) return -1;
+    if (num_tokens <= 0 || K <= 0 || K > kMaxExperts || hidden_size != e->info.hidden) return -1;
+    if (num_unique_experts < 0) return -1;
+    if (num_unique_experts == 0) return 0;
+    const int total = group_starts[num_unique_experts];
+    if (group_starts[0] < 0 || total < group_starts[0]) return -1;
+    // Rebuild the [T][K] id table from the CSR groups; pairs no group covers
+    // keep their output untouched, as in the reference.
+    std::vector<int32_t> idx((size_t)num_tokens * K, 0);
+    std::vector<uint8_t> covered((size_t)num_tokens * K, 0);
+    for (int g = 0; g < num_unique_experts; ++g) {
+        const int eid = unique_experts[g];
+        if (eid < 0 || eid >= e->info.num_experts) {
+            fprintf(stderr, "[kandiga] ERROR: expert index %d out of range\n", eid);
+            return -1;
+        }
+        for (int i = group_starts[g]; i < group_starts[g + 1]; ++i) {
+            const int t = sorted_token_indices[i], k = sorted_k_positions[i];
+            if (t < 0 || t >= num_tokens || k < 0 || k >= K) return -1;
+            idx[(size_t)t * K + k] = eid;
+            covered[(size_t)t * K + k] = 1;
+        }
+    }
+    (void)sorted_expert_indices;
+    const size_t row = (size_t)hidden_size * 2;
+    e->host_stage.resize((size_t)num_tokens * K * row);
+    if (run(e, layer_idx, x_f16, KQ_DT_F16, idx.data(), num_tokens, K, e->host_stage.data(), KQ_DT_F16))
+        return -1;
+    uint8_t* out = static_cast<uint8_t*>(output_f16);
+    for (size_t i = 0; i < covered.size(); ++i)
+        if (covered[i]) memcpy(out + i * row, e->host_stage.data() + i * row, row);
+    return 0;
+}
+
+extern "C" int bakan_cpu_expert_pread_batch(void* engine, int layer_idx, const int32_t* expert_ids,
+                                            int num_experts_to_read, void* output_buffer) {
+    Engine* e = static_cast<Engine*>(engine);
+    if (!e || layer_idx < 0 || layer_idx >= e->num_layers || num_experts_to_read < 0) return -1;
+    if (num_experts_to_read == 0) return 0;
+    if (!expert_ids || !output_buffer) return -1;
+    const BkexInfo& I = e->info;
+    const size_t esz = I.expert_size;
+    void* dbuf = nullptr;
+    if (cudaMalloc(&dbuf, esz) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    uint8_t* d = static_cast<uint8_t*>(dbuf);
+    int rc = 0;
+    for (int i = 0; i < num_experts_to_read && rc == 0; ++i) {
+        const int eid = expert_ids[i];
+        if (eid < 0 || eid >= I.num_experts) {
+            rc = -1;
+            break;
+        }
+        for (int m = 0; m < 3 && rc == 0; ++m)
+            if (kq_table_unpack_mlx(e->table, layer_idx, eid, m, d + I.off[3 * m], d + I.off[3 * m + 1],
+                                    d + I.off[3 * m + 2], e->stream) != KQ_OK)
+                rc = -1;
+        if (rc == 0 &&
+            (cudaMemcpyAsync(static_cast<uint8_t*>(output_buffer) + (size_t)i * esz, d, esz,
+                             cudaMemcpyDeviceToHost, e->stream) != cudaSuccess ||
+             cudaStreamSynchronize(e->stream) != cudaSuccess))
+            rc = -1;
+    }
+    cudaFree(dbuf);
+    return rc;
+}
+
+extern "C" void bakan_cpu_expert_destroy(void* engine_ptr) {
+    Engine* e = static_cast<Engine*>(engine_ptr);
+    if (!e) return;
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    kq_table_destroy(e->table);
+    if (e->ws) cudaFree(e->ws);
+    if (e->dx) cudaFree(e->dx);
+    if (e->dout) cudaFree(e->dout);
+    if (e->didx) cudaFree(e->didx);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+    fprintf(stderr, "[kandiga] Engine destroyed\n");
+}
+
+extern "C" int bakan_cpu_expert_num_layers(void* engine_ptr) {
+    Engine* e = static_cast<Engine*>(engine_ptr);
+    return e ? e->num_layers : 0;
+}

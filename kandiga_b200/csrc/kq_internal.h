@@ -1,0 +1,47 @@
+// kq_internal.h -- host-side structures shared by the libkq translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <new>
+
+#include "../../include/kq.h"
+#include "kq_qtile.cuh"
+
+struct kq_table {
+    kq_table_desc d;
+    uint8_t* base = nullptr;
+    size_t bytes = 0;
+    int tb = 0;                 // tile bytes
+    int nst_h = 0, nst_i = 0;   // column tiles along H / I
+    int i8 = 0, h16 = 0;        // gate/up row-tiles (8 intermediate rows), down row-tiles
+    size_t gateup_bytes = 0, down_bytes = 0, expert_bytes = 0, layer_bytes = 0;
+};
+
+struct kq_qmat {
+    int rows = 0, cols = 0, bits = 0, sb_dtype = 0, pair = 0;
+    int nrt = 0, nst = 0, tb = 0;
+    uint8_t* base = nullptr;
+    size_t bytes = 0;
+};
+
+namespace kq {
+
+struct BkexInfo {
+    int num_experts, hidden, inter, bits, sb_dtype, activation;
+    uint64_t expert_size;
+    uint32_t off[9], nbytes[9], d0[9], d1[9];
+    uint8_t dtype[9];
+};
+int bkex_parse(const uint8_t* hdr, size_t n, BkexInfo* info);
+
+// Workspace carve-up for kq_moe_* (offsets in bytes, 256-aligned).
+struct MoeWs {
+    size_t status, idx, w, act, y, cnt, total;
+};
+MoeWs moe_ws_layout(const kq_table* t, int T, int K);
+
+}  // namespace kq

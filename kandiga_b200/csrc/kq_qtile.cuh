@@ -1,0 +1,267 @@
+// kq_qtile.cuh -- the HBM tile layout of quantized matrices and the
+// dequant-GEMV engine that consumes it.
+//
+// TILE LAYOUT ("KQ tile").  A quantized matrix [rows][cols] (MLX affine,
+// group 64, 3 or 4 bits) is cut into tiles of 16 rows x 512 columns
+// (8 groups).  A tile is 32 lanes' worth of 16-byte chunks, chunk-major:
+//     byte offset of lane l's chunk c  =  c * 512 + l * 16
+// so a warp reading chunk c reads 512 contiguous bytes (coalesced, and bank-
+// conflict-free from shared memory).  Lane l = 4*r + t (r = l/4, t = l%4)
+// owns four (row, group) "sets":
+//     set 0 = (row r,   group t)     set 1 = (row r,   group t+4)
+//     set 2 = (row r+8, group t)     set 3 = (row r+8, group t+4)
+// W = 6 (3-bit) or 8 (4-bit) 32-bit words per set; lane word q = set*W + w
+// lives in chunk q/4, position q%4.  After the 4*W/4 = W code chunks comes one
+// scale/bias chunk: lane l holds (scale | bias<<16) for
+//     (row r, group 2t), (row r, group 2t+1), (row r+8, group 2t), (row r+8, group 2t+1).
+// Tile bytes: 3584 (3-bit) or 4608 (4-bit) -- exactly 16*512*(bits/8 + 4/64),
+// the same bytes per weight as the MLX layout.
+//
+// Within a set, code i (0..63 of the group) is half (i%2) of pair j = i/2.
+// 3-bit: pair j < 30 sits in word j/5, slot s = j%5: low code at bit 3s, high
+//        code at bit 16+3s; pairs 30 and 31 are spread over bit 15 (low) and
+//        bit 31 (high) of words 0-2 and 3-5 (bit b of the code in word b).
+// 4-bit: pair j sits in word j/4, slot s = j%4: low at bit 4s, high at 16+4s.
+// One LOP3 per pair ((word >> shift) & mask | magic) yields two fp16 values
+// 2^(10-k) + q exactly (k = field offset inside the 16-bit half), i.e. an
+// fp16x2 A-fragment register of the m16n8k16 MMA.  The constant 2^(10-k) per
+// pair is removed once per group through C[g] = sum_pairs 2^(10-k) (x_a + x_b).
+//
+// MMA MAPPING.  MMA j (0..31) of a tile takes pair j of every set:
+//     a0 = set 0, a1 = set 2, a2 = set 1, a3 = set 3,
+// i.e. A[m][k] with k in {2t,2t+1} -> group t and k in {2t+8,2t+9} -> group t+4.
+// B[k][n] = x (pair j of group n) where group(k) == n, 0 elsewhere, so column n
+// of D accumulates the dot product of group n alone: after 32 MMAs
+//     D[m][n] = sum_{i in group n} (2^(10-k_i) + q_{m,i}) x_i
+// and the per-group affine terms are applied once:
+//     y_m += s_{m,n} (D[m][n] - C[n]) + b_{m,n} X[n],   X[n] = sum_{i in n} x_i.
+// Each lane ends with partial sums over its groups 2t, 2t+1 for rows r, r+8;
+// two xor-shuffles finish the row dot products.
+#pragma once
+
+#include "kq_common.cuh"
+
+namespace kq {
+
+constexpr int TILE_ROWS = 16;
+constexpr int TILE_COLS = 512;
+constexpr int TILE_GROUPS = 8;
+constexpr int GS = 64;
+
+template <int BITS>
+struct TileT {
+    static constexpr int W = (BITS == 3) ? 6 : 8;  // words per (row, group) set
+    static constexpr int CODE_CHUNKS = W;          // 4 sets * W words / 4 words per chunk
+    static constexpr int CHUNKS = W + 1;
+    static constexpr int BYTES = CHUNKS * 512;
+};
+
+__host__ __device__ constexpr int tile_bytes(int bits) { return bits == 3 ? 3584 : 4608; }
+
+// offset constant 2^(10-k) of pair j (fp32)
+template <int BITS>
+__host__ __device__ __forceinline__ float pair_offset(int j) {
+    if (BITS == 3) {
+        if (j >= 30) return 1024.f;
+        int s = j % 5;
+        return s == 0 || s == 3 ? 1024.f : (s == 1 || s == 4 ? 128.f : 16.f);
+    } else {
+        return (j & 1) ? 64.f : 1024.f;
+    }
+}
+
+// fp16 exponent pattern with value 2^(10-k) in both halves
+__device__ __forceinline__ constexpr uint32_t magic2(int k) {
+    return ((uint32_t)(25 - k) << 10) * 0x00010001u;
+}
+
+// Extract pair j of one set (words wd[0..W-1]; sh[] = words >> 9 (3-bit) or >> 8 (4-bit))
+template <int BITS, int J>
+__device__ __forceinline__ uint32_t pair_of(const uint32_t* wd, const uint32_t* sh) {
+    if constexpr (BITS == 3) {
+        if constexpr (J < 30) {
+            constexpr int w = J / 5, s = J % 5;
+            constexpr int k = (s < 3) ? 3 * s : 3 * (s - 3);
+            constexpr uint32_t mask = (7u << k) | (7u << (16 + k));
+            const uint32_t src = (s < 3) ? wd[w] : sh[w];
+            return (src & mask) | magic2(k);
+        } else {
+            constexpr int b = (J - 30) * 3;
+            uint32_t v = ((wd[b] >> 15) & 0x00010001u) | magic2(0);
+            v |= (wd[b + 1] >> 14) & 0x00020002u;
+            v |= (wd[b + 2] >> 13) & 0x00040004u;
+            return v;
+        }
+    } else {
+        constexpr int w = J / 4, s = J % 4;
+        constexpr int k = (s & 1) * 4;
+        constexpr uint32_t mask = (15u << k) | (15u << (16 + k));
+        const uint32_t src = (s < 2) ? wd[w] : sh[w];
+        return (src & mask) | magic2(k);
+    }
+}
+
+// Stage a vector of n real values (read through `load(i)`, i < n) into a
+// warp's buffers, zero-padded to npad (multiple of 512).  Picks a power-of-two
+// scale so that max|x| lands in [2^14, 2^15): values cannot overflow fp16 and
+// small activations keep full fp16 precision.  Whole warp calls it.
+template <int BITS, typename Load>
+__device__ __forceinline__ float stage_vector(Load load, int n, int npad, __half* xs, float2* cx) {
+    const int lane = threadIdx.x & 31;
+    float amax = 0.f;
+    for (int i = lane; i < n; i += 32) amax = fmaxf(amax, fabsf(load(i)));
+    amax = warp_max(amax);
+    int e = 0;
+    float scale = 1.f;
+    if (amax > 0.f && amax < 3.0e38f) {
+        frexpf(amax, &e);
+        scale = ldexpf(1.f, 15 - e);
+    }
+    for (int i = lane; i < npad; i += 32) {
+        float v = i < n ? load(i) * scale : 0.f;
+        xs[i] = __float2half_rn(v);
+    }
+    __syncwarp();
+    const int ng = npad / GS;
+    for (int g = lane; g < ng; g += 32) {
+        const __half2* p = reinterpret_cast<const __half2*>(xs + g * GS);
+        float c = 0.f, xsum = 0.f;
+#pragma unroll 8
+        for (int j = 0; j < 32; ++j) {
+            float2 f = __half22float2(p[j]);
+            float pr = f.x + f.y;
+            c += pair_offset<BITS>(j) * pr;
+            xsum += pr;
+        }
+        cx[g] = make_float2(c, xsum);
+    }
+    __syncwarp();
+    return 1.f / scale;
+}
+
+// MMA steps J..31 of a tile (compile-time recursion: every pair extraction
+// uses constant masks and shifts).  x pairs J..J+3 arrive in one 16-byte load.
+template <int BITS, int J>
+__device__ __forceinline__ void mma_steps(float (&d)[4], const uint32_t (&wd)[4][TileT<BITS>::W],
+                                          const uint32_t (&sh)[4][TileT<BITS>::W],
+                                          const uint4* xp, bool has_x, bool use_b0, bool use_b1) {
+    if constexpr (J < 32) {
+        const uint4 xv = has_x ? xp[J / 4] : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            // u is a compile-time constant after unrolling; pair index J + u
+            const uint32_t b0 = use_b0 ? xw[u] : 0u;
+            const uint32_t b1 = use_b1 ? xw[u] : 0u;
+            uint32_t a0, a1, a2, a3;
+            if (u == 0) {
+                a0 = pair_of<BITS, J + 0>(wd[0], sh[0]); a1 = pair_of<BITS, J + 0>(wd[2], sh[2]);
+                a2 = pair_of<BITS, J + 0>(wd[1], sh[1]); a3 = pair_of<BITS, J + 0>(wd[3], sh[3]);
+            } else if (u == 1) {
+                a0 = pair_of<BITS, J + 1>(wd[0], sh[0]); a1 = pair_of<BITS, J + 1>(wd[2], sh[2]);
+                a2 = pair_of<BITS, J + 1>(wd[1], sh[1]); a3 = pair_of<BITS, J + 1>(wd[3], sh[3]);
+            } else if (u == 2) {
+                a0 = pair_of<BITS, J + 2>(wd[0], sh[0]); a1 = pair_of<BITS, J + 2>(wd[2], sh[2]);
+                a2 = pair_of<BITS, J + 2>(wd[1], sh[1]); a3 = pair_of<BITS, J + 2>(wd[3], sh[3]);
+            } else {
+                a0 = pair_of<BITS, J + 3>(wd[0], sh[0]); a1 = pair_of<BITS, J + 3>(wd[2], sh[2]);
+                a2 = pair_of<BITS, J + 3>(wd[1], sh[1]); a3 = pair_of<BITS, J + 3>(wd[3], sh[3]);
+            }
+            mma_f16(d, a0, a1, a2, a3, b0, b1);
+        }
+        mma_steps<BITS, J + 4>(d, wd, sh, xp, has_x, use_b0, use_b1);
+    }
+}
+
+// Registers of one tile for this lane: its 4 sets of code words + scale/bias chunk.
+template <int BITS>
+struct TileRegs {
+    uint32_t wd[4][TileT<BITS>::W];
+    uint4 sb;
+};
+
+// Load this lane's part of a tile (16 rows x 512 cols) from shared memory.
+template <int BITS>
+__device__ __forceinline__ void tile_load(const uint8_t* tile, TileRegs<BITS>& R) {
+    constexpr int W = TileT<BITS>::W;
+    const int lane = threadIdx.x & 31;
+    const uint4* ch = reinterpret_cast<const uint4*>(tile) + lane;  // chunk c at ch[c * 32]
+#pragma unroll
+    for (int c = 0; c < W; ++c) {
+        const uint4 v = ch[c * 32];
+        const int q0 = c * 4;
+        R.wd[(q0 + 0) / W][(q0 + 0) % W] = v.x;
+        R.wd[(q0 + 1) / W][(q0 + 1) % W] = v.y;
+        R.wd[(q0 + 2) / W][(q0 + 2) % W] = v.z;
+        R.wd[(q0 + 3) / W][(q0 + 3) % W] = v.w;
+    }
+    R.sb = ch[W * 32];
+}
+
+// 32 MMAs + per-group epilogue of one tile; st = column-tile index of the tile.
+// Accumulates into y0 (row r) and y1 (row r+8) of this lane's partial sums.
+template <int BITS, int SB_DT>
+__device__ __forceinline__ void tile_compute(const TileRegs<BITS>& R, int st, const __half* xs,
+                                             const float2* cxv, float& y0, float& y1) {
+    constexpr int W = TileT<BITS>::W;
+    const int lane = threadIdx.x & 31;
+    const int n = lane >> 2, t = lane & 3;
+    uint32_t sh[4][W];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int w = 0; w < W; ++w) sh[q][w] = R.wd[q][w] >> (BITS == 3 ? 9 : 8);
+
+    // B operand: lane (n, t) feeds b0 for group t when n == t, b1 for group t+4 when n == t+4.
+    const bool use_b0 = (n == t), use_b1 = (n == t + 4);
+    const int xg = use_b0 ? t : (use_b1 ? t + 4 : 0);
+    const uint4* xp = reinterpret_cast<const uint4*>(xs + st * TILE_COLS + xg * GS);
+
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_steps<BITS, 0>(d, R.wd, sh, xp, use_b0 || use_b1, use_b0, use_b1);
+
+    // epilogue: groups G0 = 2t, G1 = 2t+1 of this column tile
+    const float4 cx = *reinterpret_cast<const float4*>(cxv + st * TILE_GROUPS + 2 * t);
+    const uint4 sb = R.sb;
+    y0 += sb_lo<SB_DT>(sb.x) * (d[0] - cx.x) + sb_hi<SB_DT>(sb.x) * cx.y;
+    y0 += sb_lo<SB_DT>(sb.y) * (d[1] - cx.z) + sb_hi<SB_DT>(sb.y) * cx.w;
+    y1 += sb_lo<SB_DT>(sb.z) * (d[2] - cx.x) + sb_hi<SB_DT>(sb.z) * cx.y;
+    y1 += sb_lo<SB_DT>(sb.w) * (d[3] - cx.z) + sb_hi<SB_DT>(sb.w) * cx.w;
+}
+
+// finish the row dot products across the 4 lanes of a quad
+__device__ __forceinline__ void quad_reduce(float& y0, float& y1) {
+    y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+    y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
+    y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+    y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
+}
+
+__device__ __forceinline__ float activate(float g, float u, int act) {
+    if (act == KQ_ACT_GELU_TANH) {
+        float tt = 0.7978845608f * (g + 0.044715f * g * g * g);
+        return 0.5f * g * (1.f + tanhf(tt)) * u;
+    }
+    return (g / (1.f + expf(-g))) * u;
+}
+
+// ---- layout index helpers shared by the repack / unpack kernels ----------------
+// Location of code (tile-local row m in 0..15, column i in 0..511) inside a tile.
+struct CodeLoc {
+    int lane, set, pair, hi;
+};
+__host__ __device__ __forceinline__ CodeLoc code_loc(int m, int i) {
+    const int g8 = i / GS, ci = i % GS;
+    CodeLoc L;
+    L.lane = (m & 7) * 4 + (g8 & 3);
+    L.set = (m >> 3) * 2 + (g8 >> 2);
+    L.pair = ci >> 1;
+    L.hi = ci & 1;
+    return L;
+}
+
+__host__ __device__ __forceinline__ uint32_t tile_word_offset(int lane, int q) {
+    return (uint32_t)((q >> 2) * 512 + lane * 16 + (q & 3) * 4);
+}
+
+}  // namespace kq
