@@ -40,7 +40,7 @@ int bkex_parse(const uint8_t* hdr, size_t n, BkexInfo* info);
 
 // Workspace carve-up for kq_moe_* (offsets in bytes, 256-aligned).
 struct MoeWs {
-    size_t status, idx, w, act, y, cnt, total;
+    size_t status, idx, w, act, y, amax, cnt, total;
 };
 MoeWs moe_ws_layout(const kq_table* t, int T, int K);
 

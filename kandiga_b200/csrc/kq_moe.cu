@@ -46,9 +46,12 @@ struct GemvParams {
     const int32_t* idx;   // [T*K]
     const float* w;       // [T*K]
     float* act;           // [T*K][I]
+    float* amax;          // [T*K][I/8] per gate/up tile max |act| (scales the down input)
+    int nrt_up;           // gate/up row-tiles per vector (I/8)
     int I;
     float* y;             // [T*K][H] fp32 (combine input) or null
-    uint32_t* cnt;        // [T][nrt]
+    uint32_t* cnt;        // [T][nrt of the down matrix]
+    int cnt_per_token;    // counters per token (down row-tiles)
     void* out_per_k;      // [T*K][H] (out_dtype) or null
     void* out;            // [T][rows]
     int out_dtype;
@@ -114,6 +117,14 @@ __global__ void __launch_bounds__(WARPS * 32) qgemv_kernel(const GemvParams p) {
     if (lane == 0)
         for (int f = 0; f < NBUF && f < ntiles; ++f) issue(f);
     if (p.prefetch_before_wait) pdl_wait();
+    if (mode == MODE_GATEUP && blockIdx.x == 0 && p.cnt) {
+        // The down kernel's arrival counters for this call: zeroed here, before
+        // the down kernel (which waits for this grid) can reach its combine.
+        // Their offset in the workspace depends on T and K, so a previous call
+        // with other shapes may have left other data there.
+        const int ncnt = p.T * p.cnt_per_token;
+        for (int i = threadIdx.x; i < ncnt; i += blockDim.x) p.cnt[i] = 0u;
+    }
     pdl_launch_dependents();
 
     int staged = -1;
@@ -124,33 +135,34 @@ __global__ void __launch_bounds__(WARPS * 32) qgemv_kernel(const GemvParams p) {
         if (st == 0) {
             const int vec = (mode == MODE_DOWN) ? tk : tk / p.K;
             if (vec != staged) {
+                float scale = 1.f;
                 if (mode == MODE_DOWN) {
-                    const float* a = p.act + (size_t)vec * p.I;
-                    inv = stage_vector<BITS>([&](int i) { return __ldcg(a + i); }, p.ncols, npad, xs, cx);
+                    // max |act| of this (token, k) from the gate/up epilogue's per-tile maxima
+                    const float* pm = p.amax + (size_t)vec * p.nrt_up;
+                    float a = 0.f;
+                    for (int i = lane; i < p.nrt_up; i += 32) a = fmaxf(a, __ldcg(pm + i));
+                    scale = pow2_scale(warp_max(a));
+                    stage_vector<BITS>(p.act, KQ_DT_F32, (size_t)vec * p.I, p.ncols, npad, nullptr, scale,
+                                       true, xs, cx);
                 } else {
-                    const size_t base = (size_t)vec * p.ncols;
-                    float rinv = 1.f;
+                    const size_t off = (size_t)vec * p.ncols;
                     if (p.norm_w) {
-                        float ss = 0.f;
-                        for (int i = lane; i < p.ncols; i += 32) {
-                            const float v = load_as_float(p.x, p.x_dtype, base + i);
-                            ss += v * v;
+                        float amax, ss;
+                        vec_stats(p.x, p.x_dtype, off, p.ncols, p.norm_w, false, amax, ss);
+                        const float rinv = rsqrtf(ss / (float)p.ncols + p.eps);
+                        scale = pow2_scale(amax * rinv);
+                        stage_vector<BITS>(p.x, p.x_dtype, off, p.ncols, npad, p.norm_w, rinv * scale, false,
+                                           xs, cx);
+                    } else {
+                        if (p.x_dtype != KQ_DT_F16) {  // fp16 inputs are staged exactly, unscaled
+                            float amax, ss;
+                            vec_stats(p.x, p.x_dtype, off, p.ncols, nullptr, false, amax, ss);
+                            scale = pow2_scale(amax);
                         }
-                        ss = warp_sum(ss);
-                        rinv = rsqrtf(ss / (float)p.ncols + p.eps);
+                        stage_vector<BITS>(p.x, p.x_dtype, off, p.ncols, npad, nullptr, scale, false, xs, cx);
                     }
-                    if (p.norm_w)
-                        inv = stage_vector<BITS>(
-                            [&](int i) {
-                                return load_as_float(p.x, p.x_dtype, base + i) * rinv *
-                                       load_as_float(p.norm_w, p.x_dtype, (size_t)i);
-                            },
-                            p.ncols, npad, xs, cx);
-                    else
-                        inv = stage_vector<BITS>(
-                            [&](int i) { return load_as_float(p.x, p.x_dtype, base + i); }, p.ncols,
-                            npad, xs, cx);
                 }
+                inv = 1.f / scale;
                 staged = vec;
             }
             y0 = y1 = 0.f;
@@ -178,13 +190,17 @@ __global__ void __launch_bounds__(WARPS * 32) qgemv_kernel(const GemvParams p) {
         }
         const float g = valid ? y0 * inv : 0.f, h = valid ? y1 * inv : 0.f;
         if (mode == MODE_GATEUP || mode == MODE_DENSE_PAIR) {
+            const float a = valid ? activate(g, h, p.act_kind) : 0.f;
             if ((lane & 3) == 0) {
-                const float a = valid ? activate(g, h, p.act_kind) : 0.f;
                 const int row = rt * 8 + r;
                 if (mode == MODE_GATEUP)
                     p.act[(size_t)tk * p.I + row] = a;
                 else
                     store_from_float(p.out, p.out_dtype, (size_t)tk * p.H + row, a);
+            }
+            if (mode == MODE_GATEUP) {
+                const float m = warp_max(fabsf(a));
+                if (lane == 0) p.amax[(size_t)tk * p.nrt + rt] = m;
             }
             continue;
         }
@@ -359,6 +375,8 @@ MoeWs moe_ws_layout(const kq_table* t, int T, int K) {
     o = align_up(o + (size_t)T * K * t->d.inter * 4, 256);
     L.y = o;
     o = align_up(o + (size_t)T * K * t->d.hidden * 4, 256);
+    L.amax = o;
+    o = align_up(o + (size_t)T * K * t->i8 * 4, 256);
     L.cnt = o;
     o = align_up(o + (size_t)T * t->h16 * 4, 256);
     L.total = o;
@@ -437,9 +455,12 @@ extern "C" int kq_moe_decode(const kq_table* t, int layer, const void* x, int x_
     p.idx = idx_use;
     p.w = w_use;
     p.act = reinterpret_cast<float*>(ws + L.act);
+    p.amax = reinterpret_cast<float*>(ws + L.amax);
+    p.nrt_up = t->i8;
     p.I = t->d.inter;
     p.y = reinterpret_cast<float*>(ws + L.y);
     p.cnt = reinterpret_cast<uint32_t*>(ws + L.cnt);
+    p.cnt_per_token = t->h16;
     p.status = reinterpret_cast<uint32_t*>(ws + L.status);
     p.act_kind = t->d.activation;
     p.x = x;

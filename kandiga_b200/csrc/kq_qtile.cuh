@@ -101,42 +101,133 @@ __device__ __forceinline__ uint32_t pair_of(const uint32_t* wd, const uint32_t* 
     }
 }
 
-// Stage a vector of n real values (read through `load(i)`, i < n) into a
-// warp's buffers, zero-padded to npad (multiple of 512).  Picks a power-of-two
-// scale so that max|x| lands in [2^14, 2^15): values cannot overflow fp16 and
-// small activations keep full fp16 precision.  Whole warp calls it.
-template <int BITS, typename Load>
-__device__ __forceinline__ float stage_vector(Load load, int n, int npad, __half* xs, float2* cx) {
-    const int lane = threadIdx.x & 31;
-    float amax = 0.f;
-    for (int i = lane; i < n; i += 32) amax = fmaxf(amax, fabsf(load(i)));
-    amax = warp_max(amax);
-    int e = 0;
-    float scale = 1.f;
-    if (amax > 0.f && amax < 3.0e38f) {
-        frexpf(amax, &e);
-        scale = ldexpf(1.f, 15 - e);
+// ---- input staging ---------------------------------------------------------------
+// The engine consumes the input vector as fp16 x * 2^sigma in a per-warp shared
+// buffer xs[npad] (zero-padded to a multiple of 512) plus per-group constants
+// cx[g] = {C[g], X[g]}.  Loads are issued 8 elements (one 16/32-byte vector)
+// per lane per chunk, BATCH chunks at a time, so a warp has all of them in
+// flight instead of paying one memory latency per element.
+
+// 8 consecutive elements starting at element i (i % 8 == 0) as floats.
+__device__ __forceinline__ void load8(const void* p, int dtype, size_t i, bool cg, float (&v)[8]) {
+    if (dtype == KQ_DT_F32) {
+        const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+        const float4 a = cg ? __ldcg(q) : __ldg(q);
+        const float4 b = cg ? __ldcg(q + 1) : __ldg(q + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        return;
     }
-    for (int i = lane; i < npad; i += 32) {
-        float v = i < n ? load(i) * scale : 0.f;
-        xs[i] = __float2half_rn(v);
+    const uint4* q = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p) + i);
+    const uint4 a = cg ? __ldcg(q) : __ldg(q);
+    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        if (dtype == KQ_DT_F16) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+            v[2 * k] = f.x;
+            v[2 * k + 1] = f.y;
+        } else {
+            v[2 * k] = __uint_as_float(w[k] << 16);
+            v[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+        }
+    }
+}
+
+constexpr int STAGE_BATCH = 4;
+
+// max |x_i| and sum x_i^2 * (w_i^2 if w) over n elements (n % 8 == 0).
+__device__ __forceinline__ void vec_stats(const void* x, int dtype, size_t off, int n, const void* w,
+                                          bool cg, float& amax, float& sumsq) {
+    const int lane = threadIdx.x & 31;
+    const int nch = n / 8;
+    amax = 0.f;
+    sumsq = 0.f;
+    for (int c0 = lane; c0 < nch; c0 += 32 * STAGE_BATCH) {
+        float v[STAGE_BATCH][8];
+        float wv[STAGE_BATCH][8];
+#pragma unroll
+        for (int b = 0; b < STAGE_BATCH; ++b) {
+            const int c = c0 + 32 * b;
+            if (c < nch) {
+                load8(x, dtype, off + (size_t)c * 8, cg, v[b]);
+                if (w) load8(w, dtype, (size_t)c * 8, false, wv[b]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[b][k] = 0.f, wv[b][k] = 0.f;
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < STAGE_BATCH; ++b)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                sumsq += v[b][k] * v[b][k];
+                amax = fmaxf(amax, fabsf(w ? v[b][k] * wv[b][k] : v[b][k]));
+            }
+    }
+    amax = warp_max(amax);
+    sumsq = warp_sum(sumsq);
+}
+
+// power-of-two scale that puts amax in [2^14, 2^15) (1 if amax is 0 or not finite)
+__device__ __forceinline__ float pow2_scale(float amax) {
+    if (!(amax > 0.f) || !(amax < 3.0e38f)) return 1.f;
+    int e = 0;
+    frexpf(amax, &e);
+    return ldexpf(1.f, 15 - e);
+}
+
+// xs[i] = fp16(x[off + i] * mul * (w ? w[i] : 1)), zero beyond n; then cx.  Whole warp.
+template <int BITS>
+__device__ __forceinline__ void stage_vector(const void* x, int dtype, size_t off, int n, int npad,
+                                             const void* w, float mul, bool cg, __half* xs, float2* cx) {
+    const int lane = threadIdx.x & 31;
+    const int nch = n / 8, npch = npad / 8;
+    for (int c0 = lane; c0 < npch; c0 += 32 * STAGE_BATCH) {
+        float v[STAGE_BATCH][8];
+        float wv[STAGE_BATCH][8];
+#pragma unroll
+        for (int b = 0; b < STAGE_BATCH; ++b) {
+            const int c = c0 + 32 * b;
+            if (c < nch) {
+                load8(x, dtype, off + (size_t)c * 8, cg, v[b]);
+                if (w) load8(w, dtype, (size_t)c * 8, false, wv[b]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[b][k] = 0.f, wv[b][k] = 1.f;
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < STAGE_BATCH; ++b) {
+            const int c = c0 + 32 * b;
+            if (c < npch) {
+                uint32_t h[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    float a = v[b][2 * k] * mul, bb = v[b][2 * k + 1] * mul;
+                    if (w) a *= wv[b][2 * k], bb *= wv[b][2 * k + 1];
+                    const __half2 hh = __floats2half2_rn(a, bb);
+                    h[k] = *reinterpret_cast<const uint32_t*>(&hh);
+                }
+                *reinterpret_cast<uint4*>(xs + (size_t)c * 8) = make_uint4(h[0], h[1], h[2], h[3]);
+            }
+        }
     }
     __syncwarp();
     const int ng = npad / GS;
     for (int g = lane; g < ng; g += 32) {
         const __half2* p = reinterpret_cast<const __half2*>(xs + g * GS);
         float c = 0.f, xsum = 0.f;
-#pragma unroll 8
+#pragma unroll
         for (int j = 0; j < 32; ++j) {
-            float2 f = __half22float2(p[j]);
-            float pr = f.x + f.y;
+            const float2 f = __half22float2(p[j]);
+            const float pr = f.x + f.y;
             c += pair_offset<BITS>(j) * pr;
             xsum += pr;
         }
         cx[g] = make_float2(c, xsum);
     }
     __syncwarp();
-    return 1.f / scale;
 }
 
 // MMA steps J..31 of a tile (compile-time recursion: every pair extraction

@@ -141,6 +141,8 @@ class ExpertTable:
             out = torch.empty(T, self.hidden, dtype=out_dtype, device=dev)
         if per_k and out_per_k is None:
             out_per_k = torch.empty(T, K, self.hidden, dtype=out_dtype, device=dev)
+        if residual is not None and (residual.dtype != out_dtype or residual.shape != (T, self.hidden)):
+            raise ValueError("residual must be [T, hidden] in out_dtype")
         ws = self.workspace(T, K)
         rc = self.lib.kq_moe_decode(self.handle, layer, _ptr(x), _DT[x.dtype], T, _ptr(logits), _ptr(idx),
                                     _ptr(weights), K, _ptr(out_per_k) if per_k else None,

@@ -174,6 +174,20 @@ def test_decode_multi_layer_and_repeat(gpu):
     assert rel_l2(outs[0].cpu().numpy(), ref) < RTOL_L2
 
 
+def test_decode_workspace_reused_across_shapes(gpu):
+    """one workspace, calls with different T and K: each combine must start from zeroed counters."""
+    layer = get_layer(3, 2048, 512, 16, "f16", seed=6)
+    t = make_table(layer)
+    rng = np.random.RandomState(12)
+    for T, K in ((3, 8), (1, 4), (5, 2), (2, 8), (1, 1)):
+        x = torch.from_numpy(rng.randn(T, 2048).astype(np.float16)).cuda()
+        logits = torch.from_numpy(rng.randn(T, 16).astype(np.float32)).cuda()
+        r = t.moe(0, x, logits=logits, top_k=K, combine=True, out_dtype=torch.float32)
+        idx = r["idx"].cpu().numpy()
+        want = O.combine(layer.moe(x.float().cpu().numpy(), idx), r["weights"].cpu().numpy())
+        assert rel_l2(r["out"].cpu().numpy(), want) < RTOL_L2, (T, K)
+
+
 def test_decode_bad_expert_flags_status(gpu):
     from kandiga_b200 import _native as N
     layer = get_layer(3, 2048, 512, 8, "f16", seed=6)
