@@ -188,6 +188,19 @@ int kq_moe_decode(const kq_table* t, int layer, const void* x, int x_dtype, int 
                   void* out, int out_dtype, const void* residual, void* workspace,
                   size_t workspace_bytes, void* stream);
 
+/* kq_moe_decode without a caller workspace, for callers that cannot allocate
+ * device memory (a runtime that hands a plugin only its input and output
+ * buffers; an FFI host with no device allocator).  No counterpart in the
+ * reference.  Scratch is one fixed 8 MiB array inside libkq.so, held by every
+ * GPU that loads the library until exit; calls needing more are rejected with
+ * KQ_ERR_WORKSPACE.  The first call on a device resolves the array's device
+ * address (cudaGetSymbolAddress) and must come before any stream capture.  All
+ * calls share the array: overlapping calls on the GPU race.  Allocates nothing;
+ * device status bits are not reported.  Arguments as kq_moe_decode. */
+int kq_moe_decode_static(const kq_table* t, int layer, const void* x, int x_dtype, int T,
+                         const float* logits, int32_t* idx, float* weights, int K, void* out_per_k,
+                         void* out, int out_dtype, const void* residual, void* stream);
+
 /* Read and clear the device status word of a workspace (synchronises `stream`). */
 int kq_status_read(void* workspace, uint32_t* status, void* stream);
 

@@ -1,0 +1,74 @@
+// kq_noalloc.cu -- routed-expert decode for callers that cannot allocate.
+//
+// kq_moe_decode needs a scratch workspace (expert activations, per-expert
+// outputs for the combine, arrival counters, a status word) that the caller
+// allocates once.  Some callers cannot do that: runtimes that hand a plugin
+// only its input and output buffers and own every other byte of device memory
+// in their own pool, and hosts that reach this library through a plain FFI
+// (ctypes, cgo) with no device allocator at hand.  kq_moe_decode_static runs
+// the same kernels with the scratch taken from one fixed array in this file:
+//
+//   * the array is a file-scope __device__ buffer of KQ_STATIC_WS_BYTES bytes;
+//     every GPU that loads libkq.so holds it until the process exits;
+//   * host code cannot use the array's name as a device address, so the first
+//     call on each device (with that device current) resolves it with
+//     cudaGetSymbolAddress and caches it; make that first call before any
+//     stream capture;
+//   * every call shares the array and it keeps the last call's contents: each
+//     call clears the status word and the arrival counters before its kernels;
+//     calls that overlap on the GPU (two streams, two threads) race on it;
+//   * a call whose workspace would exceed the array is rejected with
+//     KQ_ERR_WORKSPACE and a message on stderr; nothing is allocated.
+#include <cstdio>
+#include <mutex>
+
+#include "kq_internal.h"
+
+#define KQ_STATIC_WS_BYTES (8u << 20)
+
+static __device__ __align__(256) uint8_t kq_static_ws[KQ_STATIC_WS_BYTES];
+
+namespace {
+std::mutex g_mu;
+void* g_ws[64] = {nullptr};
+}  // namespace
+
+extern "C" int kq_moe_decode_static(const kq_table* t, int layer, const void* x, int x_dtype, int T,
+                                    const float* logits, int32_t* idx, float* weights, int K,
+                                    void* out_per_k, void* out, int out_dtype, const void* residual,
+                                    void* stream) {
+    if (!t || T < 0 || K <= 0) return KQ_ERR_ARG;
+    if (T == 0) return KQ_OK;
+    const kq::MoeWs L = kq::moe_ws_layout(t, T, K);
+    if (L.total > KQ_STATIC_WS_BYTES) {
+        fprintf(stderr,
+                "[kq] kq_moe_decode_static: T=%d K=%d needs %zu bytes of scratch; the static buffer holds "
+                "%u bytes (use kq_moe_decode with a caller workspace, or fewer tokens per call)\n",
+                T, K, L.total, (unsigned)KQ_STATIC_WS_BYTES);
+        return KQ_ERR_WORKSPACE;
+    }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KQ_ERR_CUDA;
+    void* ws = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        if (!g_ws[dev]) {
+            void* p = nullptr;
+            const cudaError_t rc = cudaGetSymbolAddress(&p, kq_static_ws);
+            if (rc != cudaSuccess || !p) {
+                fprintf(stderr, "[kq] kq_moe_decode_static: cudaGetSymbolAddress failed: %s\n",
+                        cudaGetErrorString(rc));
+                return KQ_ERR_CUDA;
+            }
+            g_ws[dev] = p;
+        }
+        ws = g_ws[dev];
+    }
+    uint8_t* w = static_cast<uint8_t*>(ws);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (cudaMemsetAsync(w + L.status, 0, L.idx - L.status, s) != cudaSuccess ||
+        cudaMemsetAsync(w + L.cnt, 0, L.total - L.cnt, s) != cudaSuccess)
+        return KQ_ERR_CUDA;
+    return kq_moe_decode(t, layer, x, x_dtype, T, logits, idx, weights, K, out_per_k, out, out_dtype,
+                         residual, ws, KQ_STATIC_WS_BYTES, stream);
+}
