@@ -10,7 +10,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
-#include "../../include/kq.h"
+#include "kq.h"
 
 #ifndef KQ_WAIT_LIMIT
 // upper bound on polls of one mbarrier phase (each try_wait already blocks

@@ -8,7 +8,7 @@
 #include <algorithm>
 #include <new>
 
-#include "../../include/kq.h"
+#include "kq.h"
 #include "kq_qtile.cuh"
 
 struct kq_table {
@@ -40,7 +40,7 @@ int bkex_parse(const uint8_t* hdr, size_t n, BkexInfo* info);
 
 // Workspace carve-up for kq_moe_* (offsets in bytes, 256-aligned).
 struct MoeWs {
-    size_t status, idx, w, act, y, amax, cnt, total;
+    size_t status, idx, w, act, amax, total;
 };
 MoeWs moe_ws_layout(const kq_table* t, int T, int K);
 

@@ -1,28 +1,30 @@
 // kq_moe.cu -- routed-expert decode path and dense quantized GEMV on sm_100a.
 //
 // Kernels
-//   router_topk_kernel  softmax/top-K/renormalise, one warp per token
-//                       (kandiga/metal/moe_block.metal:419-505).
-//   qgemv_kernel        the tile engine of kq_qtile.cuh driven by a per-warp
-//                       TMA bulk-copy ring.  Four epilogues:
-//     MODE_GATEUP   gate+up rows of the routed experts -> act = silu(g)*u (fp32
-//                   scratch)  (kandiga/metal/kandiga_cpu_expert.m:372-394)
-//     MODE_DOWN     down rows -> unweighted per-expert outputs and/or the
-//                   weighted combine (+ residual) done by the last of the K
-//                   experts to finish a 16-row tile (no spin: an arrival
-//                   counter, self-resetting)
-//                   (kandiga/metal/kandiga_cpu_expert.m:396-398,
-//                    kandiga/metal/moe_block.metal:556-584)
-//     MODE_DENSE    y = W x with optional RMSNorm prologue
+//   router_topk_kernel  softmax / top-K / renormalise, one warp per token
+//                       (kandiga/metal/moe_block.metal:419-505), built on
+//                       warp_topk (REDUX max/min on order-preserving keys).
+//   qunit_kernel        one CTA per 16-row unit of a quantized matrix: the unit's
+//                       512-column tiles are spread over the CTA's warps, each
+//                       tile fetched by its own TMA bulk copy into shared memory
+//                       and consumed by the 32-MMA tile engine (kq_qtile.cuh);
+//                       the input vector is staged once per CTA; warp partials
+//                       are reduced through shared memory.  Epilogues:
+//     MODE_GATEUP      routed experts' gate+up rows -> act = silu(g) * u (fp32
+//                      scratch) + per-unit max|act|
+//                      (kandiga/metal/kandiga_cpu_expert.m:372-394)
+//     MODE_DENSE       y = W x, optional RMSNorm prologue
 //     MODE_DENSE_PAIR  y = act(Wg x) * (Wu x)
+//   moe_down_kernel     one CTA per (token, 16 hidden rows) owning all K
+//                       experts: each warp streams its experts' down tiles
+//                       (issued before the programmatic-dependent-launch wait on
+//                       the gate/up grid), and the CTA forms the per-expert
+//                       outputs and the weighted combine (+ residual) in shared
+//                       memory (kandiga/metal/kandiga_cpu_expert.m:396-398,
+//                       kandiga/metal/moe_block.metal:556-584).
 //
-// Each warp owns a ring of NBUF tile slots in shared memory.  Lane 0 issues a
-// cp.async.bulk per 16x512 tile (3.5 KB at 3-bit) as soon as a slot frees up,
-// so every warp keeps NBUF tiles of HBM traffic in flight; the whole warp
-// waits on the slot's mbarrier (bounded), pulls its lane's words into
-// registers and runs the 32-MMA tile.  The decode chain router -> gate/up ->
-// down uses programmatic dependent launch: the down kernel issues its weight
-// copies before waiting for the gate/up kernel's activations.
+// For small token counts the routing runs inside the prologues of both expert
+// kernels (no separate router launch); otherwise router_topk_kernel runs first.
 #include <cstdio>
 
 #include "kq_internal.h"
@@ -31,11 +33,14 @@ namespace kq {
 
 enum { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_DENSE = 2, MODE_DENSE_PAIR = 3 };
 
+constexpr int MAX_K = 32;
+constexpr int ROUTE_INLINE_MAX_T = 8;
+
 struct GemvParams {
     const uint8_t* base;  // layer base (MoE) or matrix base (dense)
-    size_t expert_bytes;  // MoE: bytes per expert (0 dense)
+    size_t expert_bytes;  // MoE: bytes per expert
     size_t mat_off;       // matrix offset inside an expert
-    int nrt, nst;         // row-tiles per vector, column tiles
+    int nrt, nst;         // row-tiles per vector, column tiles of the matrix
     int E;                // experts (1 for dense)
     int ncols;            // real input length
     int T, K;             // tokens, experts per token (dense: 1)
@@ -43,211 +48,93 @@ struct GemvParams {
     int x_dtype;
     const void* norm_w;
     float eps;
-    const int32_t* idx;   // [T*K]
-    const float* w;       // [T*K]
+    const float* logits;  // [T][E] when routing runs in the prologues, else null
+    int32_t* idx;         // [T*K]
+    float* w;             // [T*K]
     float* act;           // [T*K][I]
-    float* amax;          // [T*K][I/8] per gate/up tile max |act| (scales the down input)
-    int nrt_up;           // gate/up row-tiles per vector (I/8)
+    float* amax;          // [T*K][I/8] per gate/up unit max |act|
+    int nrt_up;           // gate/up units per (token, k): I/8
     int I;
-    float* y;             // [T*K][H] fp32 (combine input) or null
-    uint32_t* cnt;        // [T][nrt of the down matrix]
-    int cnt_per_token;    // counters per token (down row-tiles)
     void* out_per_k;      // [T*K][H] (out_dtype) or null
-    void* out;            // [T][rows]
+    void* out;            // [T][rows] (out_dtype) or null
     int out_dtype;
-    const void* residual;
+    const void* residual; // [T][H] (out_dtype) or null
     int act_kind;
-    int H;                // output rows (down: hidden; dense: rows or rows/2 for pair)
+    int H;                // output rows
     uint32_t* status;
-    int prefetch_before_wait;
     int mode;
 };
 
 __host__ __device__ constexpr size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-template <int BITS, int NBUF>
-__host__ __device__ constexpr size_t warp_smem(int nst) {
-    return align_up((size_t)NBUF * TileT<BITS>::BYTES + (size_t)nst * TILE_COLS * 2 +
-                        (size_t)nst * TILE_GROUPS * 8 + NBUF * 8,
-                    128);
+// ---- routing ------------------------------------------------------------------------
+
+// Order-preserving 32-bit key of a float (larger float -> larger key); +-0 share
+// a key, NaN maps to 0 (never selected, as the reference's strict '>' never
+// selects it).
+__device__ __forceinline__ uint32_t fkey(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7fffffffu) == 0u) u = 0u;
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu)) return 0u;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float kfloat(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-template <int BITS, int SB_DT, int NBUF, int WARPS>
-__global__ void __launch_bounds__(WARPS * 32) qgemv_kernel(const GemvParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    constexpr int TB = TileT<BITS>::BYTES;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int npad = p.nst * TILE_COLS, ng = npad / GS;
-    uint8_t* wb = smem + (size_t)warp * warp_smem<BITS, NBUF>(p.nst);
-    uint8_t* tiles = wb;
-    __half* xs = reinterpret_cast<__half*>(wb + NBUF * TB);
-    float2* cx = reinterpret_cast<float2*>(wb + NBUF * TB + (size_t)npad * 2);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(wb + NBUF * TB + (size_t)npad * 2 + (size_t)ng * 8);
-    const int mode = p.mode;
-    const bool is_moe = (mode == MODE_GATEUP || mode == MODE_DOWN);
-
-    if (lane == 0) {
+// Top-K (K <= 32) of E <= 32*VPL logits by one warp: K rounds of (warp max of
+// the keys, then the lowest index holding it) -- strict '>' with the lowest index
+// winning ties, as the reference's scan.  Lane k < K returns the k-th index and
+// its weight exp(l_k - max) / sum_selected exp(l_j - max).
+template <int VPL>
+__device__ __forceinline__ void warp_topk(const float* __restrict__ l, int E, int K, int& out_idx,
+                                          float& out_w) {
+    const int lane = threadIdx.x & 31;
+    uint32_t key[VPL];
 #pragma unroll
-        for (int b = 0; b < NBUF; ++b) mbar_init(&bars[b], 1);
-        fence_mbar_init();
+    for (int j = 0; j < VPL; ++j) {
+        const int i = lane + 32 * j;
+        key[j] = i < E ? fkey(__ldcg(l + i)) : 0u;
     }
-    __syncwarp();
-    if (!p.prefetch_before_wait) pdl_wait();
-
-    const int units = p.T * p.K * p.nrt;
-    const int wg = blockIdx.x * WARPS + warp, stride = gridDim.x * WARPS;
-    const int nun = wg < units ? (units - 1 - wg) / stride + 1 : 0;
-    const int ntiles = nun * p.nst;
-    const uint64_t pol = policy_evict_first();
-
-    auto issue = [&](int f) {
-        const int u = wg + (f / p.nst) * stride, st = f % p.nst;
-        const int tk = u / p.nrt, rt = u % p.nrt;
-        int e = 0;
-        if (is_moe) {
-            e = __ldcg(p.idx + tk);
-            if ((unsigned)e >= (unsigned)p.E) e = 0;  // flagged and zeroed in the epilogue
+    uint32_t lm = 0u;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) lm = max(lm, key[j]);
+    const float mx = kfloat(__reduce_max_sync(0xffffffffu, lm));
+    uint32_t my_key = 0u;
+    int my_i = -1;
+    for (int k = 0; k < K; ++k) {
+        uint32_t l2 = 0u;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) l2 = max(l2, key[j]);
+        const uint32_t g = __reduce_max_sync(0xffffffffu, l2);
+        uint32_t cand = 0xffffffffu;
+#pragma unroll
+        for (int j = VPL - 1; j >= 0; --j)
+            if (g != 0u && key[j] == g) cand = (uint32_t)(lane + 32 * j);
+        const uint32_t win = __reduce_min_sync(0xffffffffu, cand);
+        if (win != 0xffffffffu && (int)(win & 31u) == lane) {
+#pragma unroll
+            for (int j = 0; j < VPL; ++j)
+                if (j == (int)(win >> 5)) key[j] = 0u;
         }
-        const uint8_t* src =
-            p.base + (size_t)e * p.expert_bytes + p.mat_off + ((size_t)rt * p.nst + st) * TB;
-        const int slot = f % NBUF;
-        mbar_expect_tx(&bars[slot], TB);
-        bulk_g2s(tiles + (size_t)slot * TB, src, TB, &bars[slot], pol);
-    };
-    if (lane == 0)
-        for (int f = 0; f < NBUF && f < ntiles; ++f) issue(f);
-    if (p.prefetch_before_wait) pdl_wait();
-    if (mode == MODE_GATEUP && blockIdx.x == 0 && p.cnt) {
-        // The down kernel's arrival counters for this call: zeroed here, before
-        // the down kernel (which waits for this grid) can reach its combine.
-        // Their offset in the workspace depends on T and K, so a previous call
-        // with other shapes may have left other data there.
-        const int ncnt = p.T * p.cnt_per_token;
-        for (int i = threadIdx.x; i < ncnt; i += blockDim.x) p.cnt[i] = 0u;
-    }
-    pdl_launch_dependents();
-
-    int staged = -1;
-    float inv = 1.f, y0 = 0.f, y1 = 0.f;
-    for (int f = 0; f < ntiles; ++f) {
-        const int u = wg + (f / p.nst) * stride, st = f % p.nst;
-        const int tk = u / p.nrt, rt = u % p.nrt;
-        if (st == 0) {
-            const int vec = (mode == MODE_DOWN) ? tk : tk / p.K;
-            if (vec != staged) {
-                float scale = 1.f;
-                if (mode == MODE_DOWN) {
-                    // max |act| of this (token, k) from the gate/up epilogue's per-tile maxima
-                    const float* pm = p.amax + (size_t)vec * p.nrt_up;
-                    float a = 0.f;
-                    for (int i = lane; i < p.nrt_up; i += 32) a = fmaxf(a, __ldcg(pm + i));
-                    scale = pow2_scale(warp_max(a));
-                    stage_vector<BITS>(p.act, KQ_DT_F32, (size_t)vec * p.I, p.ncols, npad, nullptr, scale,
-                                       true, xs, cx);
-                } else {
-                    const size_t off = (size_t)vec * p.ncols;
-                    if (p.norm_w) {
-                        float amax, ss;
-                        vec_stats(p.x, p.x_dtype, off, p.ncols, p.norm_w, false, amax, ss);
-                        const float rinv = rsqrtf(ss / (float)p.ncols + p.eps);
-                        scale = pow2_scale(amax * rinv);
-                        stage_vector<BITS>(p.x, p.x_dtype, off, p.ncols, npad, p.norm_w, rinv * scale, false,
-                                           xs, cx);
-                    } else {
-                        if (p.x_dtype != KQ_DT_F16) {  // fp16 inputs are staged exactly, unscaled
-                            float amax, ss;
-                            vec_stats(p.x, p.x_dtype, off, p.ncols, nullptr, false, amax, ss);
-                            scale = pow2_scale(amax);
-                        }
-                        stage_vector<BITS>(p.x, p.x_dtype, off, p.ncols, npad, nullptr, scale, false, xs, cx);
-                    }
-                }
-                inv = 1.f / scale;
-                staged = vec;
-            }
-            y0 = y1 = 0.f;
-        }
-        const int slot = f % NBUF;
-        mbar_wait(&bars[slot], (uint32_t)((f / NBUF) & 1), p.status);
-        TileRegs<BITS> R;
-        tile_load<BITS>(tiles + (size_t)slot * TB, R);
-        __syncwarp();
-        if (lane == 0 && f + NBUF < ntiles) {
-            fence_proxy_async_smem();
-            issue(f + NBUF);
-        }
-        tile_compute<BITS, SB_DT>(R, st, xs, cx, y0, y1);
-        if (st != p.nst - 1) continue;
-
-        // ---- unit epilogue --------------------------------------------------------
-        quad_reduce(y0, y1);
-        const int r = lane >> 2;
-        bool valid = true;
-        if (is_moe) {
-            const int e = __ldcg(p.idx + tk);
-            valid = (unsigned)e < (unsigned)p.E;
-            if (!valid && lane == 0) set_status(p.status, KQ_DEV_BAD_EXPERT);
-        }
-        const float g = valid ? y0 * inv : 0.f, h = valid ? y1 * inv : 0.f;
-        if (mode == MODE_GATEUP || mode == MODE_DENSE_PAIR) {
-            const float a = valid ? activate(g, h, p.act_kind) : 0.f;
-            if ((lane & 3) == 0) {
-                const int row = rt * 8 + r;
-                if (mode == MODE_GATEUP)
-                    p.act[(size_t)tk * p.I + row] = a;
-                else
-                    store_from_float(p.out, p.out_dtype, (size_t)tk * p.H + row, a);
-            }
-            if (mode == MODE_GATEUP) {
-                const float m = warp_max(fabsf(a));
-                if (lane == 0) p.amax[(size_t)tk * p.nrt + rt] = m;
-            }
-            continue;
-        }
-        if (mode == MODE_DENSE) {
-            if ((lane & 3) == 0) {
-                store_from_float(p.out, p.out_dtype, (size_t)tk * p.H + rt * 16 + r, g);
-                store_from_float(p.out, p.out_dtype, (size_t)tk * p.H + rt * 16 + r + 8, h);
-            }
-            continue;
-        }
-        // MODE_DOWN
-        if ((lane & 3) == 0) {
-            const size_t o = (size_t)tk * p.H + rt * 16 + r;
-            if (p.out_per_k) {
-                store_from_float(p.out_per_k, p.out_dtype, o, g);
-                store_from_float(p.out_per_k, p.out_dtype, o + 8, h);
-            }
-            if (p.out) {
-                p.y[o] = g;
-                p.y[o + 8] = h;
-            }
-        }
-        if (!p.out) continue;
-        __threadfence();
-        __syncwarp();
-        const int t = tk / p.K;
-        uint32_t old = 0;
-        if (lane == 0) old = atomicAdd(p.cnt + (size_t)t * p.nrt + rt, 1u);
-        old = __shfl_sync(0xffffffffu, old, 0);
-        if (old == (uint32_t)(p.K - 1)) {
-            __threadfence();
-            if (lane < 16) {
-                const int row = rt * 16 + lane;
-                float acc = 0.f;
-                for (int k = 0; k < p.K; ++k)
-                    acc += __ldcg(p.y + ((size_t)t * p.K + k) * p.H + row) * __ldcg(p.w + (size_t)t * p.K + k);
-                if (p.residual) acc = load_as_float(p.residual, p.out_dtype, (size_t)t * p.H + row) + acc;
-                store_from_float(p.out, p.out_dtype, (size_t)t * p.H + row, acc);
-            }
-            if (lane == 0) atomicExch(p.cnt + (size_t)t * p.nrt + rt, 0u);
+        if (lane == k && win != 0xffffffffu) {
+            my_key = g;
+            my_i = (int)win;
         }
     }
+    const float ev = (lane < K && my_i >= 0) ? expf(kfloat(my_key) - mx) : 0.f;
+    const float esum = warp_sum(ev);
+    out_idx = my_i;
+    out_w = (lane < K && esum > 0.f) ? ev / esum : 0.f;
 }
 
-// ---- router ------------------------------------------------------------------------
-// One warp per token.  Selection compares logits (softmax is monotone) with
-// strict '>' and lowest index on ties; weights = exp(l_k - max) / sum_sel.
+__device__ __forceinline__ void warp_topk_any(const float* l, int E, int K, int& i, float& w) {
+    if (E <= 256)
+        warp_topk<8>(l, E, K, i, w);
+    else
+        warp_topk<32>(l, E, K, i, w);
+}
+
 __global__ void router_topk_kernel(const float* __restrict__ logits, int T, int E, int K,
                                    int32_t* __restrict__ idx, float* __restrict__ wout) {
     const int lane = threadIdx.x & 31;
@@ -255,100 +142,436 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int T, int 
     pdl_wait();
     pdl_launch_dependents();
     if (t >= T) return;
-    constexpr int MAXV = 32;  // E <= 1024
-    float v[MAXV];
-    const float* l = logits + (size_t)t * E;
-    float mx = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < MAXV; ++j) {
-        const int i = lane + 32 * j;
-        v[j] = i < E ? l[i] : -INFINITY;
-        mx = fmaxf(mx, v[j]);
+    int i;
+    float w;
+    warp_topk_any(logits + (size_t)t * E, E, K, i, w);
+    if (lane < K) {
+        idx[(size_t)t * K + lane] = i;
+        wout[(size_t)t * K + lane] = w;
     }
-    mx = warp_max(mx);
-    uint32_t taken = 0;
-    float esel = 0.f, esum = 0.f;
-    for (int k = 0; k < K; ++k) {
-        float bv = 0.f;
-        int bi = -1;
-#pragma unroll
-        for (int j = 0; j < MAXV; ++j) {
-            const int i = lane + 32 * j;
-            if (i < E && !((taken >> j) & 1u) && (bi < 0 || v[j] > bv)) {
-                bv = v[j];
-                bi = i;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            const bool take = oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi));
-            if (take) {
-                bv = ov;
-                bi = oi;
-            }
-        }
-        if (bi >= 0 && (bi & 31) == lane) taken |= 1u << (bi >> 5);
-        const float ev = expf(bv - mx);
-        esum += ev;
-        if (lane == k) esel = ev;
-        if (lane == 0) idx[(size_t)t * K + k] = bi;
-    }
-    if (lane < K) wout[(size_t)t * K + lane] = esel / esum;
 }
 
-// ---- launch helpers -----------------------------------------------------------------
+// ---- block-wide input staging ----------------------------------------------------------
 
-template <int BITS, int SB_DT, int NBUF>
-static cudaError_t launch_gemv(const GemvParams& p, cudaStream_t s, bool pdl, int max_blocks) {
-    constexpr int WARPS = 4;
-    const size_t smem = warp_smem<BITS, NBUF>(p.nst) * WARPS;
-    auto kern = qgemv_kernel<BITS, SB_DT, NBUF, WARPS>;
-    // raise the dynamic shared-memory limit once per instantiation (and per device)
-    static int configured_bytes[64] = {0};
+__device__ __forceinline__ void named_barrier(int id, int nthr) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthr) : "memory");
+}
+
+// Stage input vector `vec` (x row, optional RMSNorm) into xs/cx, using the
+// threads [t0, t0 + nthr) of the CTA (whole warps, sharing named barrier 1).
+// Returns 1/scale.
+template <int BITS>
+__device__ __forceinline__ float block_stage_x(const GemvParams& p, int vec, int npad, __half* xs,
+                                               float2* cx, float* scratch, int t0, int nthr) {
+    const int rank = threadIdx.x - t0, lane = rank & 31, wl = rank >> 5;
+    const size_t off = (size_t)vec * p.ncols;
+    const int nch = p.ncols / 8;
+    float scale = 1.f, rinv = 1.f;
+    if (p.norm_w != nullptr || p.x_dtype != KQ_DT_F16) {
+        float amax = 0.f, ss = 0.f;
+        for (int c = rank; c < nch; c += nthr) {
+            float v[8], wv[8];
+            load8(p.x, p.x_dtype, off + (size_t)c * 8, false, v);
+            if (p.norm_w) load8(p.norm_w, p.x_dtype, (size_t)c * 8, false, wv);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                ss += v[k] * v[k];
+                amax = fmaxf(amax, fabsf(p.norm_w ? v[k] * wv[k] : v[k]));
+            }
+        }
+        amax = warp_max(amax);
+        ss = warp_sum(ss);
+        if (lane == 0) {
+            scratch[wl] = amax;
+            scratch[16 + wl] = ss;
+        }
+        named_barrier(1, nthr);
+        amax = 0.f;
+        ss = 0.f;
+        for (int w = 0; w < nthr / 32; ++w) {
+            amax = fmaxf(amax, scratch[w]);
+            ss += scratch[16 + w];
+        }
+        if (p.norm_w) rinv = rsqrtf(ss / (float)p.ncols + p.eps);
+        scale = pow2_scale(amax * rinv);
+    }
+    stage_fused<BITS, 2>(p.x, p.x_dtype, off, p.ncols, npad, rinv * scale, false, rank, nthr, xs, cx, p.norm_w);
+    return 1.f / scale;
+}
+
+// Warp-level staging of a down-projection input: act row (fp32) scaled by the
+// power of two derived from the gate/up units' max |act|.  The max and the first
+// chunks are loaded together, so one round trip covers both.  Returns 1/scale.
+template <int BITS>
+__device__ __forceinline__ float stage_act_warp(const float* act, const float* amax, int n_part, int n,
+                                                int npad, __half* xs, float2* cx) {
+    const int lane = threadIdx.x & 31;
+    const int nch = n / 8, npch = npad / 8;
+    constexpr int MAXB = 4;
+    float am = 0.f;
+    for (int i = lane; i < n_part; i += 32) am = fmaxf(am, __ldcg(amax + i));
+    float v[MAXB][8];
+#pragma unroll
+    for (int b = 0; b < MAXB; ++b) {
+        const int c = lane + 32 * b;
+        if (c < nch)
+            load8(act, KQ_DT_F32, (size_t)c * 8, true, v[b]);
+        else
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[b][k] = 0.f;
+    }
+    const float scale = pow2_scale(warp_max(am));
+    float offv[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) offv[k] = chunk_offset<BITS>(lane & 7, k);
+#pragma unroll
+    for (int b = 0; b < MAXB; ++b) {
+        const int c = lane + 32 * b;
+        if (c < npch) {
+            const float2 part = store_chunk<BITS>(v[b], scale, offv, xs, c);
+            group_reduce_store(part, lane, c, cx, 0xffffffffu);
+        }
+    }
+    if (npch > 32 * MAXB)  // longer rows: the rest with the generic loop
+        stage_fused<BITS, MAXB>(act, KQ_DT_F32, (size_t)32 * MAXB * 8, n - 32 * MAXB * 8 > 0 ? n - 32 * MAXB * 8 : 0,
+                                npad - 32 * MAXB * 8, scale, true, lane, 32, xs + 32 * MAXB * 8, cx + 4 * MAXB);
+    __syncwarp();
+    return 1.f / scale;
+}
+
+// ---- qunit_kernel: gate/up and dense matrices ---------------------------------------------
+
+template <int BITS, int NW, int NBUF>
+__host__ __device__ constexpr size_t qunit_smem(int nst) {
+    return align_up((size_t)NW * NBUF * TileT<BITS>::BYTES, 128) +     // tiles
+           align_up((size_t)nst * TILE_COLS * 2, 128) +                  // xs
+           align_up((size_t)nst * TILE_GROUPS * 8, 128) +                // cx
+           align_up((size_t)NW * 32 * 8, 128) +                          // warp partials
+           align_up((size_t)NW * NBUF * 8, 128) +                        // mbarriers
+           256;                                                           // scratch
+}
+
+template <int BITS, int SB_DT, int NW, int NBUF>
+__global__ void __launch_bounds__(NW * 32) qunit_kernel(const GemvParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int TB = TileT<BITS>::BYTES;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int npad = p.nst * TILE_COLS, ng = npad / GS;
+    uint8_t* sp = smem;
+    uint8_t* tiles = sp;
+    sp += align_up((size_t)NW * NBUF * TB, 128);
+    __half* xs = reinterpret_cast<__half*>(sp);
+    sp += align_up((size_t)npad * 2, 128);
+    float2* cx = reinterpret_cast<float2*>(sp);
+    sp += align_up((size_t)ng * 8, 128);
+    float2* red = reinterpret_cast<float2*>(sp);
+    sp += align_up((size_t)NW * 32 * 8, 128);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sp);
+    sp += align_up((size_t)NW * NBUF * 8, 128);
+    float* scratch = reinterpret_cast<float*>(sp);   // 2*NW floats
+    int* s_e = reinterpret_cast<int*>(sp + 192);     // expert id of this unit
+
+    float* s_inv = reinterpret_cast<float*>(sp + 196);  // 1/scale of the staged input
+
+    const int mode = p.mode;
+    const int u = blockIdx.x;
+    const int tk = u / p.nrt, rt = u % p.nrt;
+    const int t = tk / p.K, k = tk % p.K;
+    uint8_t* my_tiles = tiles + (size_t)warp * NBUF * TB;
+    uint64_t* my_bars = bars + warp * NBUF;
+    if (tid == 0) {  // every warp's barriers, so warp 0 may issue copies for all of them
+        for (int b = 0; b < NW * NBUF; ++b) mbar_init(&bars[b], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    auto ntiles_of = [&](int w) { return w < p.nst ? (p.nst - 1 - w) / NW + 1 : 0; };
+    const int ntl = ntiles_of(warp);  // this warp's tiles: st = warp, warp + NW, ...
+    const uint64_t pol = policy_evict_first();
+    auto issue_for = [&](int w, int i, const uint8_t* mb) {
+        const int st = w + i * NW, slot = i % NBUF;
+        uint64_t* bar = bars + w * NBUF + slot;
+        mbar_expect_tx(bar, TB);
+        bulk_g2s(tiles + ((size_t)w * NBUF + slot) * TB, mb + ((size_t)rt * p.nst + st) * TB, TB, bar, pol);
+    };
+
+    bool valid = true;
+    const uint8_t* mbase = p.base + p.mat_off;
+    float inv = 1.f;
+    if (mode == MODE_GATEUP) {
+        pdl_wait();  // routing inputs and x come from earlier work on the stream
+        pdl_launch_dependents();
+        if (warp == 0) {
+            // routing, then every warp's first tiles; warps 1.. stage x meanwhile
+            int e;
+            if (p.logits) {
+                int ix;
+                float wt;
+                warp_topk<8>(p.logits + (size_t)t * p.E, p.E, p.K, ix, wt);
+                if (rt == 0 && k == 0 && lane < p.K) {  // one CTA per token publishes the routing
+                    p.idx[(size_t)t * p.K + lane] = ix;
+                    p.w[(size_t)t * p.K + lane] = wt;
+                }
+                e = __shfl_sync(0xffffffffu, ix, k);
+            } else {
+                e = __ldcg(p.idx + tk);
+            }
+            if (lane == 0) {
+                *s_e = e;
+                const uint8_t* mb = mbase + (size_t)((unsigned)e < (unsigned)p.E ? e : 0) * p.expert_bytes;
+                for (int w = 0; w < NW; ++w)
+                    for (int i = 0; i < NBUF && i < ntiles_of(w); ++i) issue_for(w, i, mb);
+            }
+        } else {
+            const float iv = block_stage_x<BITS>(p, t, npad, xs, cx, scratch, 32, (NW - 1) * 32);
+            if (tid == 32) *s_inv = iv;
+        }
+        __syncthreads();
+        int e = *s_e;
+        inv = *s_inv;
+        valid = (unsigned)e < (unsigned)p.E;
+        if (!valid) {
+            e = 0;  // a real expert was addressed; rows are zeroed and the condition latched
+            if (tid == 0) set_status(p.status, KQ_DEV_BAD_EXPERT);
+        }
+        mbase += (size_t)e * p.expert_bytes;
+    } else {
+        if (lane == 0)  // dense weights do not depend on earlier work: fetch before the wait
+            for (int i = 0; i < NBUF && i < ntl; ++i) issue_for(warp, i, mbase);
+        pdl_wait();
+        pdl_launch_dependents();
+        inv = block_stage_x<BITS>(p, tk, npad, xs, cx, scratch, 0, NW * 32);
+        __syncthreads();
+    }
+
+    float y0 = 0.f, y1 = 0.f;
+    for (int i = 0; i < ntl; ++i) {
+        const int slot = i % NBUF;
+        mbar_wait(&my_bars[slot], (uint32_t)((i / NBUF) & 1), p.status);
+        TileRegs<BITS> R;
+        tile_load<BITS>(my_tiles + (size_t)slot * TB, R);
+        __syncwarp();
+        if (lane == 0 && i + NBUF < ntl) {
+            fence_proxy_async_smem();
+            issue_for(warp, i + NBUF, mbase);
+        }
+        tile_compute<BITS, SB_DT>(R, warp + i * NW, xs, cx, y0, y1);
+    }
+    red[warp * 32 + lane] = make_float2(y0, y1);
+    __syncthreads();
+    if (warp != 0) return;
+    y0 = 0.f;
+    y1 = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        const float2 v = red[w * 32 + lane];
+        y0 += v.x;
+        y1 += v.y;
+    }
+    quad_reduce(y0, y1);
+    const int r = lane >> 2;
+    const float g = valid ? y0 * inv : 0.f, h = valid ? y1 * inv : 0.f;
+    if (mode == MODE_DENSE) {
+        if ((lane & 3) == 0) {
+            store_from_float(p.out, p.out_dtype, (size_t)tk * p.H + rt * 16 + r, g);
+            store_from_float(p.out, p.out_dtype, (size_t)tk * p.H + rt * 16 + r + 8, h);
+        }
+        return;
+    }
+    const float a = valid ? activate(g, h, p.act_kind) : 0.f;
+    if (mode == MODE_DENSE_PAIR) {
+        if ((lane & 3) == 0) store_from_float(p.out, p.out_dtype, (size_t)tk * p.H + rt * 8 + r, a);
+        return;
+    }
+    if ((lane & 3) == 0) p.act[(size_t)tk * p.I + rt * 8 + r] = a;
+    const float m = warp_max(fabsf(a));
+    if (lane == 0) p.amax[(size_t)tk * p.nrt + rt] = m;
+}
+
+// ---- moe_down_kernel ------------------------------------------------------------------------
+
+constexpr int DOWN_NW = 8;
+constexpr int DOWN_NBUF = 2;
+
+template <int BITS>
+__host__ __device__ constexpr size_t down_warp_smem(int nst) {
+    return align_up((size_t)DOWN_NBUF * TileT<BITS>::BYTES + (size_t)nst * TILE_COLS * 2 +
+                        (size_t)nst * TILE_GROUPS * 8 + DOWN_NBUF * 8,
+                    128);
+}
+template <int BITS>
+__host__ __device__ constexpr size_t down_smem(int nst) {
+    return DOWN_NW * down_warp_smem<BITS>(nst) + MAX_K * 16 * 4 + MAX_K * 8 + 128;
+}
+
+template <int BITS, int SB_DT>
+__global__ void __launch_bounds__(DOWN_NW * 32, 1) moe_down_kernel(const GemvParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int TB = TileT<BITS>::BYTES;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int npad = p.nst * TILE_COLS, ng = npad / GS;
+    uint8_t* wb = smem + (size_t)warp * down_warp_smem<BITS>(p.nst);
+    uint8_t* tiles = wb;
+    __half* xs = reinterpret_cast<__half*>(wb + DOWN_NBUF * TB);
+    float2* cx = reinterpret_cast<float2*>(wb + DOWN_NBUF * TB + (size_t)npad * 2);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(wb + DOWN_NBUF * TB + (size_t)npad * 2 + (size_t)ng * 8);
+    float* red = reinterpret_cast<float*>(smem + DOWN_NW * down_warp_smem<BITS>(p.nst));  // [MAX_K][16]
+    int* s_idx = reinterpret_cast<int*>(red + MAX_K * 16);
+    float* s_w = reinterpret_cast<float*>(s_idx + MAX_K);
+
+    const int t = blockIdx.x / p.nrt, rt = blockIdx.x % p.nrt;
+    if (lane == 0) {
+#pragma unroll
+        for (int b = 0; b < DOWN_NBUF; ++b) mbar_init(&bars[b], 1);
+        fence_mbar_init();
+    }
+    // Routing of token t.  The gate/up grid may still be running: routing is
+    // recomputed from the logits (or read from idx, written before that grid
+    // started), so the down weights can be fetched before the dependency wait.
+    if (p.logits) {
+        if (warp == 0) {
+            int ix;
+            float wt;
+            warp_topk<8>(p.logits + (size_t)t * p.E, p.E, p.K, ix, wt);
+            if (lane < p.K) {
+                s_idx[lane] = ix;
+                s_w[lane] = wt;
+            }
+        }
+    } else if (tid < p.K) {
+        s_idx[tid] = __ldcg(p.idx + (size_t)t * p.K + tid);
+        s_w[tid] = p.w ? __ldcg(p.w + (size_t)t * p.K + tid) : 0.f;
+    }
+    __syncthreads();
+    // this warp's experts: k = warp, warp + DOWN_NW, ...; tiles f = j * nst + st
+    const int nexp = warp < p.K ? (p.K - 1 - warp) / DOWN_NW + 1 : 0;
+    const int ntl = nexp * p.nst;
+    const uint64_t pol = policy_evict_first();
+    auto issue = [&](int f) {
+        const int kk = warp + (f / p.nst) * DOWN_NW, st = f % p.nst;
+        int e = s_idx[kk];
+        if ((unsigned)e >= (unsigned)p.E) e = 0;
+        const uint8_t* src = p.base + (size_t)e * p.expert_bytes + p.mat_off + ((size_t)rt * p.nst + st) * TB;
+        const int slot = f % DOWN_NBUF;
+        mbar_expect_tx(&bars[slot], TB);
+        bulk_g2s(tiles + (size_t)slot * TB, src, TB, &bars[slot], pol);
+    };
+    if (lane == 0)
+        for (int f = 0; f < DOWN_NBUF && f < ntl; ++f) issue(f);
+    pdl_launch_dependents();
+    pdl_wait();  // gate/up activations are complete and visible
+
+    for (int j = 0; j < nexp; ++j) {
+        const int kk = warp + j * DOWN_NW;
+        const size_t tk = (size_t)t * p.K + kk;
+        const bool valid = (unsigned)s_idx[kk] < (unsigned)p.E;
+        const float inv = stage_act_warp<BITS>(p.act + tk * p.I, p.amax + tk * p.nrt_up, p.nrt_up, p.ncols,
+                                               npad, xs, cx);
+        float y0 = 0.f, y1 = 0.f;
+        for (int st = 0; st < p.nst; ++st) {
+            const int f = j * p.nst + st, slot = f % DOWN_NBUF;
+            mbar_wait(&bars[slot], (uint32_t)((f / DOWN_NBUF) & 1), p.status);
+            TileRegs<BITS> R;
+            tile_load<BITS>(tiles + (size_t)slot * TB, R);
+            __syncwarp();
+            if (lane == 0 && f + DOWN_NBUF < ntl) {
+                fence_proxy_async_smem();
+                issue(f + DOWN_NBUF);
+            }
+            tile_compute<BITS, SB_DT>(R, st, xs, cx, y0, y1);
+        }
+        quad_reduce(y0, y1);
+        const float g = valid ? y0 * inv : 0.f, h = valid ? y1 * inv : 0.f;
+        if (!valid && lane == 0) set_status(p.status, KQ_DEV_BAD_EXPERT);
+        if ((lane & 3) == 0) {
+            const int r = lane >> 2;
+            if (p.out_per_k) {
+                const size_t o = tk * p.H + rt * 16 + r;
+                store_from_float(p.out_per_k, p.out_dtype, o, g);
+                store_from_float(p.out_per_k, p.out_dtype, o + 8, h);
+            }
+            red[kk * 16 + r] = g;
+            red[kk * 16 + r + 8] = h;
+        }
+    }
+    if (!p.out) return;
+    __syncthreads();
+    if (tid < 16) {
+        const int row = rt * 16 + tid;
+        float acc = 0.f;
+        for (int kk = 0; kk < p.K; ++kk) acc += red[kk * 16 + tid] * s_w[kk];
+        if (p.residual) acc = load_as_float(p.residual, p.out_dtype, (size_t)t * p.H + row) + acc;
+        store_from_float(p.out, p.out_dtype, (size_t)t * p.H + row, acc);
+    }
+}
+
+// ---- launch helpers -----------------------------------------------------------------------------
+
+// Raise a kernel's dynamic shared-memory limit once per device.
+template <typename Kern>
+static cudaError_t smem_attr(Kern kern, size_t bytes, int* configured) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if ((size_t)configured_bytes[dev] < smem) {
-        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if ((size_t)configured[dev] < bytes) {
+        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
         if (err != cudaSuccess) return err;
-        configured_bytes[dev] = (int)smem;
+        configured[dev] = (int)bytes;
     }
-    const int units = p.T * p.K * p.nrt;
-    int blocks = (units + WARPS - 1) / WARPS;
-    if (max_blocks > 0 && blocks > max_blocks) blocks = max_blocks;
-    if (blocks < 1) blocks = 1;
+    return cudaSuccess;
+}
+
+template <typename Kern>
+static cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              const GemvParams& p) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(blocks);
-    cfg.blockDim = dim3(WARPS * 32);
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-static cudaError_t dispatch_gemv(int bits, int sb_dt, bool down, const GemvParams& p, cudaStream_t s,
-                                 bool pdl) {
-    const int maxb = 148 * 8;
-    if (bits == 3) {
-        if (down) return sb_dt == KQ_DT_F16 ? launch_gemv<3, KQ_DT_F16, 2>(p, s, pdl, maxb)
-                                            : launch_gemv<3, KQ_DT_BF16, 2>(p, s, pdl, maxb);
-        return sb_dt == KQ_DT_F16 ? launch_gemv<3, KQ_DT_F16, 4>(p, s, pdl, maxb)
-                                  : launch_gemv<3, KQ_DT_BF16, 4>(p, s, pdl, maxb);
-    }
-    if (down) return sb_dt == KQ_DT_F16 ? launch_gemv<4, KQ_DT_F16, 2>(p, s, pdl, maxb)
-                                        : launch_gemv<4, KQ_DT_BF16, 2>(p, s, pdl, maxb);
-    return sb_dt == KQ_DT_F16 ? launch_gemv<4, KQ_DT_F16, 4>(p, s, pdl, maxb)
-                              : launch_gemv<4, KQ_DT_BF16, 4>(p, s, pdl, maxb);
+constexpr int QUNIT_NW = 4;
+constexpr int QUNIT_NBUF = 2;
+
+template <int BITS, int SB_DT>
+static cudaError_t launch_qunit_t(const GemvParams& p, cudaStream_t s) {
+    static int configured[64] = {0};
+    auto kern = qunit_kernel<BITS, SB_DT, QUNIT_NW, QUNIT_NBUF>;
+    const size_t smem = qunit_smem<BITS, QUNIT_NW, QUNIT_NBUF>(p.nst);
+    cudaError_t err = smem_attr(kern, smem, configured);
+    if (err != cudaSuccess) return err;
+    const long units = (long)p.T * p.K * p.nrt;
+    return launch_pdl(kern, dim3((unsigned)units), dim3(QUNIT_NW * 32), smem, s, p);
+}
+
+template <int BITS, int SB_DT>
+static cudaError_t launch_down_t(const GemvParams& p, cudaStream_t s) {
+    static int configured[64] = {0};
+    auto kern = moe_down_kernel<BITS, SB_DT>;
+    const size_t smem = down_smem<BITS>(p.nst);
+    cudaError_t err = smem_attr(kern, smem, configured);
+    if (err != cudaSuccess) return err;
+    return launch_pdl(kern, dim3((unsigned)(p.T * p.nrt)), dim3(DOWN_NW * 32), smem, s, p);
+}
+
+static cudaError_t launch_qunit(int bits, int sb_dt, const GemvParams& p, cudaStream_t s) {
+    if (bits == 3) return sb_dt == KQ_DT_F16 ? launch_qunit_t<3, KQ_DT_F16>(p, s) : launch_qunit_t<3, KQ_DT_BF16>(p, s);
+    return sb_dt == KQ_DT_F16 ? launch_qunit_t<4, KQ_DT_F16>(p, s) : launch_qunit_t<4, KQ_DT_BF16>(p, s);
+}
+
+static cudaError_t launch_down(int bits, int sb_dt, const GemvParams& p, cudaStream_t s) {
+    if (bits == 3) return sb_dt == KQ_DT_F16 ? launch_down_t<3, KQ_DT_F16>(p, s) : launch_down_t<3, KQ_DT_BF16>(p, s);
+    return sb_dt == KQ_DT_F16 ? launch_down_t<4, KQ_DT_F16>(p, s) : launch_down_t<4, KQ_DT_BF16>(p, s);
 }
 
 static cudaError_t launch_router(const float* logits, int T, int E, int K, int32_t* idx, float* w,
-                                 cudaStream_t s, bool pdl) {
+                                 cudaStream_t s) {
     const int warps = 4;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((T + warps - 1) / warps);
@@ -358,7 +581,7 @@ static cudaError_t launch_router(const float* logits, int T, int E, int K, int32
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, router_topk_kernel, logits, T, E, K, idx, w);
 }
 
@@ -373,12 +596,8 @@ MoeWs moe_ws_layout(const kq_table* t, int T, int K) {
     o = align_up(o + (size_t)T * K * 4, 256);
     L.act = o;
     o = align_up(o + (size_t)T * K * t->d.inter * 4, 256);
-    L.y = o;
-    o = align_up(o + (size_t)T * K * t->d.hidden * 4, 256);
     L.amax = o;
     o = align_up(o + (size_t)T * K * t->i8 * 4, 256);
-    L.cnt = o;
-    o = align_up(o + (size_t)T * t->h16 * 4, 256);
     L.total = o;
     return L;
 }
@@ -411,11 +630,10 @@ extern "C" int kq_status_read(void* workspace, uint32_t* status, void* stream) {
 
 extern "C" int kq_router_topk(const float* logits, int T, int E, int K, int32_t* idx, float* weights,
                               void* stream) {
-    if (T < 0 || E <= 0 || E > 1024 || K <= 0 || K > E || K > 32) return KQ_ERR_ARG;
+    if (T < 0 || E <= 0 || E > 1024 || K <= 0 || K > E || K > MAX_K) return KQ_ERR_ARG;
     if (T == 0) return KQ_OK;
     if (!logits || !idx || !weights) return KQ_ERR_ARG;
-    return launch_router(logits, T, E, K, idx, weights, static_cast<cudaStream_t>(stream), false) ==
-                   cudaSuccess
+    return launch_router(logits, T, E, K, idx, weights, static_cast<cudaStream_t>(stream)) == cudaSuccess
                ? KQ_OK
                : KQ_ERR_CUDA;
 }
@@ -426,7 +644,7 @@ extern "C" int kq_moe_decode(const kq_table* t, int layer, const void* x, int x_
                              void* workspace, size_t workspace_bytes, void* stream) {
     if (!t) return KQ_ERR_ARG;
     if (layer < 0 || layer >= t->d.num_layers) return KQ_ERR_ARG;
-    if (T < 0 || K <= 0 || K > 32 || K > t->d.num_experts) return KQ_ERR_ARG;
+    if (T < 0 || K <= 0 || K > MAX_K || K > t->d.num_experts) return KQ_ERR_ARG;
     if (T == 0) return KQ_OK;
     if (!x || !valid_dtype(x_dtype)) return KQ_ERR_ARG;
     if (!logits && !idx) return KQ_ERR_ARG;
@@ -441,10 +659,9 @@ extern "C" int kq_moe_decode(const kq_table* t, int layer, const void* x, int x_
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     int32_t* idx_use = idx ? idx : reinterpret_cast<int32_t*>(ws + L.idx);
     float* w_use = weights ? weights : reinterpret_cast<float*>(ws + L.w);
-    const bool pdl = true;
-    if (logits) {
-        if (launch_router(logits, T, t->d.num_experts, K, idx_use, w_use, s, false) != cudaSuccess)
-            return KQ_ERR_CUDA;
+    const bool inline_route = logits && T <= ROUTE_INLINE_MAX_T && t->d.num_experts <= 256;
+    if (logits && !inline_route) {
+        if (launch_router(logits, T, t->d.num_experts, K, idx_use, w_use, s) != cudaSuccess) return KQ_ERR_CUDA;
     }
     GemvParams p{};
     p.base = t->base + (size_t)layer * t->layer_bytes;
@@ -452,27 +669,24 @@ extern "C" int kq_moe_decode(const kq_table* t, int layer, const void* x, int x_
     p.E = t->d.num_experts;
     p.T = T;
     p.K = K;
+    p.logits = inline_route ? logits : nullptr;
     p.idx = idx_use;
     p.w = w_use;
     p.act = reinterpret_cast<float*>(ws + L.act);
     p.amax = reinterpret_cast<float*>(ws + L.amax);
     p.nrt_up = t->i8;
     p.I = t->d.inter;
-    p.y = reinterpret_cast<float*>(ws + L.y);
-    p.cnt = reinterpret_cast<uint32_t*>(ws + L.cnt);
-    p.cnt_per_token = t->h16;
     p.status = reinterpret_cast<uint32_t*>(ws + L.status);
     p.act_kind = t->d.activation;
     p.x = x;
     p.x_dtype = x_dtype;
-    // gate/up
+    // gate/up + SwiGLU
     p.mode = MODE_GATEUP;
     p.mat_off = 0;
     p.nrt = t->i8;
     p.nst = t->nst_h;
     p.ncols = t->d.hidden;
-    p.prefetch_before_wait = 0;
-    if (dispatch_gemv(t->d.bits, t->d.sb_dtype, false, p, s, pdl) != cudaSuccess) return KQ_ERR_CUDA;
+    if (launch_qunit(t->d.bits, t->d.sb_dtype, p, s) != cudaSuccess) return KQ_ERR_CUDA;
     // down (+ combine)
     p.mode = MODE_DOWN;
     p.mat_off = t->gateup_bytes;
@@ -484,8 +698,7 @@ extern "C" int kq_moe_decode(const kq_table* t, int layer, const void* x, int x_
     p.out = out;
     p.out_dtype = out_dtype;
     p.residual = residual;
-    p.prefetch_before_wait = 1;
-    if (dispatch_gemv(t->d.bits, t->d.sb_dtype, true, p, s, true) != cudaSuccess) return KQ_ERR_CUDA;
+    if (launch_down(t->d.bits, t->d.sb_dtype, p, s) != cudaSuccess) return KQ_ERR_CUDA;
     return KQ_OK;
 }
 
@@ -526,10 +739,6 @@ extern "C" int kq_qmat_destroy(kq_qmat* m) {
     return KQ_OK;
 }
 
-namespace kq {
-int qmat_repack(kq_qmat* m, const kq_mlx_matrix* a, const kq_mlx_matrix* b, cudaStream_t s);
-}
-
 extern "C" int kq_dense_gemv(const kq_qmat* m, const void* x, int x_dtype, int T, const void* norm_w,
                              float eps, int activation, void* y, int y_dtype, void* stream) {
     if (!m || !x || !y) return KQ_ERR_ARG;
@@ -555,9 +764,7 @@ extern "C" int kq_dense_gemv(const kq_qmat* m, const void* x, int x_dtype, int T
     p.act_kind = activation;
     p.H = m->rows;
     p.mode = m->pair ? MODE_DENSE_PAIR : MODE_DENSE;
-    p.prefetch_before_wait = 1;
-    return dispatch_gemv(m->bits, m->sb_dtype, false, p, static_cast<cudaStream_t>(stream), true) ==
-                   cudaSuccess
+    return launch_qunit(m->bits, m->sb_dtype, p, static_cast<cudaStream_t>(stream)) == cudaSuccess
                ? KQ_OK
                : KQ_ERR_CUDA;
 }

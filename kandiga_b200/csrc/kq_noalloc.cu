@@ -15,7 +15,8 @@
 //     cudaGetSymbolAddress and caches it; make that first call before any
 //     stream capture;
 //   * every call shares the array and it keeps the last call's contents: each
-//     call clears the status word and the arrival counters before its kernels;
+//     call clears the status word (the only part that must start at zero; the
+//     rest is written before it is read) before its kernels;
 //     calls that overlap on the GPU (two streams, two threads) race on it;
 //   * a call whose workspace would exceed the array is rejected with
 //     KQ_ERR_WORKSPACE and a message on stderr; nothing is allocated.
@@ -66,9 +67,7 @@ extern "C" int kq_moe_decode_static(const kq_table* t, int layer, const void* x,
     }
     uint8_t* w = static_cast<uint8_t*>(ws);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (cudaMemsetAsync(w + L.status, 0, L.idx - L.status, s) != cudaSuccess ||
-        cudaMemsetAsync(w + L.cnt, 0, L.total - L.cnt, s) != cudaSuccess)
-        return KQ_ERR_CUDA;
+    if (cudaMemsetAsync(w + L.status, 0, L.idx - L.status, s) != cudaSuccess) return KQ_ERR_CUDA;
     return kq_moe_decode(t, layer, x, x_dtype, T, logits, idx, weights, K, out_per_k, out, out_dtype,
                          residual, ws, KQ_STATIC_WS_BYTES, stream);
 }

@@ -230,10 +230,95 @@ __device__ __forceinline__ void stage_vector(const void* x, int dtype, size_t of
     __syncwarp();
 }
 
+// ---- fused staging: fp16 conversion + per-group constants in one pass -------------
+// A chunk is 8 consecutive inputs = 4 pairs; group g holds chunks 8g..8g+7 and
+// chunk c covers pairs 4*(c%8) .. 4*(c%8)+3 of group c/8.  Threads that stage
+// chunk c also produce its part of C[g] and X[g] (from the fp16 values the MMA
+// will read); 8 consecutive ranks hold the 8 chunks of a group and finish the
+// sums with three shuffles.  `rank` is the thread's index among `nthr`
+// participating threads (nthr a multiple of 32), so c % 8 == rank % 8.
+
+template <int BITS>
+__device__ __forceinline__ float chunk_offset(int c8, int k) {
+    return pair_offset<BITS>(4 * c8 + k);
+}
+
+// scaled floats -> fp16 chunk c of xs; returns (C part, X part) of the chunk
+template <int BITS>
+__device__ __forceinline__ float2 store_chunk(const float (&v)[8], float mul, const float (&off)[4],
+                                              __half* xs, int c) {
+    uint32_t h[4];
+    float cc = 0.f, xx = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const __half2 hh = __floats2half2_rn(v[2 * k] * mul, v[2 * k + 1] * mul);
+        h[k] = *reinterpret_cast<const uint32_t*>(&hh);
+        const float2 f = __half22float2(hh);
+        const float pr = f.x + f.y;
+        cc += off[k] * pr;
+        xx += pr;
+    }
+    *reinterpret_cast<uint4*>(xs + (size_t)c * 8) = make_uint4(h[0], h[1], h[2], h[3]);
+    return make_float2(cc, xx);
+}
+
+// reduce a chunk's (C, X) over the 8 ranks of its group; rank%8 == 0 stores cx[g]
+__device__ __forceinline__ void group_reduce_store(float2 v, int rank, int c, float2* cx, unsigned mask) {
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+        v.x += __shfl_xor_sync(mask, v.x, o);
+        v.y += __shfl_xor_sync(mask, v.y, o);
+    }
+    if ((rank & 7) == 0) cx[c >> 3] = v;
+}
+
+// Stage n elements of `src` (dtype, starting at element `off`) times `mul` into
+// xs (zero-padded to npad) and cx.  Called by `nthr` threads with ranks 0..nthr-1
+// (whole warps); loads of a thread's chunks are issued before any is used.
+template <int BITS, int MAXB>
+__device__ __forceinline__ void stage_fused(const void* src, int dtype, size_t off, int n, int npad,
+                                            float mul, bool cg, int rank, int nthr, __half* xs,
+                                            float2* cx, const void* w2 = nullptr) {
+    const int nch = n / 8, npch = npad / 8;
+    float offv[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) offv[k] = chunk_offset<BITS>(rank & 7, k);
+    for (int c0 = rank; c0 < npch; c0 += nthr * MAXB) {
+        float v[MAXB][8];
+#pragma unroll
+        for (int b = 0; b < MAXB; ++b) {
+            const int c = c0 + b * nthr;
+            if (c < nch) {
+                load8(src, dtype, off + (size_t)c * 8, cg, v[b]);
+                if (w2) {
+                    float wv[8];
+                    load8(w2, dtype, (size_t)c * 8, false, wv);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) v[b][k] *= wv[k];
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[b][k] = 0.f;
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < MAXB; ++b) {
+            const int c = c0 + b * nthr;
+            // npch is a multiple of 64 and ranks come in whole warps, so `c < npch`
+            // is uniform across a warp and the full-warp shuffles are safe
+            if (c < npch) {
+                const float2 part = store_chunk<BITS>(v[b], mul, offv, xs, c);
+                group_reduce_store(part, rank, c, cx, 0xffffffffu);
+            }
+        }
+    }
+}
+
 // MMA steps J..31 of a tile (compile-time recursion: every pair extraction
 // uses constant masks and shifts).  x pairs J..J+3 arrive in one 16-byte load.
+// Two accumulator sets (pair index parity) halve the dependent MMA chain.
 template <int BITS, int J>
-__device__ __forceinline__ void mma_steps(float (&d)[4], const uint32_t (&wd)[4][TileT<BITS>::W],
+__device__ __forceinline__ void mma_steps(float (&d)[2][4], const uint32_t (&wd)[4][TileT<BITS>::W],
                                           const uint32_t (&sh)[4][TileT<BITS>::W],
                                           const uint4* xp, bool has_x, bool use_b0, bool use_b1) {
     if constexpr (J < 32) {
@@ -258,7 +343,7 @@ __device__ __forceinline__ void mma_steps(float (&d)[4], const uint32_t (&wd)[4]
                 a0 = pair_of<BITS, J + 3>(wd[0], sh[0]); a1 = pair_of<BITS, J + 3>(wd[2], sh[2]);
                 a2 = pair_of<BITS, J + 3>(wd[1], sh[1]); a3 = pair_of<BITS, J + 3>(wd[3], sh[3]);
             }
-            mma_f16(d, a0, a1, a2, a3, b0, b1);
+            mma_f16(d[u & 1], a0, a1, a2, a3, b0, b1);
         }
         mma_steps<BITS, J + 4>(d, wd, sh, xp, has_x, use_b0, use_b1);
     }
@@ -308,8 +393,11 @@ __device__ __forceinline__ void tile_compute(const TileRegs<BITS>& R, int st, co
     const int xg = use_b0 ? t : (use_b1 ? t + 4 : 0);
     const uint4* xp = reinterpret_cast<const uint4*>(xs + st * TILE_COLS + xg * GS);
 
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
-    mma_steps<BITS, 0>(d, R.wd, sh, xp, use_b0 || use_b1, use_b0, use_b1);
+    float acc[2][4] = {};
+    mma_steps<BITS, 0>(acc, R.wd, sh, xp, use_b0 || use_b1, use_b0, use_b1);
+    float d[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = acc[0][i] + acc[1][i];
 
     // epilogue: groups G0 = 2t, G1 = 2t+1 of this column tile
     const float4 cx = *reinterpret_cast<const float4*>(cxv + st * TILE_GROUPS + 2 * t);
