@@ -222,6 +222,15 @@ int kq_qmat_unpack_mlx(const kq_qmat* m, int which, void* weight, void* scales, 
 int kq_dense_gemv(const kq_qmat* m, const void* x, int x_dtype, int T, const void* norm_w,
                   float eps, int activation, void* y, int y_dtype, void* stream);
 
+/* ---- tensor-core building block ---------------------------------------------- */
+
+/* C[M][N] (fp32) = A[M][K] * B[N][K]^T with fp16 A, B (K contiguous), on the
+ * 5th-generation tensor cores (tcgen05, TMEM accumulator).  M % 128 == 0,
+ * 16 <= N <= 256 with N % 16 == 0, K % 64 == 0.  The operand staging and MMA
+ * path of the prefill expert GEMM, exposed for direct checks.  No counterpart
+ * in the reference (its prefill matmuls run in Metal / MLX). */
+int kq_gemm_f16_tc(const void* A, const void* B, float* C, int M, int N, int K, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -74,6 +74,7 @@ SIGNATURES = {
     "kq_qmat_load_mlx": (c_int, [c_void_p, ctypes.POINTER(kq_mlx_matrix), ctypes.POINTER(kq_mlx_matrix),
                                  c_void_p]),
     "kq_qmat_unpack_mlx": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "kq_gemm_f16_tc": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "kq_dense_gemv": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_float, c_int, c_void_p, c_int,
                               c_void_p]),
 }
