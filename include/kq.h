@@ -201,6 +201,21 @@ int kq_moe_decode_static(const kq_table* t, int layer, const void* x, int x_dtyp
                          const float* logits, int32_t* idx, float* weights, int K, void* out_per_k,
                          void* out, int out_dtype, const void* residual, void* stream);
 
+/* Routed-expert MLP for many tokens (prefill), same arguments and outputs as
+ * kq_moe_decode.  The T*K assignments are grouped by expert (stable, token
+ * order inside an expert, as kandiga/engine.py:407-418) and every expert runs
+ * once over its tokens on the tensor cores (tcgen05): weights dequantised to
+ * fp16 in shared memory, the expert's tokens as the MMA's N dimension, fp32
+ * accumulators in tensor memory.  replaces _gpu_prefill_experts
+ * (kandiga/engine.py:386-516) and bakan_cpu_expert_mlp_prefill_f16
+ * (kandiga/metal/kandiga_cpu_expert.m:773-838).  Requires hidden and inter to
+ * be multiples of 512 and per-group |scale| < 64. */
+size_t kq_moe_prefill_workspace_size(const kq_table* t, int max_tokens, int top_k);
+int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x_dtype, int T,
+                   const float* logits, int32_t* idx, float* weights, int K, void* out_per_k,
+                   void* out, int out_dtype, const void* residual, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
 /* Read and clear the device status word of a workspace (synchronises `stream`). */
 int kq_status_read(void* workspace, uint32_t* status, void* stream);
 

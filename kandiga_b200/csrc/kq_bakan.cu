@@ -51,13 +51,25 @@ bool grow(void** p, size_t* have, size_t need) {
     return true;
 }
 
+// Many tokens go through the grouped tensor-core path (every expert once over
+// its tokens); one or a few tokens through the decode kernels.
+bool use_prefill(const Engine* e, int T) {
+    return T >= 16 && e->info.hidden % 512 == 0 && e->info.inter % 512 == 0;
+}
+
+size_t ws_need(const Engine* e, int T, int K) {
+    return use_prefill(e, T) ? kq_moe_prefill_workspace_size(e->table, T, K)
+                             : kq_moe_workspace_size(e->table, T, K);
+}
+
 bool ensure(Engine* e, int T, int K) {
     const int H = e->info.hidden;
     if (!grow(&e->dx, &e->dx_bytes, (size_t)T * H * 4)) return false;
     if (!grow(&e->dout, &e->dout_bytes, (size_t)T * K * H * 4)) return false;
     if (!grow(reinterpret_cast<void**>(&e->didx), &e->didx_bytes, (size_t)T * K * 4)) return false;
-    if (T > e->ws_tokens || e->ws_bytes < kq_moe_workspace_size(e->table, T, K)) {
-        size_t need = kq_moe_workspace_size(e->table, std::max(T, e->ws_tokens), kMaxExperts);
+    if (T > e->ws_tokens || e->ws_bytes < ws_need(e, T, K)) {
+        size_t need = std::max(ws_need(e, std::max(T, e->ws_tokens), kMaxExperts),
+                               kq_moe_workspace_size(e->table, std::max(T, e->ws_tokens), kMaxExperts));
         if (e->ws) cudaFree(e->ws);
         e->ws = nullptr;
         e->ws_bytes = 0;
@@ -107,8 +119,9 @@ int run(Engine* e, int layer, const void* x, int x_dtype, const int32_t* idx, in
         fprintf(stderr, "[kandiga] ERROR: host->device copy failed for layer %d\n", layer);
         return -1;
     }
-    int rc = kq_moe_decode(e->table, layer, e->dx, x_dtype, T, nullptr, e->didx, nullptr, K, e->dout,
-                           nullptr, out_dtype, nullptr, e->ws, e->ws_bytes, s);
+    int rc = (use_prefill(e, T) ? kq_moe_prefill : kq_moe_decode)(e->table, layer, e->dx, x_dtype, T, nullptr,
+                                                                 e->didx, nullptr, K, e->dout, nullptr, out_dtype,
+                                                                 nullptr, e->ws, e->ws_bytes, s);
     if (rc != KQ_OK) {
         fprintf(stderr, "[kandiga] ERROR: expert kernels failed for layer %d (code %d)\n", layer, rc);
         return -1;

@@ -54,10 +54,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait: returns false (and latches the timeout bit) if the phase never
-// completed within KQ_WAIT_LIMIT polls.
+// completed within KQ_WAIT_LIMIT polls.  Once any wait of the launch has timed
+// out (bit latched in *status), later waits return at once, so a stalled
+// pipeline drains in one wait limit instead of one per stage.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
-    for (uint32_t i = 0; i < KQ_WAIT_LIMIT; ++i)
+    for (uint32_t i = 0; i < KQ_WAIT_LIMIT; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 1023u) == 1023u && status &&
+            (*reinterpret_cast<volatile uint32_t*>(status) & KQ_DEV_WAIT_TIMEOUT))
+            return false;
+    }
     set_status(status, KQ_DEV_WAIT_TIMEOUT);
     return false;
 }

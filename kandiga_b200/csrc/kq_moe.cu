@@ -585,6 +585,11 @@ static cudaError_t launch_router(const float* logits, int T, int E, int K, int32
     return cudaLaunchKernelEx(&cfg, router_topk_kernel, logits, T, E, K, idx, w);
 }
 
+int launch_router_ext(const float* logits, int T, int E, int K, int32_t* idx, float* w, cudaStream_t s) {
+    if (E > 1024 || K > MAX_K) return KQ_ERR_UNSUPPORTED;
+    return launch_router(logits, T, E, K, idx, w, s) == cudaSuccess ? KQ_OK : KQ_ERR_CUDA;
+}
+
 MoeWs moe_ws_layout(const kq_table* t, int T, int K) {
     MoeWs L{};
     size_t o = 0;

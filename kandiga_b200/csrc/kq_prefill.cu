@@ -1,0 +1,705 @@
+// kq_prefill.cu -- grouped routed-expert MLP for many tokens (prefill) on tcgen05.
+//
+// The reference groups the T*K (token, slot) assignments by expert with a
+// stable sort and runs every expert once over its tokens
+// (kandiga/engine.py:407-418 grouping, :260-292 gate/up+SwiGLU and down
+// kernels; kandiga/metal/kandiga_cpu_expert.m:773-838 for the CPU path).  Here:
+//
+//   group_kernel         one CTA: tokens per expert, offsets, the position of
+//                        every assignment in expert-sorted order and the list
+//                        of live 128-token work chunks
+//   gather_kernel        x rows gathered into expert-sorted order as fp16
+//   moe_tc_kernel        grouped GEMM, once for gate/up (+SwiGLU) and once for
+//                        down.  Swap-AB: the MMA's M = 128 weight rows, N = the
+//                        expert's tokens (16..128 per chunk), K = input dim.
+//                        Warp-specialised and persistent (one CTA per SM):
+//                          warp 0     TMA: packed KQ tiles of the expert (bulk
+//                                     copies) and the tokens' 64-wide K chunks
+//                                     (2D tensor map, 128-byte swizzle)
+//                          warps 1-8  dequantise, two sets of four taking
+//                                     alternate 64-wide groups: thread = weight
+//                                     row; a group's words -> 32 exact fp16
+//                                     pairs -> W = q*s + b -> one swizzled
+//                                     128-byte row of an A stage
+//                          warp 9     one thread issues tcgen05.mma (M=128,
+//                                     N=tokens, K=16) into a TMEM accumulator
+//                                     (two buffers), commits free the stages
+//                          warps 10-13 epilogue: tcgen05.ld; gate/up rows sit
+//                                     8 lanes apart, act = silu(g)*u -> fp16
+//                                     in expert-sorted order; down -> fp32
+//   combine_kernel       out = [res] + sum_k w_k y_k, per-k outputs
+//                        (kandiga/metal/moe_block.metal:515-584)
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <cstring>
+
+#include "kq_internal.h"
+#include "kq_tc.cuh"
+
+namespace kq {
+
+// ---- grouping ----------------------------------------------------------------------------
+
+constexpr int GROUP_THREADS = 1024;
+constexpr int GROUP_MAX_E = 4096;  // experts per layer the one-CTA grouping supports
+
+// Grouping in one CTA (the T*K assignments of a prefill batch are a few
+// thousand ids; one CTA avoids grid-wide synchronisation):
+//   1. rank[a] = atomicAdd(&cnt[idx[a]], 1) in shared memory (kept in inv_pos)
+//   2. exclusive scans of cnt (offsets) and of ceil(cnt/128) (work chunks)
+//   3. pos = offset[e] + rank[a]; s_tok[pos] = a / K; inv_pos[a] = pos
+// The order of an expert's assignments inside its segment is unspecified; each
+// position is an independent MMA column, so results do not depend on it.
+// Ids outside [0, E) get inv_pos = -1 and latch KQ_DEV_BAD_EXPERT.
+__global__ void __launch_bounds__(GROUP_THREADS, 1)
+    group_kernel(const int32_t* __restrict__ idx, int A, int K, int E, int* __restrict__ count,
+                 int* __restrict__ offset, int32_t* __restrict__ s_tok, int32_t* __restrict__ inv_pos,
+                 int32_t* __restrict__ chunk_list, int* __restrict__ n_chunks, uint32_t* status) {
+    __shared__ int cnt[GROUP_MAX_E];
+    __shared__ int off_s[GROUP_MAX_E];
+    __shared__ int wsum[2][32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int e = tid; e < E; e += GROUP_THREADS) cnt[e] = 0;
+    __syncthreads();
+    for (int a = tid; a < A; a += GROUP_THREADS) {
+        const int v = idx[a];
+        if ((unsigned)v < (unsigned)E) {
+            inv_pos[a] = atomicAdd(&cnt[v], 1);
+        } else {
+            inv_pos[a] = -1;
+            set_status(status, KQ_DEV_BAD_EXPERT);
+        }
+    }
+    __syncthreads();
+    // thread t owns experts [t*per, t*per + per)
+    const int per = (E + GROUP_THREADS - 1) / GROUP_THREADS;
+    const int e0 = min(tid * per, E), e1 = min(e0 + per, E);
+    int n_loc = 0, c_loc = 0;
+    for (int e = e0; e < e1; ++e) {
+        n_loc += cnt[e];
+        c_loc += (cnt[e] + 127) >> 7;
+    }
+    int n_inc = n_loc, c_inc = c_loc;  // inclusive warp scans
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xffffffffu, n_inc, o), b = __shfl_up_sync(0xffffffffu, c_inc, o);
+        if (lane >= o) {
+            n_inc += a;
+            c_inc += b;
+        }
+    }
+    if (lane == 31) {
+        wsum[0][warp] = n_inc;
+        wsum[1][warp] = c_inc;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int a = wsum[0][lane], b = wsum[1][lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int x = __shfl_up_sync(0xffffffffu, a, o), y = __shfl_up_sync(0xffffffffu, b, o);
+            if (lane >= o) {
+                a += x;
+                b += y;
+            }
+        }
+        wsum[0][lane] = a;  // inclusive over warps
+        wsum[1][lane] = b;
+    }
+    __syncthreads();
+    int n_run = n_inc - n_loc + (warp ? wsum[0][warp - 1] : 0);
+    int c_run = c_inc - c_loc + (warp ? wsum[1][warp - 1] : 0);
+    for (int e = e0; e < e1; ++e) {
+        const int ne = cnt[e], nch = (ne + 127) >> 7;
+        off_s[e] = n_run;
+        offset[e] = n_run;
+        count[e] = ne;
+        for (int c = 0; c < nch; ++c) chunk_list[c_run + c] = (e << 16) | c;
+        n_run += ne;
+        c_run += nch;
+    }
+    if (tid == GROUP_THREADS - 1) *n_chunks = c_run;
+    __syncthreads();
+    for (int a = tid; a < A; a += GROUP_THREADS) {
+        const int r = inv_pos[a];  // written by this thread above
+        if (r < 0) continue;
+        const int pos = off_s[idx[a]] + r;
+        s_tok[pos] = a / K;
+        inv_pos[a] = pos;
+    }
+}
+
+// Xs[pos] = fp16(x[s_tok[pos]] * scale[tok]); one warp per position.  fp16
+// inputs are copied unscaled (xinv == nullptr); other types get a power-of-two
+// scale so every value fits fp16, and xinv[pos] = 1/scale.
+__global__ void gather_kernel(const void* __restrict__ x, int x_dtype, int H, const int32_t* __restrict__ s_tok,
+                              const int* __restrict__ count, const int* __restrict__ offset, int E,
+                              __half* __restrict__ Xs, float* __restrict__ xinv) {
+    const int pos = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (pos >= offset[E - 1] + count[E - 1]) return;  // only placed positions
+    const int tok = s_tok[pos];
+    const size_t src = (size_t)tok * H;
+    float scale = 1.f;
+    if (x_dtype != KQ_DT_F16) {
+        float amax = 0.f;
+        for (int c = lane; c < H / 8; c += 32) {
+            float v[8];
+            load8(x, x_dtype, src + (size_t)c * 8, false, v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(v[k]));
+        }
+        scale = pow2_scale(warp_max(amax));
+        if (lane == 0) xinv[pos] = 1.f / scale;
+    }
+    for (int c = lane; c < H / 8; c += 32) {
+        float v[8];
+        load8(x, x_dtype, src + (size_t)c * 8, false, v);
+        uint32_t h[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const __half2 hh = __floats2half2_rn(v[2 * k] * scale, v[2 * k + 1] * scale);
+            h[k] = *reinterpret_cast<const uint32_t*>(&hh);
+        }
+        *reinterpret_cast<uint4*>(Xs + (size_t)pos * H + (size_t)c * 8) = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+}
+
+// ---- grouped expert GEMM on tcgen05 ----------------------------------------------------------
+
+struct TcParams {
+    const uint8_t* base;  // layer base
+    size_t expert_bytes;
+    size_t mat_off;       // matrix offset inside an expert
+    int nst;              // 512-wide K super-tiles
+    int n_mt;             // 128-row M-tiles per expert
+    int E;
+    const int* count;
+    const int* offset;
+    const int32_t* chunk_list;  // live work chunks, (expert << 16) | chunk
+    const int* n_chunks;
+    int mode;             // 0: gate/up + activation -> act_s; 1: down -> ys
+    __half* act_s;        // [A][I]
+    int I;
+    float* ys;            // [A][H]
+    int H;
+    const float* xinv;    // [A] input scale inverse (gate/up), or null
+    int act_kind;
+    uint32_t* status;
+};
+
+constexpr int TC_NSTAGE = 4;          // A/B stages (one 64-wide group each)
+constexpr int TC_NKQ = 2;             // packed super-tile stages
+constexpr int TC_NDQ = 2;             // dequantising warp sets (4 warps each), alternating groups
+constexpr int TC_THREADS = 32 * (2 + 4 * TC_NDQ + 4);  // producer, MMA, dequant sets, epilogue
+constexpr int TC_STAGE_BYTES = 16384; // 128 rows x 128 B
+constexpr int TC_TMEM_COLS = 256;     // two 128-column accumulators
+
+// Packed tiles land in shared memory through a 2D tensor map that views the
+// layer as rows of 128 bytes with the 128-byte swizzle: byte (row, 16*slot + b)
+// of a tile sits at row*128 + 16*(slot ^ (row & 7)) + b.  A dequantising
+// quarter-warp (rows r16 = 0..7 of one tile, one 64-wide group) then reads
+// eight distinct 16-byte bank groups.  Tile slots are 1024-byte aligned.
+template <int BITS>
+__host__ __device__ constexpr int tc_tile_slot() {
+    return (TileT<BITS>::BYTES + 1023) / 1024 * 1024;
+}
+
+template <int BITS>
+__host__ __device__ constexpr size_t tc_smem_bytes() {
+    return 1024 + (size_t)TC_NSTAGE * TC_STAGE_BYTES * 2 + (size_t)TC_NKQ * 8 * tc_tile_slot<BITS>() + 256;
+}
+
+// 16-byte unit `lane` of 512-byte chunk `chunk` of a swizzled tile
+__device__ __forceinline__ uint4 tile_u4(const uint8_t* tile, int chunk, int lane) {
+    const int row = chunk * 4 + (lane >> 3);
+    return *reinterpret_cast<const uint4*>(tile + row * 128 + (((lane & 7) ^ (row & 7)) << 4));
+}
+
+template <int SB_DT>
+__device__ __forceinline__ __half to_half16(uint32_t v16) {
+    if (SB_DT == KQ_DT_F16) return __ushort_as_half((unsigned short)v16);
+    return __float2half_rn(__uint_as_float(v16 << 16));
+}
+
+// Dequantise row r16 (0..15) x group g (0..7) of a KQ tile into 64 fp16 weights
+// W = q*s + b, written as one 128-byte row (row m) of a swizzled A stage.
+template <int BITS, int SB_DT, int J>
+__device__ __forceinline__ void dq_pairs(const uint32_t* wd, const uint32_t* sh, __half2 s2, __half2 b2,
+                                         __half2 c1024, __half2 c_mid, __half2 c_lo, uint32_t* out) {
+    if constexpr (J < 32) {
+        const uint32_t h = pair_of<BITS, J>(wd, sh);
+        const float off = pair_offset<BITS>(J);
+        const __half2 c = off == 1024.f ? c1024 : (off == 16.f ? c_lo : c_mid);
+        __half2 w2 = __hfma2(*reinterpret_cast<const __half2*>(&h), s2, c);  // (2^(10-k) + q) s - 2^(10-k) s
+        w2 = __hadd2(w2, b2);
+        out[J] = *reinterpret_cast<const uint32_t*>(&w2);
+        dq_pairs<BITS, SB_DT, J + 1>(wd, sh, s2, b2, c1024, c_mid, c_lo, out);
+    }
+}
+
+template <int BITS, int SB_DT>
+__device__ __forceinline__ void dequant_row(const uint8_t* tile, int r16, int g, uint8_t* a_stage, int m) {
+    constexpr int W = TileT<BITS>::W;  // words per (lane, set); the scale/bias chunk is chunk W
+    const int l = 4 * (r16 & 7) + (g & 3);
+    const int set = 2 * (r16 >> 3) + (g >> 2);
+    const int q0 = set * W;  // first word of the set; q0 % 4 is 0 (4-bit) or 0/2 (3-bit)
+    const uint4 u0 = tile_u4(tile, q0 >> 2, l), u1 = tile_u4(tile, (q0 >> 2) + 1, l);
+    const uint32_t arr[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    const bool odd = (q0 & 3) != 0;
+    uint32_t wd[W], sh[W];
+#pragma unroll
+    for (int w = 0; w < W; ++w) wd[w] = (W == 8 || !odd) ? arr[w] : arr[(w + 2) & 7];
+#pragma unroll
+    for (int w = 0; w < W; ++w) sh[w] = wd[w] >> (BITS == 3 ? 9 : 8);
+    const int l2 = 4 * (r16 & 7) + (g >> 1), kk = 2 * (r16 >> 3) + (g & 1);
+    const int srow = W * 4 + (l2 >> 3);
+    const uint32_t sbw =
+        *reinterpret_cast<const uint32_t*>(tile + srow * 128 + (((l2 & 7) ^ (srow & 7)) << 4) + kk * 4);
+    const __half s = to_half16<SB_DT>(sbw & 0xFFFFu), b = to_half16<SB_DT>(sbw >> 16);
+    const __half2 s2 = __halves2half2(s, s), b2 = __halves2half2(b, b);
+    // -2^(10-k) * s is exact in fp16 (power-of-two multiple) for |s| < 64
+    const __half2 c1024 = __hmul2(s2, __float2half2_rn(-1024.f));
+    const __half2 c_mid = __hmul2(s2, __float2half2_rn(BITS == 3 ? -128.f : -64.f));
+    const __half2 c_lo = __hmul2(s2, __float2half2_rn(-16.f));
+    uint32_t out[32];
+    dq_pairs<BITS, SB_DT, 0>(wd, sh, s2, b2, c1024, c_mid, c_lo, out);
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(a_stage + tc::sw128_offset(m, c * 8)) =
+            make_uint4(out[4 * c], out[4 * c + 1], out[4 * c + 2], out[4 * c + 3]);
+}
+
+struct TcItem {
+    int e, nc, mt, n, box, pos0;
+};
+
+// item = chunk * n_mt + mt over the live chunks only
+__device__ __forceinline__ TcItem tc_item(const TcParams& p, int item) {
+    TcItem it;
+    const int32_t ch = p.chunk_list[item / p.n_mt];
+    it.mt = item % p.n_mt;
+    it.e = ch >> 16;
+    it.nc = ch & 0xFFFF;
+    const int ne = p.count[it.e];
+    it.n = min(128, ne - it.nc * 128);
+    it.box = it.n <= 16 ? 16 : (it.n <= 32 ? 32 : (it.n <= 64 ? 64 : 128));
+    it.pos0 = p.offset[it.e] + it.nc * 128;
+    return it;
+}
+
+template <int BITS, int SB_DT>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    moe_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap tb16, const __grid_constant__ CUtensorMap tb32,
+                  const __grid_constant__ CUtensorMap tb64, const __grid_constant__ CUtensorMap tb128,
+                  const __grid_constant__ CUtensorMap tkq) {
+    extern __shared__ uint8_t smem_raw[];
+    constexpr int TB = TileT<BITS>::BYTES;
+    constexpr int TS = tc_tile_slot<BITS>();
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = sm;
+    uint8_t* sB = sA + TC_NSTAGE * TC_STAGE_BYTES;
+    uint8_t* sK = sB + TC_NSTAGE * TC_STAGE_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sK + TC_NKQ * 8 * TS);
+    uint64_t* kq_full = bars;       // [2]
+    uint64_t* kq_empty = bars + 2;  // [2]
+    uint64_t* a_full = bars + 4;    // [4]
+    uint64_t* b_full = bars + 8;    // [4]
+    uint64_t* ab_empty = bars + 12; // [4]
+    uint64_t* d_full = bars + 16;   // [2]
+    uint64_t* d_empty = bars + 18;  // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (tid == 0) {
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&kq_full[i], 1);
+            mbar_init(&kq_empty[i], 128 * TC_NDQ);
+            mbar_init(&d_full[i], 1);
+            mbar_init(&d_empty[i], 128);
+        }
+        for (int i = 0; i < TC_NSTAGE; ++i) {
+            mbar_init(&a_full[i], 128);
+            mbar_init(&b_full[i], 1);
+            mbar_init(&ab_empty[i], 1);
+        }
+        fence_mbar_init();
+    }
+    constexpr int MMA_WARP = 1 + 4 * TC_NDQ;
+    if (warp == MMA_WARP) {
+        tc::tmem_alloc(tmem_slot, TC_TMEM_COLS);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    const int n_items = *p.n_chunks * p.n_mt;
+    const int groups = p.nst * 8;
+
+    if (warp == 0) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            uint32_t kc = 0, gc = 0;
+            for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+                const TcItem it = tc_item(p, item);
+                const void* tm = it.box == 16 ? (const void*)&tb16
+                                              : (it.box == 32 ? (const void*)&tb32
+                                                              : (it.box == 64 ? (const void*)&tb64 : (const void*)&tb128));
+                const size_t ebase = (size_t)it.e * p.expert_bytes + p.mat_off;  // bytes into the layer
+                for (int st = 0; st < p.nst; ++st, ++kc) {
+                    const int s = kc & 1;
+                    mbar_wait(&kq_empty[s], ((kc >> 1) & 1) ^ 1, p.status);
+                    mbar_expect_tx(&kq_full[s], 8 * TB);
+                    for (int j = 0; j < 8; ++j) {
+                        const int rt = it.mt * 8 + j;
+                        const size_t off = ebase + ((size_t)rt * p.nst + st) * TB;  // multiple of 128
+                        tc::tma_load_2d(sK + ((size_t)s * 8 + j) * TS, &tkq, 0, (int)(off >> 7), &kq_full[s]);
+                    }
+                    for (int g = 0; g < 8; ++g, ++gc) {
+                        const int gs = gc % TC_NSTAGE;
+                        mbar_wait(&ab_empty[gs], ((gc / TC_NSTAGE) & 1) ^ 1, p.status);
+                        mbar_expect_tx(&b_full[gs], (uint32_t)it.box * 128);
+                        tc::tma_load_2d(sB + (size_t)gs * TC_STAGE_BYTES, tm, (st * 8 + g) * 64, it.pos0, &b_full[gs]);
+                    }
+                }
+            }
+        }
+    } else if (warp >= 1 && warp < MMA_WARP) {
+        // ---------------- dequantise (set `ds` takes groups gc % TC_NDQ == ds) ----------------
+        const int ds = (warp - 1) >> 2;
+        const int m = (tid - 32) & 127;  // A row 0..127
+        const int jt = m >> 4, r16 = m & 15;
+        uint32_t kc = 0, gc = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+            const TcItem it = tc_item(p, item);
+            for (int st = 0; st < p.nst; ++st, ++kc) {
+                const int s = kc & 1;
+                mbar_wait(&kq_full[s], (kc >> 1) & 1, p.status);
+                const uint8_t* tile = sK + ((size_t)s * 8 + jt) * TS;
+                for (int g = 0; g < 8; ++g, ++gc) {
+                    if ((int)(gc % TC_NDQ) != ds) continue;
+                    const int gs = gc % TC_NSTAGE;
+                    mbar_wait(&ab_empty[gs], ((gc / TC_NSTAGE) & 1) ^ 1, p.status);
+                    dequant_row<BITS, SB_DT>(tile, r16, g, sA + (size_t)gs * TC_STAGE_BYTES, m);
+                    fence_proxy_async_smem();
+                    tc::mbar_arrive(&a_full[gs]);
+                }
+                tc::mbar_arrive(&kq_empty[s]);
+            }
+        }
+    } else if (warp == MMA_WARP) {
+        // ---------------- MMA issue ----------------
+        if (lane == 0) {
+            uint32_t gc = 0, ic = 0;
+            for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+                const TcItem it = tc_item(p, item);
+                const int db = ic & 1;
+                mbar_wait(&d_empty[db], ((ic >> 1) & 1) ^ 1, p.status);
+                tc::fence_after_sync();
+                const uint32_t d_tmem = tmem + (uint32_t)(db * 128);
+                const uint32_t idesc = tc::idesc_f16(128, it.box, false);
+                for (int gi = 0; gi < groups; ++gi, ++gc) {
+                    const int gs = gc % TC_NSTAGE;
+                    const uint32_t ph = (gc / TC_NSTAGE) & 1;
+                    mbar_wait(&a_full[gs], ph, p.status);
+                    mbar_wait(&b_full[gs], ph, p.status);
+                    tc::fence_after_sync();
+                    const uint64_t da = tc::smem_desc_sw128(sA + (size_t)gs * TC_STAGE_BYTES);
+                    const uint64_t dbd = tc::smem_desc_sw128(sB + (size_t)gs * TC_STAGE_BYTES);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        tc::mma_f16_ss(d_tmem, tc::desc_advance(da, 32 * k), tc::desc_advance(dbd, 32 * k), idesc,
+                                       gi > 0 || k > 0);
+                    tc::mma_commit(&ab_empty[gs]);
+                }
+                tc::mma_commit(&d_full[db]);
+                ++ic;
+            }
+        }
+    } else {
+        // ---------------- epilogue (last four warps) ----------------
+        const int q = warp & 3;         // TMEM lane quarter this warp may access
+        const int L = q * 32 + lane;    // accumulator row
+        uint32_t ic = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+            const TcItem it = tc_item(p, item);
+            const int db = ic & 1;
+            mbar_wait(&d_full[db], (ic >> 1) & 1, p.status);
+            tc::fence_after_sync();
+            const uint32_t taddr = tmem + (uint32_t)(db * 128) + ((uint32_t)(q * 32) << 16);
+            for (int c0 = 0; c0 < it.box; c0 += 16) {
+                uint32_t r[16];
+                tc::tmem_ld16(taddr + (uint32_t)c0, r);
+                tc::tmem_ld_wait();
+                if (p.mode == 0) {
+                    const int jt = L >> 4, r16 = L & 15;
+                    const int irow = it.mt * 64 + jt * 8 + (r16 & 7);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float v = __uint_as_float(r[i]);
+                        const float u = __shfl_down_sync(0xffffffffu, v, 8);  // up row sits 8 lanes below
+                        const int n = c0 + i;
+                        if (r16 < 8 && n < it.n) {
+                            const float xi = p.xinv ? p.xinv[it.pos0 + n] : 1.f;
+                            const float a = activate(v * xi, u * xi, p.act_kind);
+                            p.act_s[(size_t)(it.pos0 + n) * p.I + irow] = __float2half_rn(a);
+                        }
+                    }
+                } else {
+                    const int hrow = it.mt * 128 + L;
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int n = c0 + i;
+                        if (n < it.n) p.ys[(size_t)(it.pos0 + n) * p.H + hrow] = __uint_as_float(r[i]);
+                    }
+                }
+            }
+            tc::fence_before_sync();
+            tc::mbar_arrive(&d_empty[db]);
+            ++ic;
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == MMA_WARP) tc::tmem_dealloc(tmem, TC_TMEM_COLS);
+}
+
+// ---- combine ----------------------------------------------------------------------------------
+
+// out[t][h] = [res[t][h]] + sum_k w[t][k] * ys[pos(t,k)][h]; per-k outputs optional.
+__global__ void combine_kernel(const float* __restrict__ ys, const int32_t* __restrict__ inv_pos,
+                               const float* __restrict__ w, int T, int K, int H, void* out, void* out_per_k,
+                               int out_dtype, const void* residual) {
+    const int t = blockIdx.y;
+    const int h = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T || h >= H) return;
+    float acc = 0.f;
+    for (int k = 0; k < K; ++k) {
+        const int pos = inv_pos[(size_t)t * K + k];
+        const float y = pos >= 0 ? ys[(size_t)pos * H + h] : 0.f;
+        if (out_per_k) store_from_float(out_per_k, out_dtype, ((size_t)t * K + k) * H + h, y);
+        if (out) acc += y * w[(size_t)t * K + k];
+    }
+    if (!out) return;
+    if (residual) acc = load_as_float(residual, out_dtype, (size_t)t * H + h) + acc;
+    store_from_float(out, out_dtype, (size_t)t * H + h, acc);
+}
+
+// ---- host ---------------------------------------------------------------------------------------
+
+struct PrefillWs {
+    size_t status, idx, w, count, offset, chunks, n_chunks, s_tok, inv_pos, xinv, Xs, act_s, ys, total;
+};
+
+static PrefillWs prefill_ws_layout(const kq_table* t, int T, int K) {
+    auto al = [](size_t v) { return (v + 255) / 256 * 256; };
+    const size_t A = (size_t)T * K;
+    PrefillWs L{};
+    size_t o = 0;
+    L.status = o;
+    o += 256;
+    L.idx = o;
+    o = al(o + A * 4);
+    L.w = o;
+    o = al(o + A * 4);
+    L.count = o;
+    o = al(o + (size_t)t->d.num_experts * 4);
+    L.offset = o;
+    o = al(o + (size_t)t->d.num_experts * 4);
+    L.chunks = o;  // at most E + A/128 live chunks
+    o = al(o + ((size_t)t->d.num_experts + A / 128 + 1) * 4);
+    L.n_chunks = o;
+    o = al(o + 4);
+    L.s_tok = o;
+    o = al(o + A * 4);
+    L.inv_pos = o;
+    o = al(o + A * 4);
+    L.xinv = o;
+    o = al(o + A * 4);
+    L.Xs = o;
+    o = al(o + A * t->d.hidden * 2);
+    L.act_s = o;
+    o = al(o + A * t->d.inter * 2);
+    L.ys = o;
+    o = al(o + A * t->d.hidden * 4);
+    L.total = o;
+    return L;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// fp16 row-major [rows][cols] tensor, 64 x box_rows boxes, 128-byte swizzle
+static bool make_tmap(CUtensorMap* m, const void* base, int rows, int cols, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// the layer's packed bytes as [rows][128] uint8, boxes of one tile (tile_bytes / 128 rows), 128-byte swizzle
+static bool make_kq_tmap(CUtensorMap* m, const void* layer, size_t layer_bytes, int tile_bytes) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {128, (cuuint64_t)(layer_bytes / 128)};
+    cuuint64_t strides[1] = {128};
+    cuuint32_t box[2] = {128, (cuuint32_t)(tile_bytes / 128)};
+    cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(layer), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BITS, int SB_DT>
+static cudaError_t launch_tc_t(const TcParams& p, const CUtensorMap (&tm)[4], const CUtensorMap& tkq, cudaStream_t s,
+                               int grid) {
+    static int configured[64] = {0};
+    auto kern = moe_tc_kernel<BITS, SB_DT>;
+    const size_t smem = tc_smem_bytes<BITS>();
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if ((size_t)configured[dev] < smem) {
+        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (err != cudaSuccess) return err;
+        configured[dev] = (int)smem;
+    }
+    kern<<<grid, TC_THREADS, smem, s>>>(p, tm[0], tm[1], tm[2], tm[3], tkq);
+    return cudaGetLastError();
+}
+
+static cudaError_t launch_tc(int bits, int sb, const TcParams& p, const CUtensorMap (&tm)[4], const CUtensorMap& tkq,
+                             cudaStream_t s, int grid) {
+    if (bits == 3)
+        return sb == KQ_DT_F16 ? launch_tc_t<3, KQ_DT_F16>(p, tm, tkq, s, grid)
+                               : launch_tc_t<3, KQ_DT_BF16>(p, tm, tkq, s, grid);
+    return sb == KQ_DT_F16 ? launch_tc_t<4, KQ_DT_F16>(p, tm, tkq, s, grid)
+                           : launch_tc_t<4, KQ_DT_BF16>(p, tm, tkq, s, grid);
+}
+
+int launch_router_ext(const float* logits, int T, int E, int K, int32_t* idx, float* w, cudaStream_t s);
+
+}  // namespace kq
+
+using namespace kq;
+
+extern "C" size_t kq_moe_prefill_workspace_size(const kq_table* t, int max_tokens, int top_k) {
+    if (!t || max_tokens < 0 || top_k <= 0) return 0;
+    return prefill_ws_layout(t, max_tokens, top_k).total;
+}
+
+extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x_dtype, int T, const float* logits,
+                              int32_t* idx, float* weights, int K, void* out_per_k, void* out, int out_dtype,
+                              const void* residual, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!t) return KQ_ERR_ARG;
+    if (layer < 0 || layer >= t->d.num_layers) return KQ_ERR_ARG;
+    if (T < 0 || K <= 0 || K > 32 || K > t->d.num_experts) return KQ_ERR_ARG;
+    if (T == 0) return KQ_OK;
+    if (!x || (x_dtype != KQ_DT_F16 && x_dtype != KQ_DT_BF16 && x_dtype != KQ_DT_F32)) return KQ_ERR_ARG;
+    if (out_dtype != KQ_DT_F16 && out_dtype != KQ_DT_BF16 && out_dtype != KQ_DT_F32) return KQ_ERR_ARG;
+    if (!logits && !idx) return KQ_ERR_ARG;
+    if (out && !weights && !logits) return KQ_ERR_ARG;
+    if (!out && !out_per_k) return KQ_ERR_ARG;
+    if (logits && t->d.num_experts > 1024) return KQ_ERR_UNSUPPORTED;
+    if (t->d.num_experts > GROUP_MAX_E) return KQ_ERR_UNSUPPORTED;
+    if (t->d.hidden % 512 || t->d.inter % 512) return KQ_ERR_UNSUPPORTED;  // whole 512-wide super-tiles
+    if (!workspace) return KQ_ERR_WORKSPACE;
+    const PrefillWs L = prefill_ws_layout(t, T, K);
+    if (workspace_bytes < L.total) return KQ_ERR_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int A = T * K, E = t->d.num_experts, H = t->d.hidden, I = t->d.inter;
+    int32_t* idx_use = idx ? idx : reinterpret_cast<int32_t*>(ws + L.idx);
+    float* w_use = weights ? weights : reinterpret_cast<float*>(ws + L.w);
+    uint32_t* status = reinterpret_cast<uint32_t*>(ws + L.status);
+    int* count = reinterpret_cast<int*>(ws + L.count);
+    int* offset = reinterpret_cast<int*>(ws + L.offset);
+    int32_t* chunk_list = reinterpret_cast<int32_t*>(ws + L.chunks);
+    int* n_chunks = reinterpret_cast<int*>(ws + L.n_chunks);
+    int32_t* s_tok = reinterpret_cast<int32_t*>(ws + L.s_tok);
+    int32_t* inv_pos = reinterpret_cast<int32_t*>(ws + L.inv_pos);
+    float* xinv = reinterpret_cast<float*>(ws + L.xinv);
+    __half* Xs = reinterpret_cast<__half*>(ws + L.Xs);
+    __half* act_s = reinterpret_cast<__half*>(ws + L.act_s);
+    float* ys = reinterpret_cast<float*>(ws + L.ys);
+
+    if (logits && launch_router_ext(logits, T, E, K, idx_use, w_use, s) != KQ_OK) return KQ_ERR_CUDA;
+    {
+        const int threads = 256;
+        group_kernel<<<1, GROUP_THREADS, 0, s>>>(idx_use, A, K, E, count, offset, s_tok, inv_pos, chunk_list,
+                                                 n_chunks, status);
+        gather_kernel<<<(A * 32 + threads - 1) / threads, threads, 0, s>>>(x, x_dtype, H, s_tok, count, offset, E,
+                                                                             Xs, xinv);
+        if (cudaGetLastError() != cudaSuccess) return KQ_ERR_CUDA;
+    }
+    // Rows of Xs / act_s past the assigned positions are never written; the
+    // epilogues ignore the MMA columns that read them.
+    int nsm = 148;
+    {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    }
+    CUtensorMap tx[4], ta[4];
+    const int boxes[4] = {16, 32, 64, 128};
+    for (int i = 0; i < 4; ++i) {
+        if (!make_tmap(&tx[i], Xs, A, H, boxes[i]) || !make_tmap(&ta[i], act_s, A, I, boxes[i])) return KQ_ERR_CUDA;
+    }
+    CUtensorMap tkq;
+    const uint8_t* layer_base = t->base + (size_t)layer * t->layer_bytes;
+    if ((reinterpret_cast<uintptr_t>(layer_base) & 127) || (t->layer_bytes & 127) || (t->expert_bytes & 127) ||
+        (t->gateup_bytes & 127) || (t->tb & 127))
+        return KQ_ERR_UNSUPPORTED;  // tiles must start on 128-byte rows
+    if (!make_kq_tmap(&tkq, layer_base, t->layer_bytes, (int)t->tb)) return KQ_ERR_CUDA;
+    // live chunks: sum over experts of ceil(n_e / 128) <= E + A / 128
+    const int max_chunks = E + A / 128;
+    TcParams p{};
+    p.base = layer_base;
+    p.expert_bytes = t->expert_bytes;
+    p.E = E;
+    p.count = count;
+    p.offset = offset;
+    p.chunk_list = chunk_list;
+    p.n_chunks = n_chunks;
+    p.act_s = act_s;
+    p.I = I;
+    p.ys = ys;
+    p.H = H;
+    p.xinv = x_dtype == KQ_DT_F16 ? nullptr : xinv;
+    p.act_kind = t->d.activation;
+    p.status = status;
+    // gate/up + activation
+    p.mode = 0;
+    p.mat_off = 0;
+    p.nst = H / 512;
+    p.n_mt = I / 64;
+    int items = max_chunks * p.n_mt;  // upper bound; the kernel reads the live count
+    if (launch_tc(t->d.bits, t->d.sb_dtype, p, tx, tkq, s, std::min(items, nsm)) != cudaSuccess) return KQ_ERR_CUDA;
+    // down
+    p.mode = 1;
+    p.mat_off = t->gateup_bytes;
+    p.nst = I / 512;
+    p.n_mt = H / 128;
+    items = max_chunks * p.n_mt;
+    if (launch_tc(t->d.bits, t->d.sb_dtype, p, ta, tkq, s, std::min(items, nsm)) != cudaSuccess) return KQ_ERR_CUDA;
+    // combine / per-k outputs
+    dim3 grid((H + 255) / 256, T);
+    combine_kernel<<<grid, 256, 0, s>>>(ys, inv_pos, w_use, T, K, H, out, out_per_k, out_dtype, residual);
+    return cudaGetLastError() == cudaSuccess ? KQ_OK : KQ_ERR_CUDA;
+}

@@ -107,8 +107,9 @@ class ExpertTable:
                                              _stream()), "kq_table_unpack_mlx")
         return w.reshape(rows, -1), s.reshape(rows, -1), b.reshape(rows, -1)
 
-    def workspace(self, T, K):
-        need = int(self.lib.kq_moe_workspace_size(self.handle, T, K))
+    def workspace(self, T, K, prefill=False):
+        fn = self.lib.kq_moe_prefill_workspace_size if prefill else self.lib.kq_moe_workspace_size
+        need = int(fn(self.handle, T, K))
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.zeros(max(need, 1), dtype=torch.uint8, device="cuda")
         return self._ws
@@ -120,14 +121,18 @@ class ExpertTable:
         N.check(self.lib.kq_status_read(_ptr(self._ws), ctypes.byref(st), _stream()), "kq_status_read")
         return st.value
 
+    # token count from which the grouped tensor-core path (kq_moe_prefill) is used
+    PREFILL_MIN_TOKENS = 16
+
     def moe(self, layer, x, *, logits=None, idx=None, weights=None, top_k=8, per_k=False, combine=True,
-            residual=None, out_dtype=None, out=None, out_per_k=None):
+            residual=None, out_dtype=None, out=None, out_per_k=None, path="auto"):
         """Routed MLP of layer `layer` for x [T, H] (fp16/bf16/fp32 CUDA tensor).
 
         Routing: pass `logits` [T, E] fp32 (router top-K runs on the GPU and
         idx/weights are returned), or `idx` [T, K] int32 (+ `weights` [T, K]
-        fp32 when combining).  Returns dict(out=[T, H] or None,
-        per_k=[T, K, H] or None, idx, weights)."""
+        fp32 when combining).  path: "decode" (every (token, k) pair runs its
+        expert), "prefill" (grouped by expert on the tensor cores) or "auto".
+        Returns dict(out=[T, H] or None, per_k=[T, K, H] or None, idx, weights)."""
         T = x.shape[0]
         K = idx.shape[1] if idx is not None else top_k
         out_dtype = out_dtype or (x.dtype if x.dtype != torch.float32 else torch.float32)
@@ -143,12 +148,15 @@ class ExpertTable:
             out_per_k = torch.empty(T, K, self.hidden, dtype=out_dtype, device=dev)
         if residual is not None and (residual.dtype != out_dtype or residual.shape != (T, self.hidden)):
             raise ValueError("residual must be [T, hidden] in out_dtype")
-        ws = self.workspace(T, K)
-        rc = self.lib.kq_moe_decode(self.handle, layer, _ptr(x), _DT[x.dtype], T, _ptr(logits), _ptr(idx),
-                                    _ptr(weights), K, _ptr(out_per_k) if per_k else None,
-                                    _ptr(out) if combine else None, _DT[out_dtype], _ptr(residual),
-                                    _ptr(ws), ws.numel(), _stream())
-        N.check(rc, "kq_moe_decode")
+        if path == "auto":
+            path = "prefill" if (T >= self.PREFILL_MIN_TOKENS and self.hidden % 512 == 0 and
+                                 self.inter % 512 == 0) else "decode"
+        ws = self.workspace(T, K, prefill=(path == "prefill"))
+        fn = self.lib.kq_moe_prefill if path == "prefill" else self.lib.kq_moe_decode
+        rc = fn(self.handle, layer, _ptr(x), _DT[x.dtype], T, _ptr(logits), _ptr(idx), _ptr(weights), K,
+                _ptr(out_per_k) if per_k else None, _ptr(out) if combine else None, _DT[out_dtype],
+                _ptr(residual), _ptr(ws), ws.numel(), _stream())
+        N.check(rc, f"kq_moe_{path}")
         return dict(out=out if combine else None, per_k=out_per_k if per_k else None, idx=idx,
                     weights=weights)
 

@@ -1,0 +1,121 @@
+"""GPU parity of the grouped tensor-core prefill path (kq_moe_prefill) against
+the C oracle of the reference's expert MLP.  Tolerance: 2e-3 relative L2 per
+(token, k) expert output and per combined token row."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests.test_decode_gpu import get_layer, make_table, rel_l2
+
+pytestmark = pytest.mark.gpu
+RTOL_L2 = 2e-3
+
+
+def check(layer, t, x, idx, w, r, res=None):
+    y = layer.moe(x.float().cpu().numpy(), idx)
+    if r["per_k"] is not None:
+        pk = r["per_k"].float().cpu().numpy()
+        worst = max(rel_l2(pk[i, k], y[i, k]) for i in range(idx.shape[0]) for k in range(idx.shape[1]))
+        assert worst < RTOL_L2, worst
+    if r["out"] is not None:
+        want = O.combine(y, w, None if res is None else res.float().cpu().numpy())
+        got = r["out"].float().cpu().numpy()
+        worst = max(rel_l2(got[i], want[i]) for i in range(idx.shape[0]))
+        assert worst < RTOL_L2, worst
+
+
+@pytest.mark.parametrize("bits,sb", [(4, "f16"), (3, "f16"), (4, "bf16"), (3, "bf16")])
+def test_prefill_matches_oracle(gpu, bits, sb):
+    E, H, I, K, T = 16, 2048, 512, 8, 96
+    layer = get_layer(bits, H, I, E, sb, seed=20 + bits)
+    t = make_table(layer)
+    rng = np.random.RandomState(bits)
+    x = torch.from_numpy(rng.randn(T, H).astype(np.float16)).cuda()
+    logits = torch.from_numpy(rng.randn(T, E).astype(np.float32)).cuda()
+    r = t.moe(0, x, logits=logits, top_k=K, per_k=True, combine=True, out_dtype=torch.float32, path="prefill")
+    idx_ref, w_ref = O.router_topk(logits.cpu().numpy(), K)
+    assert np.array_equal(r["idx"].cpu().numpy(), idx_ref)
+    check(layer, t, x, idx_ref, r["weights"].cpu().numpy(), r)
+    assert t.status() == 0
+
+
+def test_prefill_skewed_chunks_and_residual(gpu):
+    """one expert receives every token (N-chunks of 128 + a ragged tail), others few."""
+    E, H, I, K, T = 8, 1024, 1024, 2, 300
+    layer = get_layer(4, H, I, E, "f16", seed=31)
+    t = make_table(layer)
+    rng = np.random.RandomState(4)
+    x = torch.from_numpy(rng.randn(T, H).astype(np.float16)).cuda()
+    idx = np.zeros((T, K), np.int32)
+    idx[:, 0] = 3
+    idx[:, 1] = rng.randint(0, E, T)
+    idx[idx[:, 1] == 3, 1] = 5
+    w = rng.rand(T, K).astype(np.float32)
+    res = torch.from_numpy(rng.randn(T, H).astype(np.float32)).cuda()
+    r = t.moe(0, x, idx=torch.from_numpy(idx).cuda(), weights=torch.from_numpy(w).cuda(), per_k=True, combine=True,
+              residual=res, out_dtype=torch.float32, path="prefill")
+    check(layer, t, x, idx, w, r, res)
+
+
+@pytest.mark.parametrize("xdt", [torch.bfloat16, torch.float32])
+def test_prefill_input_dtypes(gpu, xdt):
+    E, H, I, K, T = 16, 2048, 512, 4, 40
+    layer = get_layer(3, H, I, E, "f16", seed=9)
+    t = make_table(layer)
+    rng = np.random.RandomState(6)
+    x = torch.from_numpy(rng.randn(T, H).astype(np.float32) * 30).to(xdt).cuda()
+    logits = torch.from_numpy(rng.randn(T, E).astype(np.float32)).cuda()
+    r = t.moe(0, x, logits=logits, top_k=K, per_k=True, combine=True, out_dtype=torch.float32, path="prefill")
+    idx = r["idx"].cpu().numpy()
+    check(layer, t, x, idx, r["weights"].cpu().numpy(), r)
+
+
+def test_prefill_matches_decode_path(gpu):
+    E, H, I, K, T = 32, 2048, 512, 8, 64
+    layer = get_layer(3, H, I, E, "f16", seed=2)
+    t = make_table(layer)
+    rng = np.random.RandomState(10)
+    x = torch.from_numpy(rng.randn(T, H).astype(np.float16)).cuda()
+    logits = torch.from_numpy(rng.randn(T, E).astype(np.float32)).cuda()
+    a = t.moe(0, x, logits=logits, top_k=K, combine=True, out_dtype=torch.float32, path="prefill")["out"]
+    b = t.moe(0, x, logits=logits, top_k=K, combine=True, out_dtype=torch.float32, path="decode")["out"]
+    assert rel_l2(a.cpu().numpy(), b.cpu().numpy()) < RTOL_L2
+
+
+def test_prefill_bad_expert(gpu):
+    from kandiga_b200 import _native as N
+    E, H, I, K, T = 8, 1024, 512, 2, 20
+    layer = get_layer(4, H, I, E, "f16", seed=7)
+    t = make_table(layer)
+    x = torch.randn(T, H, device="cuda").half()
+    idx = torch.randint(0, E, (T, K), device="cuda", dtype=torch.int32)
+    idx[3, 1] = 77
+    r = t.moe(0, x, idx=idx, per_k=True, combine=False, out_dtype=torch.float32, path="prefill")
+    assert t.status() & N.DEV_BAD_EXPERT
+    assert torch.count_nonzero(r["per_k"][3, 1]) == 0
+
+
+def test_prefill_large_batch_bitwise_repeatable(gpu):
+    """T*K = 8192 assignments (several grouping rounds, ~128 tokens per expert):
+    prefill agrees with the decode path and with the oracle on sampled tokens,
+    and two runs give identical bits although the order of an expert's tokens
+    inside its segment may differ between runs."""
+    E, H, I, K, T = 64, 1024, 512, 8, 1024
+    layer = get_layer(4, H, I, E, "f16", seed=12)
+    t = make_table(layer)
+    rng = np.random.RandomState(12)
+    x = torch.from_numpy(rng.randn(T, H).astype(np.float16)).cuda()
+    logits = torch.from_numpy(rng.randn(T, E).astype(np.float32)).cuda()
+    a = t.moe(0, x, logits=logits, top_k=K, per_k=True, combine=True, out_dtype=torch.float32, path="prefill")
+    b = t.moe(0, x, logits=logits, top_k=K, per_k=True, combine=True, out_dtype=torch.float32, path="prefill")
+    assert torch.equal(a["out"], b["out"]) and torch.equal(a["per_k"], b["per_k"])
+    d = t.moe(0, x, logits=logits, top_k=K, combine=True, out_dtype=torch.float32, path="decode")["out"]
+    assert rel_l2(a["out"].cpu().numpy(), d.cpu().numpy()) < RTOL_L2
+    rows = [0, 1, 511, 1023]
+    idx = a["idx"].cpu().numpy()[rows]
+    y = layer.moe(x.float().cpu().numpy()[rows], idx)
+    pk = a["per_k"].float().cpu().numpy()[rows]
+    worst = max(rel_l2(pk[i, k], y[i, k]) for i in range(len(rows)) for k in range(K))
+    assert worst < RTOL_L2, worst
+    assert t.status() == 0
