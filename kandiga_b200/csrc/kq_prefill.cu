@@ -13,18 +13,22 @@
 //                        down.  Swap-AB: the MMA's M = 128 weight rows, N = the
 //                        expert's tokens (16..128 per chunk), K = input dim.
 //                        Warp-specialised and persistent (one CTA per SM):
-//                          warp 0     TMA: packed KQ tiles of the expert (bulk
-//                                     copies) and the tokens' 64-wide K chunks
-//                                     (2D tensor map, 128-byte swizzle)
-//                          warps 1-8  dequantise, two sets of four taking
+//                          warp 0     TMA: packed KQ tiles of the expert
+//                                     (2D tensor map over 128-byte rows,
+//                                     128-byte swizzle)
+//                          warp 1     TMA: the tokens' 64-wide K chunks, several
+//                                     groups per stage when the box is small
+//                          warps 2-9  dequantise, two sets of four taking
 //                                     alternate 64-wide groups: thread = weight
 //                                     row; a group's words -> 32 exact fp16
 //                                     pairs -> W = q*s + b -> one swizzled
 //                                     128-byte row of an A stage
-//                          warp 9     one thread issues tcgen05.mma (M=128,
-//                                     N=tokens, K=16) into a TMEM accumulator
-//                                     (two buffers), commits free the stages
-//                          warps 10-13 epilogue: tcgen05.ld; gate/up rows sit
+//                          warps 10-11 one thread each issues tcgen05.mma
+//                                     (M=128, N=tokens, K=16) for alternate
+//                                     groups into its own TMEM accumulator
+//                                     (two buffers each); commits free stages
+//                          warps 12-15 epilogue: tcgen05.ld of both
+//                                     accumulators, summed; gate/up rows sit
 //                                     8 lanes apart, act = silu(g)*u -> fp16
 //                                     in expert-sorted order; down -> fp32
 //   combine_kernel       out = [res] + sum_k w_k y_k, per-k outputs
@@ -189,12 +193,14 @@ struct TcParams {
     uint32_t* status;
 };
 
-constexpr int TC_NSTAGE = 4;          // A/B stages (one 64-wide group each)
+constexpr int TC_NSTAGE = 6;          // A stages (one 64-wide group of 128 weight rows each)
+constexpr int TC_NB = 2;              // B stages (16 KB: 16384 / (box * 128) groups of tokens each)
 constexpr int TC_NKQ = 2;             // packed super-tile stages
 constexpr int TC_NDQ = 2;             // dequantising warp sets (4 warps each), alternating groups
-constexpr int TC_THREADS = 32 * (2 + 4 * TC_NDQ + 4);  // producer, MMA, dequant sets, epilogue
+constexpr int TC_NMMA = 2;            // MMA-issuing warps: issuer i takes groups gi % 2 == i
+constexpr int TC_THREADS = 32 * (2 + 4 * TC_NDQ + TC_NMMA + 4);  // producers, dequant, MMA, epilogue
 constexpr int TC_STAGE_BYTES = 16384; // 128 rows x 128 B
-constexpr int TC_TMEM_COLS = 256;     // two 128-column accumulators
+constexpr int TC_TMEM_COLS = 512;     // 2 buffers x TC_NMMA issuers x 128-column accumulators
 
 // Packed tiles land in shared memory through a 2D tensor map that views the
 // layer as rows of 128 bytes with the 128-byte swizzle: byte (row, 16*slot + b)
@@ -208,7 +214,7 @@ __host__ __device__ constexpr int tc_tile_slot() {
 
 template <int BITS>
 __host__ __device__ constexpr size_t tc_smem_bytes() {
-    return 1024 + (size_t)TC_NSTAGE * TC_STAGE_BYTES * 2 + (size_t)TC_NKQ * 8 * tc_tile_slot<BITS>() + 256;
+    return 1024 + (size_t)(TC_NSTAGE + TC_NB) * TC_STAGE_BYTES + (size_t)TC_NKQ * 8 * tc_tile_slot<BITS>() + 256;
 }
 
 // 16-byte unit `lane` of 512-byte chunk `chunk` of a swizzled tile
@@ -300,33 +306,39 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = sm;
     uint8_t* sB = sA + TC_NSTAGE * TC_STAGE_BYTES;
-    uint8_t* sK = sB + TC_NSTAGE * TC_STAGE_BYTES;
+    uint8_t* sK = sB + TC_NB * TC_STAGE_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sK + TC_NKQ * 8 * TS);
-    uint64_t* kq_full = bars;       // [2]
-    uint64_t* kq_empty = bars + 2;  // [2]
-    uint64_t* a_full = bars + 4;    // [4]
-    uint64_t* b_full = bars + 8;    // [4]
-    uint64_t* ab_empty = bars + 12; // [4]
-    uint64_t* d_full = bars + 16;   // [2]
-    uint64_t* d_empty = bars + 18;  // [2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+    uint64_t* kq_full = bars;                        // [TC_NKQ]
+    uint64_t* kq_empty = kq_full + TC_NKQ;           // [TC_NKQ]
+    uint64_t* a_full = kq_empty + TC_NKQ;            // [TC_NSTAGE]
+    uint64_t* a_empty = a_full + TC_NSTAGE;          // [TC_NSTAGE]
+    uint64_t* b_full = a_empty + TC_NSTAGE;          // [TC_NB]
+    uint64_t* b_empty = b_full + TC_NB;              // [TC_NB]
+    uint64_t* d_full = b_empty + TC_NB;              // [2]
+    uint64_t* d_empty = d_full + 2;                  // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 2);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (tid == 0) {
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < TC_NKQ; ++i) {
             mbar_init(&kq_full[i], 1);
             mbar_init(&kq_empty[i], 128 * TC_NDQ);
-            mbar_init(&d_full[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&d_full[i], TC_NMMA);
             mbar_init(&d_empty[i], 128);
         }
         for (int i = 0; i < TC_NSTAGE; ++i) {
             mbar_init(&a_full[i], 128);
+            mbar_init(&a_empty[i], 1);
+        }
+        for (int i = 0; i < TC_NB; ++i) {
             mbar_init(&b_full[i], 1);
-            mbar_init(&ab_empty[i], 1);
+            mbar_init(&b_empty[i], TC_NMMA);
         }
         fence_mbar_init();
     }
-    constexpr int MMA_WARP = 1 + 4 * TC_NDQ;
+    constexpr int MMA_WARP = 2 + 4 * TC_NDQ;
     if (warp == MMA_WARP) {
         tc::tmem_alloc(tmem_slot, TC_TMEM_COLS);
         tc::tmem_relinquish();
@@ -339,49 +351,69 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int groups = p.nst * 8;
 
     if (warp == 0) {
-        // ---------------- producer ----------------
+        // ---------------- producer: packed super-tiles ----------------
         if (lane == 0) {
-            uint32_t kc = 0, gc = 0;
+            const uint64_t pol = policy_evict_first();
+            uint32_t kc = 0;
+            TcItem nxt = (int)blockIdx.x < n_items ? tc_item(p, blockIdx.x) : TcItem{};
             for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-                const TcItem it = tc_item(p, item);
-                const void* tm = it.box == 16 ? (const void*)&tb16
-                                              : (it.box == 32 ? (const void*)&tb32
-                                                              : (it.box == 64 ? (const void*)&tb64 : (const void*)&tb128));
+                const TcItem it = nxt;  // descriptor loads of the next item overlap this one
+                if (item + (int)gridDim.x < n_items) nxt = tc_item(p, item + gridDim.x);
                 const size_t ebase = (size_t)it.e * p.expert_bytes + p.mat_off;  // bytes into the layer
                 for (int st = 0; st < p.nst; ++st, ++kc) {
-                    const int s = kc & 1;
-                    mbar_wait(&kq_empty[s], ((kc >> 1) & 1) ^ 1, p.status);
+                    const int s = kc % TC_NKQ;
+                    mbar_wait(&kq_empty[s], ((kc / TC_NKQ) & 1) ^ 1, p.status);
                     mbar_expect_tx(&kq_full[s], 8 * TB);
                     for (int j = 0; j < 8; ++j) {
                         const int rt = it.mt * 8 + j;
                         const size_t off = ebase + ((size_t)rt * p.nst + st) * TB;  // multiple of 128
-                        tc::tma_load_2d(sK + ((size_t)s * 8 + j) * TS, &tkq, 0, (int)(off >> 7), &kq_full[s]);
-                    }
-                    for (int g = 0; g < 8; ++g, ++gc) {
-                        const int gs = gc % TC_NSTAGE;
-                        mbar_wait(&ab_empty[gs], ((gc / TC_NSTAGE) & 1) ^ 1, p.status);
-                        mbar_expect_tx(&b_full[gs], (uint32_t)it.box * 128);
-                        tc::tma_load_2d(sB + (size_t)gs * TC_STAGE_BYTES, tm, (st * 8 + g) * 64, it.pos0, &b_full[gs]);
+                        tc::tma_load_2d_hint(sK + ((size_t)s * 8 + j) * TS, &tkq, 0, (int)(off >> 7), &kq_full[s],
+                                             pol);
                     }
                 }
             }
         }
-    } else if (warp >= 1 && warp < MMA_WARP) {
+    } else if (warp == 1) {
+        // ---------------- producer: token K-chunks (B operand) ----------------
+        // A B stage holds gpb = 16384 / (box * 128) consecutive groups of the item
+        // (box rows x 64 fp16 each, one swizzled block per group).
+        if (lane == 0) {
+            const uint64_t pol = tc::policy_evict_last();
+            uint32_t bc = 0;
+            TcItem nxt = (int)blockIdx.x < n_items ? tc_item(p, blockIdx.x) : TcItem{};
+            for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+                const TcItem it = nxt;  // descriptor loads of the next item overlap this one
+                if (item + (int)gridDim.x < n_items) nxt = tc_item(p, item + gridDim.x);
+                const void* tm = it.box == 16 ? (const void*)&tb16
+                                              : (it.box == 32 ? (const void*)&tb32
+                                                              : (it.box == 64 ? (const void*)&tb64 : (const void*)&tb128));
+                const int gpb = TC_STAGE_BYTES / (it.box * 128);
+                for (int g0 = 0; g0 < groups; g0 += gpb, ++bc) {
+                    const int bs = bc % TC_NB;
+                    const int ng = min(gpb, groups - g0);
+                    mbar_wait(&b_empty[bs], ((bc / TC_NB) & 1) ^ 1, p.status);
+                    mbar_expect_tx(&b_full[bs], (uint32_t)(ng * it.box * 128));
+                    for (int j = 0; j < ng; ++j)
+                        tc::tma_load_2d_hint(sB + (size_t)bs * TC_STAGE_BYTES + (size_t)j * it.box * 128, tm,
+                                             (g0 + j) * 64, it.pos0, &b_full[bs], pol);
+                }
+            }
+        }
+    } else if (warp >= 2 && warp < MMA_WARP) {
         // ---------------- dequantise (set `ds` takes groups gc % TC_NDQ == ds) ----------------
-        const int ds = (warp - 1) >> 2;
-        const int m = (tid - 32) & 127;  // A row 0..127
+        const int ds = (warp - 2) >> 2;
+        const int m = (tid - 64) & 127;  // A row 0..127
         const int jt = m >> 4, r16 = m & 15;
         uint32_t kc = 0, gc = 0;
         for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-            const TcItem it = tc_item(p, item);
             for (int st = 0; st < p.nst; ++st, ++kc) {
-                const int s = kc & 1;
-                mbar_wait(&kq_full[s], (kc >> 1) & 1, p.status);
+                const int s = kc % TC_NKQ;
+                mbar_wait(&kq_full[s], (kc / TC_NKQ) & 1, p.status);
                 const uint8_t* tile = sK + ((size_t)s * 8 + jt) * TS;
                 for (int g = 0; g < 8; ++g, ++gc) {
                     if ((int)(gc % TC_NDQ) != ds) continue;
                     const int gs = gc % TC_NSTAGE;
-                    mbar_wait(&ab_empty[gs], ((gc / TC_NSTAGE) & 1) ^ 1, p.status);
+                    mbar_wait(&a_empty[gs], ((gc / TC_NSTAGE) & 1) ^ 1, p.status);
                     dequant_row<BITS, SB_DT>(tile, r16, g, sA + (size_t)gs * TC_STAGE_BYTES, m);
                     fence_proxy_async_smem();
                     tc::mbar_arrive(&a_full[gs]);
@@ -389,31 +421,49 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 tc::mbar_arrive(&kq_empty[s]);
             }
         }
-    } else if (warp == MMA_WARP) {
+    } else if (warp < MMA_WARP + TC_NMMA) {
         // ---------------- MMA issue ----------------
+        // The tensor pipe accepts an M=128, K=16 MMA about every 40 cycles at
+        // small N, but one issuing thread only every ~68: two issuers, each
+        // with its own accumulator (the epilogue adds them), keep it fed.
+        // Issuer `mi` takes the groups gi % 2 == mi (the A stages its dequant
+        // set fills).  Every B stage of the item is waited for and released by
+        // both issuers, even one holding none of an issuer's groups.
+        const int mi = warp - MMA_WARP;
         if (lane == 0) {
-            uint32_t gc = 0, ic = 0;
+            uint32_t gc = 0, ic = 0, bc = 0;
+            TcItem nxt = (int)blockIdx.x < n_items ? tc_item(p, blockIdx.x) : TcItem{};
             for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-                const TcItem it = tc_item(p, item);
+                const TcItem it = nxt;  // descriptor loads of the next item overlap this one
+                if (item + (int)gridDim.x < n_items) nxt = tc_item(p, item + gridDim.x);
                 const int db = ic & 1;
+                const int gpb = TC_STAGE_BYTES / (it.box * 128);
                 mbar_wait(&d_empty[db], ((ic >> 1) & 1) ^ 1, p.status);
                 tc::fence_after_sync();
-                const uint32_t d_tmem = tmem + (uint32_t)(db * 128);
+                const uint32_t d_tmem = tmem + (uint32_t)(db * 256 + mi * 128);
                 const uint32_t idesc = tc::idesc_f16(128, it.box, false);
-                for (int gi = 0; gi < groups; ++gi, ++gc) {
-                    const int gs = gc % TC_NSTAGE;
-                    const uint32_t ph = (gc / TC_NSTAGE) & 1;
-                    mbar_wait(&a_full[gs], ph, p.status);
-                    mbar_wait(&b_full[gs], ph, p.status);
+                for (int g0 = 0; g0 < groups; g0 += gpb, ++bc) {
+                    const int bs = bc % TC_NB;
+                    mbar_wait(&b_full[bs], (bc / TC_NB) & 1, p.status);
                     tc::fence_after_sync();
-                    const uint64_t da = tc::smem_desc_sw128(sA + (size_t)gs * TC_STAGE_BYTES);
-                    const uint64_t dbd = tc::smem_desc_sw128(sB + (size_t)gs * TC_STAGE_BYTES);
+                    const int g1 = min(g0 + gpb, groups);
+                    for (int gi = g0 + ((g0 & 1) != mi ? 1 : 0); gi < g1; gi += 2) {
+                        const uint32_t g = gc + (uint32_t)gi;
+                        const int gs = g % TC_NSTAGE;
+                        mbar_wait(&a_full[gs], (g / TC_NSTAGE) & 1, p.status);
+                        tc::fence_after_sync();
+                        const uint64_t da = tc::smem_desc_sw128(sA + (size_t)gs * TC_STAGE_BYTES);
+                        const uint64_t dbd =
+                            tc::smem_desc_sw128(sB + (size_t)bs * TC_STAGE_BYTES + (size_t)(gi - g0) * it.box * 128);
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        tc::mma_f16_ss(d_tmem, tc::desc_advance(da, 32 * k), tc::desc_advance(dbd, 32 * k), idesc,
-                                       gi > 0 || k > 0);
-                    tc::mma_commit(&ab_empty[gs]);
+                        for (int k = 0; k < 4; ++k)
+                            tc::mma_f16_ss(d_tmem, tc::desc_advance(da, 32 * k), tc::desc_advance(dbd, 32 * k), idesc,
+                                           gi > mi || k > 0);
+                        tc::mma_commit(&a_empty[gs]);
+                    }
+                    tc::mma_commit(&b_empty[bs]);
                 }
+                gc += (uint32_t)groups;
                 tc::mma_commit(&d_full[db]);
                 ++ic;
             }
@@ -423,16 +473,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int q = warp & 3;         // TMEM lane quarter this warp may access
         const int L = q * 32 + lane;    // accumulator row
         uint32_t ic = 0;
+        TcItem nxt = (int)blockIdx.x < n_items ? tc_item(p, blockIdx.x) : TcItem{};
         for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-            const TcItem it = tc_item(p, item);
+            const TcItem it = nxt;  // descriptor loads of the next item overlap this one
+            if (item + (int)gridDim.x < n_items) nxt = tc_item(p, item + gridDim.x);
             const int db = ic & 1;
             mbar_wait(&d_full[db], (ic >> 1) & 1, p.status);
             tc::fence_after_sync();
-            const uint32_t taddr = tmem + (uint32_t)(db * 128) + ((uint32_t)(q * 32) << 16);
+            const uint32_t taddr = tmem + (uint32_t)(db * 256) + ((uint32_t)(q * 32) << 16);
             for (int c0 = 0; c0 < it.box; c0 += 16) {
-                uint32_t r[16];
+                uint32_t r[16], r2[16];
                 tc::tmem_ld16(taddr + (uint32_t)c0, r);
+                tc::tmem_ld16(taddr + 128u + (uint32_t)c0, r2);
                 tc::tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) + __uint_as_float(r2[i]));
                 if (p.mode == 0) {
                     const int jt = L >> 4, r16 = L & 15;
                     const int irow = it.mt * 64 + jt * 8 + (r16 & 7);

@@ -116,5 +116,21 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
         : "memory");
 }
 
+// same with an L2 cache policy (createpolicy)
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const void* tmap, int x, int y, uint64_t* bar,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 }  // namespace tc
 }  // namespace kq
