@@ -68,6 +68,48 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     return false;
 }
 
+// try_wait that lets the hardware suspend the thread for up to `ns`
+// nanoseconds; the thread resumes as soon as the phase completes.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+#ifndef KQ_WAIT_NS
+#define KQ_WAIT_NS 1000000000ull  // 1 s: a phase that takes longer latches KQ_DEV_WAIT_TIMEOUT
+#endif
+
+// Bounded wait for waits that are often long (pipeline roles of persistent
+// kernels): sleeping try_wait instead of a hot poll, so waiting warps leave
+// the issue slots to the working ones.  Bounded by KQ_WAIT_NS of wall time
+// (%globaltimer); returns false, with the timeout bit latched, if exceeded,
+// and at once if another wait of the launch already timed out.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t* status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait_hint(bar, parity, 200000u)) return true;
+        if (status && (*reinterpret_cast<volatile uint32_t*>(status) & KQ_DEV_WAIT_TIMEOUT)) return false;
+        if (global_ns() - t0 > KQ_WAIT_NS) {
+            set_status(status, KQ_DEV_WAIT_TIMEOUT);
+            return false;
+        }
+    }
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -60,7 +60,7 @@ constexpr int GROUP_MAX_E = 4096;  // experts per layer the one-CTA grouping sup
 __global__ void __launch_bounds__(GROUP_THREADS, 1)
     group_kernel(const int32_t* __restrict__ idx, int A, int K, int E, int* __restrict__ count,
                  int* __restrict__ offset, int32_t* __restrict__ s_tok, int32_t* __restrict__ inv_pos,
-                 int32_t* __restrict__ chunk_list, int* __restrict__ n_chunks, uint32_t* status) {
+                 int4* __restrict__ chunk_list, int* __restrict__ n_chunks, uint32_t* status) {
     __shared__ int cnt[GROUP_MAX_E];
     __shared__ int off_s[GROUP_MAX_E];
     __shared__ int wsum[2][32];
@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1)
         off_s[e] = n_run;
         offset[e] = n_run;
         count[e] = ne;
-        for (int c = 0; c < nch; ++c) chunk_list[c_run + c] = (e << 16) | c;
+        for (int c = 0; c < nch; ++c) chunk_list[c_run + c] = make_int4(e, min(128, ne - c * 128), n_run + c * 128, c);
         n_run += ne;
         c_run += nch;
     }
@@ -181,7 +181,7 @@ struct TcParams {
     int E;
     const int* count;
     const int* offset;
-    const int32_t* chunk_list;  // live work chunks, (expert << 16) | chunk
+    const int4* chunk_list;     // live work chunks: {expert, tokens (<= 128), first position, chunk}
     const int* n_chunks;
     int mode;             // 0: gate/up + activation -> act_s; 1: down -> ys
     __half* act_s;        // [A][I]
@@ -196,7 +196,7 @@ struct TcParams {
 constexpr int TC_NSTAGE = 6;          // A stages (one 64-wide group of 128 weight rows each)
 constexpr int TC_NB = 2;              // B stages (16 KB: 16384 / (box * 128) groups of tokens each)
 constexpr int TC_NKQ = 2;             // packed super-tile stages
-constexpr int TC_NDQ = 2;             // dequantising warp sets (4 warps each), alternating groups
+constexpr int TC_NDQ = 4;             // dequantising warp sets (4 warps each), alternating groups
 constexpr int TC_NMMA = 2;            // MMA-issuing warps: issuer i takes groups gi % 2 == i
 constexpr int TC_THREADS = 32 * (2 + 4 * TC_NDQ + TC_NMMA + 4);  // producers, dequant, MMA, epilogue
 constexpr int TC_STAGE_BYTES = 16384; // 128 rows x 128 B
@@ -278,20 +278,27 @@ __device__ __forceinline__ void dequant_row(const uint8_t* tile, int r16, int g,
 }
 
 struct TcItem {
-    int e, nc, mt, n, box, pos0;
+    int e, mt, n, box, pos0;
 };
 
-// item = chunk * n_mt + mt over the live chunks only
-__device__ __forceinline__ TcItem tc_item(const TcParams& p, int item) {
+// item = chunk * n_mt + mt over the live chunks.  The descriptor load is
+// volatile so it issues where it is written: each role loads the next item's
+// descriptor one item ahead.
+__device__ __forceinline__ int4 tc_desc_load(const TcParams& p, int item) {
+    int4 d;
+    asm volatile("ld.global.nc.v4.s32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(d.x), "=r"(d.y), "=r"(d.z), "=r"(d.w)
+                 : "l"(p.chunk_list + item / p.n_mt));
+    return d;
+}
+
+__device__ __forceinline__ TcItem tc_item(const TcParams& p, int4 d, int item) {
     TcItem it;
-    const int32_t ch = p.chunk_list[item / p.n_mt];
     it.mt = item % p.n_mt;
-    it.e = ch >> 16;
-    it.nc = ch & 0xFFFF;
-    const int ne = p.count[it.e];
-    it.n = min(128, ne - it.nc * 128);
+    it.e = d.x;
+    it.n = d.y;
+    it.pos0 = d.z;
     it.box = it.n <= 16 ? 16 : (it.n <= 32 ? 32 : (it.n <= 64 ? 64 : 128));
-    it.pos0 = p.offset[it.e] + it.nc * 128;
     return it;
 }
 
@@ -355,14 +362,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();
             uint32_t kc = 0;
-            TcItem nxt = (int)blockIdx.x < n_items ? tc_item(p, blockIdx.x) : TcItem{};
+            int4 nd = (int)blockIdx.x < n_items ? tc_desc_load(p, blockIdx.x) : make_int4(0, 0, 0, 0);
             for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-                const TcItem it = nxt;  // descriptor loads of the next item overlap this one
-                if (item + (int)gridDim.x < n_items) nxt = tc_item(p, item + gridDim.x);
+                const TcItem it = tc_item(p, nd, item);
+                if (item + (int)gridDim.x < n_items) nd = tc_desc_load(p, item + gridDim.x);
                 const size_t ebase = (size_t)it.e * p.expert_bytes + p.mat_off;  // bytes into the layer
                 for (int st = 0; st < p.nst; ++st, ++kc) {
                     const int s = kc % TC_NKQ;
-                    mbar_wait(&kq_empty[s], ((kc / TC_NKQ) & 1) ^ 1, p.status);
+                    mbar_wait_sleep(&kq_empty[s], ((kc / TC_NKQ) & 1) ^ 1, p.status);
                     mbar_expect_tx(&kq_full[s], 8 * TB);
                     for (int j = 0; j < 8; ++j) {
                         const int rt = it.mt * 8 + j;
@@ -380,10 +387,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (lane == 0) {
             const uint64_t pol = tc::policy_evict_last();
             uint32_t bc = 0;
-            TcItem nxt = (int)blockIdx.x < n_items ? tc_item(p, blockIdx.x) : TcItem{};
+            int4 nd = (int)blockIdx.x < n_items ? tc_desc_load(p, blockIdx.x) : make_int4(0, 0, 0, 0);
             for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-                const TcItem it = nxt;  // descriptor loads of the next item overlap this one
-                if (item + (int)gridDim.x < n_items) nxt = tc_item(p, item + gridDim.x);
+                const TcItem it = tc_item(p, nd, item);
+                if (item + (int)gridDim.x < n_items) nd = tc_desc_load(p, item + gridDim.x);
                 const void* tm = it.box == 16 ? (const void*)&tb16
                                               : (it.box == 32 ? (const void*)&tb32
                                                               : (it.box == 64 ? (const void*)&tb64 : (const void*)&tb128));
@@ -391,7 +398,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 for (int g0 = 0; g0 < groups; g0 += gpb, ++bc) {
                     const int bs = bc % TC_NB;
                     const int ng = min(gpb, groups - g0);
-                    mbar_wait(&b_empty[bs], ((bc / TC_NB) & 1) ^ 1, p.status);
+                    mbar_wait_sleep(&b_empty[bs], ((bc / TC_NB) & 1) ^ 1, p.status);
                     mbar_expect_tx(&b_full[bs], (uint32_t)(ng * it.box * 128));
                     for (int j = 0; j < ng; ++j)
                         tc::tma_load_2d_hint(sB + (size_t)bs * TC_STAGE_BYTES + (size_t)j * it.box * 128, tm,
@@ -408,12 +415,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
             for (int st = 0; st < p.nst; ++st, ++kc) {
                 const int s = kc % TC_NKQ;
-                mbar_wait(&kq_full[s], (kc / TC_NKQ) & 1, p.status);
+                mbar_wait_sleep(&kq_full[s], (kc / TC_NKQ) & 1, p.status);
                 const uint8_t* tile = sK + ((size_t)s * 8 + jt) * TS;
                 for (int g = 0; g < 8; ++g, ++gc) {
                     if ((int)(gc % TC_NDQ) != ds) continue;
                     const int gs = gc % TC_NSTAGE;
-                    mbar_wait(&a_empty[gs], ((gc / TC_NSTAGE) & 1) ^ 1, p.status);
+                    mbar_wait_sleep(&a_empty[gs], ((gc / TC_NSTAGE) & 1) ^ 1, p.status);
                     dequant_row<BITS, SB_DT>(tile, r16, g, sA + (size_t)gs * TC_STAGE_BYTES, m);
                     fence_proxy_async_smem();
                     tc::mbar_arrive(&a_full[gs]);
@@ -430,41 +437,45 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // set fills).  Every B stage of the item is waited for and released by
         // both issuers, even one holding none of an issuer's groups.
         const int mi = warp - MMA_WARP;
-        if (lane == 0) {
+        const uint32_t leader = lane == 0;
+        {
             uint32_t gc = 0, ic = 0, bc = 0;
-            TcItem nxt = (int)blockIdx.x < n_items ? tc_item(p, blockIdx.x) : TcItem{};
+            int4 nd = (int)blockIdx.x < n_items ? tc_desc_load(p, blockIdx.x) : make_int4(0, 0, 0, 0);
             for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-                const TcItem it = nxt;  // descriptor loads of the next item overlap this one
-                if (item + (int)gridDim.x < n_items) nxt = tc_item(p, item + gridDim.x);
+                const TcItem it = tc_item(p, nd, item);
+                if (item + (int)gridDim.x < n_items) nd = tc_desc_load(p, item + gridDim.x);
                 const int db = ic & 1;
                 const int gpb = TC_STAGE_BYTES / (it.box * 128);
-                mbar_wait(&d_empty[db], ((ic >> 1) & 1) ^ 1, p.status);
+                mbar_wait_sleep(&d_empty[db], ((ic >> 1) & 1) ^ 1, p.status);
+                __syncwarp();
                 tc::fence_after_sync();
                 const uint32_t d_tmem = tmem + (uint32_t)(db * 256 + mi * 128);
                 const uint32_t idesc = tc::idesc_f16(128, it.box, false);
                 for (int g0 = 0; g0 < groups; g0 += gpb, ++bc) {
                     const int bs = bc % TC_NB;
-                    mbar_wait(&b_full[bs], (bc / TC_NB) & 1, p.status);
+                    mbar_wait_sleep(&b_full[bs], (bc / TC_NB) & 1, p.status);
+                    __syncwarp();
                     tc::fence_after_sync();
                     const int g1 = min(g0 + gpb, groups);
                     for (int gi = g0 + ((g0 & 1) != mi ? 1 : 0); gi < g1; gi += 2) {
                         const uint32_t g = gc + (uint32_t)gi;
                         const int gs = g % TC_NSTAGE;
-                        mbar_wait(&a_full[gs], (g / TC_NSTAGE) & 1, p.status);
+                        mbar_wait_sleep(&a_full[gs], (g / TC_NSTAGE) & 1, p.status);
+                        __syncwarp();
                         tc::fence_after_sync();
                         const uint64_t da = tc::smem_desc_sw128(sA + (size_t)gs * TC_STAGE_BYTES);
                         const uint64_t dbd =
                             tc::smem_desc_sw128(sB + (size_t)bs * TC_STAGE_BYTES + (size_t)(gi - g0) * it.box * 128);
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
-                            tc::mma_f16_ss(d_tmem, tc::desc_advance(da, 32 * k), tc::desc_advance(dbd, 32 * k), idesc,
-                                           gi > mi || k > 0);
-                        tc::mma_commit(&a_empty[gs]);
+                            tc::mma_f16_ss_warp(d_tmem, tc::desc_advance(da, 32 * k), tc::desc_advance(dbd, 32 * k),
+                                                idesc, gi > mi || k > 0, leader);
+                        tc::mma_commit_warp(&a_empty[gs], leader);
                     }
-                    tc::mma_commit(&b_empty[bs]);
+                    tc::mma_commit_warp(&b_empty[bs], leader);
                 }
                 gc += (uint32_t)groups;
-                tc::mma_commit(&d_full[db]);
+                tc::mma_commit_warp(&d_full[db], leader);
                 ++ic;
             }
         }
@@ -473,12 +484,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int q = warp & 3;         // TMEM lane quarter this warp may access
         const int L = q * 32 + lane;    // accumulator row
         uint32_t ic = 0;
-        TcItem nxt = (int)blockIdx.x < n_items ? tc_item(p, blockIdx.x) : TcItem{};
+        int4 nd = (int)blockIdx.x < n_items ? tc_desc_load(p, blockIdx.x) : make_int4(0, 0, 0, 0);
         for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-            const TcItem it = nxt;  // descriptor loads of the next item overlap this one
-            if (item + (int)gridDim.x < n_items) nxt = tc_item(p, item + gridDim.x);
+            const TcItem it = tc_item(p, nd, item);
+            if (item + (int)gridDim.x < n_items) nd = tc_desc_load(p, item + gridDim.x);
             const int db = ic & 1;
-            mbar_wait(&d_full[db], (ic >> 1) & 1, p.status);
+            mbar_wait_sleep(&d_full[db], (ic >> 1) & 1, p.status);
             tc::fence_after_sync();
             const uint32_t taddr = tmem + (uint32_t)(db * 256) + ((uint32_t)(q * 32) << 16);
             for (int c0 = 0; c0 < it.box; c0 += 16) {
@@ -564,7 +575,7 @@ static PrefillWs prefill_ws_layout(const kq_table* t, int T, int K) {
     L.offset = o;
     o = al(o + (size_t)t->d.num_experts * 4);
     L.chunks = o;  // at most E + A/128 live chunks
-    o = al(o + ((size_t)t->d.num_experts + A / 128 + 1) * 4);
+    o = al(o + ((size_t)t->d.num_experts + A / 128 + 1) * 16);
     L.n_chunks = o;
     o = al(o + 4);
     L.s_tok = o;
@@ -685,7 +696,7 @@ extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x
     uint32_t* status = reinterpret_cast<uint32_t*>(ws + L.status);
     int* count = reinterpret_cast<int*>(ws + L.count);
     int* offset = reinterpret_cast<int*>(ws + L.offset);
-    int32_t* chunk_list = reinterpret_cast<int32_t*>(ws + L.chunks);
+    int4* chunk_list = reinterpret_cast<int4*>(ws + L.chunks);
     int* n_chunks = reinterpret_cast<int*>(ws + L.n_chunks);
     int32_t* s_tok = reinterpret_cast<int32_t*>(ws + L.s_tok);
     int32_t* inv_pos = reinterpret_cast<int32_t*>(ws + L.inv_pos);

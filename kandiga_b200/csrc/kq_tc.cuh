@@ -78,6 +78,30 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uin
         : "memory");
 }
 
+// Warp-converged forms: the whole warp executes the instruction, predicated
+// on `leader` (one lane).  Keeping the issuing warp converged lets the
+// descriptors live in uniform registers, which the MMA issue rate depends on.
+__device__ __forceinline__ void mma_f16_ss_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                bool accumulate, uint32_t leader) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.ne.b32 e, %5, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u), "r"(leader)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_warp(uint64_t* bar, uint32_t leader) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "setp.ne.b32 e, %1, 0;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+            smem_u32(bar)),
+        "r"(leader)
+        : "memory");
+}
+
 // arrive on an mbarrier when all previously issued MMAs of this thread complete
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
