@@ -110,6 +110,21 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
     }
 }
 
+#ifndef KQ_DRAIN_NS
+#define KQ_DRAIN_NS 100000000ull  // 100 ms
+#endif
+
+// Exit-path wait for this thread's own asynchronous work (a TMA fill or an
+// MMA commit) on a barrier: ignores the timeout latch, so a role that gave up
+// early still lets its copies and MMAs finish before the CTA frees its shared
+// and tensor memory.  Bounded by KQ_DRAIN_NS.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return;
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait_hint(bar, parity, 100000u))
+        if (global_ns() - t0 > KQ_DRAIN_NS) return;
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -18,16 +18,16 @@
 //                                     128-byte swizzle)
 //                          warp 1     TMA: the tokens' 64-wide K chunks, several
 //                                     groups per stage when the box is small
-//                          warps 2-9  dequantise, two sets of four taking
+//                          warps 2-13 dequantise, three sets of four taking
 //                                     alternate 64-wide groups: thread = weight
 //                                     row; a group's words -> 32 exact fp16
 //                                     pairs -> W = q*s + b -> one swizzled
 //                                     128-byte row of an A stage
-//                          warps 10-11 one thread each issues tcgen05.mma
-//                                     (M=128, N=tokens, K=16) for alternate
-//                                     groups into its own TMEM accumulator
-//                                     (two buffers each); commits free stages
-//                          warps 12-15 epilogue: tcgen05.ld of both
+//                          next 3     one thread each issues tcgen05.mma
+//                                     (M=128, N=tokens, K=16) for every 3rd
+//                                     group into its own TMEM accumulator;
+//                                     commits free the stages
+//                          last 4     epilogue: tcgen05.ld of the
 //                                     accumulators, summed; gate/up rows sit
 //                                     8 lanes apart, act = silu(g)*u -> fp16
 //                                     in expert-sorted order; down -> fp32
@@ -193,14 +193,20 @@ struct TcParams {
     uint32_t* status;
 };
 
-constexpr int TC_NSTAGE = 6;          // A stages (one 64-wide group of 128 weight rows each)
+constexpr int TC_NMMA = 3;            // MMA-issuing warps = dequantising warp sets (4 warps each)
+constexpr int TC_SLOTS = 2;           // A stages per issuer
+constexpr int TC_NSTAGE = TC_NMMA * TC_SLOTS;  // A stages (one 64-wide group of 128 weight rows each)
 constexpr int TC_NB = 2;              // B stages (16 KB: 16384 / (box * 128) groups of tokens each)
 constexpr int TC_NKQ = 2;             // packed super-tile stages
-constexpr int TC_NDQ = 4;             // dequantising warp sets (4 warps each), alternating groups
-constexpr int TC_NMMA = 2;            // MMA-issuing warps: issuer i takes groups gi % 2 == i
+constexpr int TC_NDQ = TC_NMMA;
+// Group gi of an item (item-local index) is dequantised by set gi % TC_NMMA
+// into that set's private ring of TC_SLOTS A stages and consumed by the
+// issuer of the same number.  An mbarrier wait tells apart only two phases,
+// so each stage must have exactly one filler and one consumer, in order.
 constexpr int TC_THREADS = 32 * (2 + 4 * TC_NDQ + TC_NMMA + 4);  // producers, dequant, MMA, epilogue
 constexpr int TC_STAGE_BYTES = 16384; // 128 rows x 128 B
-constexpr int TC_TMEM_COLS = 512;     // 2 buffers x TC_NMMA issuers x 128-column accumulators
+constexpr int TC_TMEM_COLS = 512;     // 2 buffers x 256 (TC_NMMA x 64) columns, or TC_NMMA x 128 for a 128-token box
+static_assert(TC_NMMA * 64 <= 256 && TC_NMMA * 128 <= TC_TMEM_COLS, "accumulators must fit tensor memory");
 
 // Packed tiles land in shared memory through a 2D tensor map that views the
 // layer as rows of 128 bytes with the 128-byte swizzle: byte (row, 16*slot + b)
@@ -323,7 +329,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint64_t* b_empty = b_full + TC_NB;              // [TC_NB]
     uint64_t* d_full = b_empty + TC_NB;              // [2]
     uint64_t* d_empty = d_full + 2;                  // [2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 2);
+    uint64_t* drain = d_empty + 2;                   // [TC_NMMA] exit: this issuer's MMAs are done
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + TC_NMMA);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (tid == 0) {
@@ -335,6 +342,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(&d_full[i], TC_NMMA);
             mbar_init(&d_empty[i], 128);
         }
+        for (int i = 0; i < TC_NMMA; ++i) mbar_init(&drain[i], 1);
         for (int i = 0; i < TC_NSTAGE; ++i) {
             mbar_init(&a_full[i], 128);
             mbar_init(&a_empty[i], 1);
@@ -379,6 +387,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                 }
             }
+            for (uint32_t f = kc > TC_NKQ ? kc - TC_NKQ : 0; f < kc; ++f)  // own fills landed
+                mbar_drain(&kq_full[f % TC_NKQ], (f / TC_NKQ) & 1);
         }
     } else if (warp == 1) {
         // ---------------- producer: token K-chunks (B operand) ----------------
@@ -405,51 +415,65 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                                              (g0 + j) * 64, it.pos0, &b_full[bs], pol);
                 }
             }
+            for (uint32_t f = bc > TC_NB ? bc - TC_NB : 0; f < bc; ++f)  // own fills landed
+                mbar_drain(&b_full[f % TC_NB], (f / TC_NB) & 1);
         }
     } else if (warp >= 2 && warp < MMA_WARP) {
-        // ---------------- dequantise (set `ds` takes groups gc % TC_NDQ == ds) ----------------
+        // ---------------- dequantise (set `ds` takes the groups gi % TC_NMMA == ds) ----------------
         const int ds = (warp - 2) >> 2;
         const int m = (tid - 64) & 127;  // A row 0..127
         const int jt = m >> 4, r16 = m & 15;
-        uint32_t kc = 0, gc = 0;
+        uint32_t kc = 0, lc = 0;
         for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
             for (int st = 0; st < p.nst; ++st, ++kc) {
                 const int s = kc % TC_NKQ;
                 mbar_wait_sleep(&kq_full[s], (kc / TC_NKQ) & 1, p.status);
                 const uint8_t* tile = sK + ((size_t)s * 8 + jt) * TS;
-                for (int g = 0; g < 8; ++g, ++gc) {
-                    if ((int)(gc % TC_NDQ) != ds) continue;
-                    const int gs = gc % TC_NSTAGE;
-                    mbar_wait_sleep(&a_empty[gs], ((gc / TC_NSTAGE) & 1) ^ 1, p.status);
+                for (int g = 0; g < 8; ++g) {
+                    if ((st * 8 + g) % TC_NMMA != ds) continue;
+                    const int gs = ds * TC_SLOTS + (int)(lc % TC_SLOTS);
+                    mbar_wait_sleep(&a_empty[gs], ((lc / TC_SLOTS) & 1) ^ 1, p.status);
                     dequant_row<BITS, SB_DT>(tile, r16, g, sA + (size_t)gs * TC_STAGE_BYTES, m);
                     fence_proxy_async_smem();
                     tc::mbar_arrive(&a_full[gs]);
+                    ++lc;
                 }
                 tc::mbar_arrive(&kq_empty[s]);
             }
         }
     } else if (warp < MMA_WARP + TC_NMMA) {
         // ---------------- MMA issue ----------------
-        // The tensor pipe accepts an M=128, K=16 MMA about every 40 cycles at
-        // small N, but one issuing thread only every ~68: two issuers, each
-        // with its own accumulator (the epilogue adds them), keep it fed.
-        // Issuer `mi` takes the groups gi % 2 == mi (the A stages its dequant
-        // set fills).  Every B stage of the item is waited for and released by
-        // both issuers, even one holding none of an issuer's groups.
+        // One thread issues an M=128, K=16 MMA about every 70 cycles at best,
+        // and each group also costs it a barrier wait and a commit; the tensor
+        // pipe takes one about every 40 cycles at small N.  So the groups of an
+        // item are spread over the TC_NMMA issuers, issuer mi accumulating the
+        // groups gi % TC_NMMA == mi into its own TMEM columns; the epilogue
+        // adds the accumulators in a fixed order, so a token's result does not
+        // depend on the size of the chunk it lands in.  Accumulators: boxes
+        // <= 64 tokens take TC_NMMA x 64 columns of one of two 256-column
+        // buffers; a 128-token box takes TC_NMMA x 128 columns from column 0,
+        // across both buffers, so it (and the item after it) first waits for
+        // the previous item's epilogue.  Issuers without groups in a B stage
+        // still wait for and release it, so every barrier sees all issuers.
         const int mi = warp - MMA_WARP;
         const uint32_t leader = lane == 0;
         {
-            uint32_t gc = 0, ic = 0, bc = 0;
+            uint32_t lc = 0, ic = 0, bc = 0;
+            bool prev_full = false;
             int4 nd = (int)blockIdx.x < n_items ? tc_desc_load(p, blockIdx.x) : make_int4(0, 0, 0, 0);
             for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
                 const TcItem it = tc_item(p, nd, item);
                 if (item + (int)gridDim.x < n_items) nd = tc_desc_load(p, item + gridDim.x);
                 const int db = ic & 1;
                 const int gpb = TC_STAGE_BYTES / (it.box * 128);
+                const bool full = it.box == 128;
                 mbar_wait_sleep(&d_empty[db], ((ic >> 1) & 1) ^ 1, p.status);
+                if ((full || prev_full) && ic > 0)  // the other buffer's item (ic - 1) must be drained too
+                    mbar_wait_sleep(&d_empty[db ^ 1], ((ic - 1) >> 1) & 1, p.status);
+                prev_full = full;
                 __syncwarp();
                 tc::fence_after_sync();
-                const uint32_t d_tmem = tmem + (uint32_t)(db * 256 + mi * 128);
+                const uint32_t d_tmem = tmem + (full ? (uint32_t)(mi * 128) : (uint32_t)(db * 256 + mi * 64));
                 const uint32_t idesc = tc::idesc_f16(128, it.box, false);
                 for (int g0 = 0; g0 < groups; g0 += gpb, ++bc) {
                     const int bs = bc % TC_NB;
@@ -457,27 +481,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     __syncwarp();
                     tc::fence_after_sync();
                     const int g1 = min(g0 + gpb, groups);
-                    for (int gi = g0 + ((g0 & 1) != mi ? 1 : 0); gi < g1; gi += 2) {
-                        const uint32_t g = gc + (uint32_t)gi;
-                        const int gs = g % TC_NSTAGE;
-                        mbar_wait_sleep(&a_full[gs], (g / TC_NSTAGE) & 1, p.status);
-                        __syncwarp();
-                        tc::fence_after_sync();
-                        const uint64_t da = tc::smem_desc_sw128(sA + (size_t)gs * TC_STAGE_BYTES);
-                        const uint64_t dbd =
-                            tc::smem_desc_sw128(sB + (size_t)bs * TC_STAGE_BYTES + (size_t)(gi - g0) * it.box * 128);
+                    {
+                        for (int gi = g0 + ((mi - g0 % TC_NMMA + TC_NMMA) % TC_NMMA); gi < g1; gi += TC_NMMA, ++lc) {
+                            const int gs = mi * TC_SLOTS + (int)(lc % TC_SLOTS);
+                            mbar_wait_sleep(&a_full[gs], (lc / TC_SLOTS) & 1, p.status);
+                            __syncwarp();
+                            tc::fence_after_sync();
+                            const uint64_t da = tc::smem_desc_sw128(sA + (size_t)gs * TC_STAGE_BYTES);
+                            const uint64_t dbd = tc::smem_desc_sw128(sB + (size_t)bs * TC_STAGE_BYTES +
+                                                                     (size_t)(gi - g0) * it.box * 128);
 #pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            tc::mma_f16_ss_warp(d_tmem, tc::desc_advance(da, 32 * k), tc::desc_advance(dbd, 32 * k),
-                                                idesc, gi > mi || k > 0, leader);
-                        tc::mma_commit_warp(&a_empty[gs], leader);
+                            for (int k = 0; k < 4; ++k)
+                                tc::mma_f16_ss_warp(d_tmem, tc::desc_advance(da, 32 * k), tc::desc_advance(dbd, 32 * k),
+                                                    idesc, gi > mi || k > 0, leader);
+                            tc::mma_commit_warp(&a_empty[gs], leader);
+                        }
                     }
                     tc::mma_commit_warp(&b_empty[bs], leader);
                 }
-                gc += (uint32_t)groups;
                 tc::mma_commit_warp(&d_full[db], leader);
                 ++ic;
             }
+            tc::mma_commit_warp(&drain[mi], leader);  // all of this issuer's MMAs complete before exit
+            mbar_drain(&drain[mi], 0);
         }
     } else {
         // ---------------- epilogue (last four warps) ----------------
@@ -491,14 +517,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int db = ic & 1;
             mbar_wait_sleep(&d_full[db], (ic >> 1) & 1, p.status);
             tc::fence_after_sync();
-            const uint32_t taddr = tmem + (uint32_t)(db * 256) + ((uint32_t)(q * 32) << 16);
+            const bool full = it.box == 128;
+            const uint32_t acc_cols = full ? 128u : 64u;
+            const uint32_t taddr = tmem + (full ? 0u : (uint32_t)(db * 256)) + ((uint32_t)(q * 32) << 16);
             for (int c0 = 0; c0 < it.box; c0 += 16) {
-                uint32_t r[16], r2[16];
+                uint32_t r[16];
                 tc::tmem_ld16(taddr + (uint32_t)c0, r);
-                tc::tmem_ld16(taddr + 128u + (uint32_t)c0, r2);
-                tc::tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) + __uint_as_float(r2[i]));
+                for (int a = 1; a < TC_NMMA; ++a) {  // fixed order: (acc0 + acc1) + acc2 ...
+                    uint32_t r2[16];
+                    tc::tmem_ld16(taddr + (uint32_t)a * acc_cols + (uint32_t)c0, r2);
+                    tc::tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) + __uint_as_float(r2[i]));
+                }
+                tc::tmem_ld_wait();
                 if (p.mode == 0) {
                     const int jt = L >> 4, r16 = L & 15;
                     const int irow = it.mt * 64 + jt * 8 + (r16 & 7);

@@ -119,3 +119,49 @@ def test_prefill_large_batch_bitwise_repeatable(gpu):
     worst = max(rel_l2(pk[i, k], y[i, k]) for i in range(len(rows)) for k in range(K))
     assert worst < RTOL_L2, worst
     assert t.status() == 0
+
+
+def test_prefill_bench_shape(gpu):
+    """The benchmark's workload shape: E=256 top-8, T=512 tokens, H2048/I512
+    4-bit (about 16 tokens per expert, many work items per CTA).  Two runs give
+    identical bits, the result agrees with the decode path, and sampled tokens
+    agree with the oracle (the layer is quantized on the GPU; the oracle gets
+    the routed experts' MLX tensors)."""
+    from kandiga_b200.experts import ExpertTable
+    from kandiga_b200.quant import quantize_affine
+    E, H, I, K, T = 256, 2048, 512, 8, 512
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(77)
+    mats = []
+    for rows, cols in ((I, H), (I, H), (H, I)):
+        ws, ss, bs = [], [], []
+        for _ in range(0, E, 64):
+            w = torch.randn(64 * rows, cols, generator=g, device=dev) * 0.02
+            p, s, b = quantize_affine(w, 4, 64, "f16")
+            ws.append(p.reshape(64, rows, -1))
+            ss.append(s.reshape(64, rows, -1))
+            bs.append(b.reshape(64, rows, -1))
+        mats.append((torch.cat(ws).contiguous(), torch.cat(ss).view(torch.int16).contiguous(),
+                     torch.cat(bs).view(torch.int16).contiguous()))
+    t = ExpertTable(1, E, H, I, 4, "f16")
+    t.load_mlx(0, *mats)
+    x = torch.randn(T, H, generator=g, device=dev).half()
+    logits = torch.randn(T, E, generator=g, device=dev)
+    a = t.moe(0, x, logits=logits, top_k=K, per_k=True, combine=True, out_dtype=torch.float32, path="prefill")
+    b = t.moe(0, x, logits=logits, top_k=K, per_k=True, combine=True, out_dtype=torch.float32, path="prefill")
+    assert t.status() == 0
+    assert torch.equal(a["out"], b["out"]) and torch.equal(a["per_k"], b["per_k"])
+    d = t.moe(0, x, logits=logits, top_k=K, combine=True, out_dtype=torch.float32, path="decode")["out"]
+    assert rel_l2(a["out"].cpu().numpy(), d.cpu().numpy()) < RTOL_L2
+    rows = [0, 257, 511]
+    idx = a["idx"].cpu().numpy()[rows]
+    ids = np.unique(idx)
+    remap = {int(e): i for i, e in enumerate(ids)}
+    sel = torch.from_numpy(ids.astype(np.int64)).to(dev)
+    sub = O.ExpertLayer(4, H, I, [m[0][sel].cpu().numpy().view(np.uint32) for m in mats],
+                        [m[1][sel].cpu().numpy().view(np.uint16) for m in mats],
+                        [m[2][sel].cpu().numpy().view(np.uint16) for m in mats], "f16", "silu")
+    y = sub.moe(x.float().cpu().numpy()[rows], np.vectorize(remap.get)(idx).astype(np.int32))
+    pk = a["per_k"].float().cpu().numpy()[rows]
+    worst = max(rel_l2(pk[i, k], y[i, k]) for i in range(len(rows)) for k in range(K))
+    assert worst < RTOL_L2, worst
