@@ -237,6 +237,49 @@ int kq_qmat_unpack_mlx(const kq_qmat* m, int which, void* weight, void* scales, 
 int kq_dense_gemv(const kq_qmat* m, const void* x, int x_dtype, int T, const void* norm_w,
                   float eps, int activation, void* y, int y_dtype, void* stream);
 
+/* ---- TurboQuant KV cache (PolarQuant 3-bit + 1-bit QJL) ----------------------- */
+
+/* A compressed K/V cache of `batch` x `num_heads` x capacity vectors of
+ * head_dim (64 or 128) elements.  replaces TurboQuantCache
+ * (kandiga/kv_compress.py:22-57): `rotation` (R, x_rot = x R) and `qjl`
+ * (P) are the caller's D x D fp32 host matrices, built as in
+ * kandiga/kv_compress.py:34-44.  Per vector the cache holds, for K and for V,
+ * one nibble per element (3-bit code | QJL sign << 3) and fp32 scale and zero
+ * (the reference's int8 codes, int8 signs, fp32 scales/zeros, packed). */
+typedef struct kq_tq_cache kq_tq_cache;
+#define KQ_ERR_CAPACITY 8
+
+int kq_tq_create(int head_dim, int num_heads, int batch, int capacity, const float* rotation, const float* qjl,
+                 kq_tq_cache** out);
+int kq_tq_destroy(kq_tq_cache* c);
+int kq_tq_seq_len(const kq_tq_cache* c);
+int kq_tq_capacity(const kq_tq_cache* c);
+/* Grow the capacity to at least `capacity` vectors per head, keeping the contents. */
+int kq_tq_reserve(kq_tq_cache* c, int capacity, void* stream);
+/* Compress T new tokens of keys and values ([batch][heads][T][head_dim] in
+ * dtype KQ_DT_*, device) onto the end of the cache: rotate, uniform 3-bit
+ * quantize per vector, residual, QJL sign sketch (kandiga/kv_compress.py:59-92,
+ * 120-150).  KQ_ERR_CAPACITY if the tokens do not fit. */
+int kq_tq_append(kq_tq_cache* c, const void* keys, const void* values, int dtype, int T, void* stream);
+/* Reconstruct all cached keys (which = 0) or values (1) as fp16
+ * [batch][heads][seq_len][head_dim] (kandiga/kv_compress.py:94-118, 152-168). */
+int kq_tq_dequant(const kq_tq_cache* c, int which, void* out_f16, void* stream);
+/* Unpacked codes/signs (int8 [batch][heads][seq_len][head_dim]) and fp32
+ * scales/zeros ([batch][heads][seq_len]) of K (0) or V (1), the reference's
+ * storage layout; any pointer may be NULL. */
+int kq_tq_export(const kq_tq_cache* c, int which, int8_t* codes, int8_t* signs, float* scales, float* zeros,
+                 void* stream);
+/* Single-query attention over the compressed cache: q [batch][q_heads][head_dim]
+ * (q_heads a multiple of num_heads, grouped-query), out fp32 [batch][q_heads][head_dim]
+ * = softmax(q K^T / sqrt(D)) V with K, V the reconstructions.  Scores are taken
+ * on the codes in the rotated domain, values are accumulated there and
+ * un-rotated once.  `scores` (fp32 [batch][q_heads][seq_len], the scaled
+ * logits) may be NULL.  No counterpart in the reference, which dequantizes
+ * the whole cache for MLX attention. */
+size_t kq_tq_attend_workspace_size(const kq_tq_cache* c, int q_heads);
+int kq_tq_attend(const kq_tq_cache* c, const void* q, int q_dtype, int q_heads, float* out, float* scores,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- tensor-core building block ---------------------------------------------- */
 
 /* C[M][N] (fp32) = A[M][K] * B[N][K]^T with fp16 A, B (K contiguous), on the

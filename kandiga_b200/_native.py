@@ -16,7 +16,9 @@ c_u32p = ctypes.POINTER(ctypes.c_uint32)
 
 KQ_OK = 0
 ERRORS = {1: "KQ_ERR_ARG", 2: "KQ_ERR_CUDA", 3: "KQ_ERR_ALLOC", 4: "KQ_ERR_IO", 5: "KQ_ERR_FORMAT",
-          6: "KQ_ERR_UNSUPPORTED", 7: "KQ_ERR_WORKSPACE"}
+          6: "KQ_ERR_UNSUPPORTED", 7: "KQ_ERR_WORKSPACE", 8: "KQ_ERR_CAPACITY"}
+KQ_ERR_CAPACITY = 8
+ERRORS_INV = {v: k for k, v in ERRORS.items()}
 DT_F16, DT_BF16, DT_F32 = 0, 1, 2
 ACT_SILU, ACT_GELU_TANH = 0, 1
 DEV_BAD_EXPERT, DEV_WAIT_TIMEOUT, DEV_BAD_INDEX = 1, 2, 4
@@ -80,6 +82,16 @@ SIGNATURES = {
     "kq_gemm_f16_tc": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "kq_dense_gemv": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_float, c_int, c_void_p, c_int,
                               c_void_p]),
+    "kq_tq_create": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p, ctypes.POINTER(c_void_p)]),
+    "kq_tq_destroy": (c_int, [c_void_p]),
+    "kq_tq_seq_len": (c_int, [c_void_p]),
+    "kq_tq_capacity": (c_int, [c_void_p]),
+    "kq_tq_reserve": (c_int, [c_void_p, c_int, c_void_p]),
+    "kq_tq_append": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "kq_tq_dequant": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
+    "kq_tq_export": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "kq_tq_attend_workspace_size": (c_size_t, [c_void_p, c_int]),
+    "kq_tq_attend": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
 }
 
 _lib = None

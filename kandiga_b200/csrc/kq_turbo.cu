@@ -1,0 +1,695 @@
+// kq_turbo.cu -- TurboQuant KV cache (PolarQuant 3-bit + 1-bit QJL) on sm_100a.
+//
+// The reference (kandiga/kv_compress.py:22-168) keeps int8 codes, int8 signs
+// and fp32 scales/zeros in MLX arrays, grows them with a concatenate per
+// append, and dequantizes the whole cache for every attention call.  Here:
+//
+//   tq_append_kernel   one pass per new vector: x R (D x D fp32, R and P staged
+//                      in shared memory, 8 vectors per warp share every R/P
+//                      load), per-vector min/max, 3-bit codes, residual,
+//                      residual P, signs; packed as one nibble per element
+//                      (code | sign << 3) into a preallocated cache.
+//   tq_dequant_kernel  the reference's reconstruction ((q s + z) +- s/4) R^T
+//                      -> fp16, for the `keys` / `values` accessors.
+//   tq_attend_kernel   single-query attention straight on the codes, split
+//                      over the sequence (flash-decoding): with q' = q R,
+//                      q.K_t = s_t (q'.c_t) + z_t sum(q') + (s_t/4) (q'.(2 sigma_t - 1)),
+//                      values accumulated in the rotated domain;
+//   tq_combine_kernel  merges the per-chunk softmax partials and un-rotates
+//                      once per query head: out = (sum p V~) R^T.
+//
+// Arithmetic that the reference fixes (kandiga/kv_compress.py:75-88) is done
+// with explicitly rounded operations (no contraction): scale = (max - min) / 7,
+// q = clip(round_half_even((r - min) / scale), 0, 7), dequant = q * scale + min,
+// residual = r - dequant.  The two D x D products use fp32 FMA chains, whose
+// summation order differs from a BLAS sgemm: codes can differ from a CPU
+// restatement only where a value sits on a rounding boundary.
+#include <cstdio>
+#include <cstring>
+
+#include "kq_internal.h"
+#include "kq_common.cuh"
+
+namespace kq {
+
+constexpr int TQ_VPW = 8;    // vectors per warp per pass (append / dequant)
+constexpr int TQ_WARPS = 8;  // warps per CTA (append / dequant)
+
+struct TqVecParams {
+    const void* src[2];  // append: keys, values [B][H][T][D]
+    int dtype;
+    int B, H, T, cap, len;  // append: T new tokens written at len; dequant: T = len
+    const float* R;
+    const float* P;
+    uint8_t* packed[2];
+    float* scale[2];
+    float* zero[2];
+    __half* out;  // dequant output [B][H][len][D]
+    int which;    // dequant: 0 = K, 1 = V
+};
+
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// acc[v][c] = sum_d xs[v][d] * M[d][lane * CPL + c], M row-major D x D in shared memory
+template <int D, int NV>
+__device__ __forceinline__ void warp_matvec(const float* M, const float* xs, int lane, float (&acc)[NV][D / 32]) {
+    constexpr int CPL = D / 32;
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) acc[v][c] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < D; ++d) {
+        float r[CPL];
+        if constexpr (CPL == 4) {
+            const float4 t = *reinterpret_cast<const float4*>(M + d * D + lane * 4);
+            r[0] = t.x;
+            r[1] = t.y;
+            r[2] = t.z;
+            r[3] = t.w;
+        } else {
+            const float2 t = *reinterpret_cast<const float2*>(M + d * D + lane * 2);
+            r[0] = t.x;
+            r[1] = t.y;
+        }
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            const float xv = xs[v * D + d];
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) acc[v][c] = fmaf(xv, r[c], acc[v][c]);
+        }
+    }
+}
+
+template <int D>
+__global__ void __launch_bounds__(TQ_WARPS * 32, 1) tq_append_kernel(TqVecParams p) {
+    constexpr int CPL = D / 32;
+    extern __shared__ float4 tq_sm[];
+    float* sR = reinterpret_cast<float*>(tq_sm);
+    float* sP = sR + D * D;
+    float* xs = sP + D * D + (threadIdx.x >> 5) * TQ_VPW * D;
+    for (int i = threadIdx.x; i < D * D / 4; i += blockDim.x) {
+        reinterpret_cast<float4*>(sR)[i] = reinterpret_cast<const float4*>(p.R)[i];
+        reinterpret_cast<float4*>(sP)[i] = reinterpret_cast<const float4*>(p.P)[i];
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long per = (long)p.B * p.H * p.T;
+    const long nvec = 2 * per;
+    const long stride = (long)gridDim.x * TQ_WARPS * TQ_VPW;
+    for (long v0 = ((long)blockIdx.x * TQ_WARPS + warp) * TQ_VPW; v0 < nvec; v0 += stride) {
+#pragma unroll
+        for (int v = 0; v < TQ_VPW; ++v) {
+            const long vi = v0 + v;
+            if (vi < nvec) {
+                const int which = vi >= per ? 1 : 0;
+                const size_t base = (size_t)(vi - which * per) * D;
+                const void* src = which ? p.src[1] : p.src[0];
+                for (int d = lane; d < D; d += 32) xs[v * D + d] = load_as_float(src, p.dtype, base + d);
+            } else {
+                for (int d = lane; d < D; d += 32) xs[v * D + d] = 0.f;
+            }
+        }
+        __syncwarp();
+        float acc[TQ_VPW][CPL];
+        warp_matvec<D, TQ_VPW>(sR, xs, lane, acc);  // rotated = x R
+        __syncwarp();
+        float vscale[TQ_VPW], vmin[TQ_VPW];
+        uint32_t codes[TQ_VPW];
+#pragma unroll
+        for (int v = 0; v < TQ_VPW; ++v) {
+            float mn = acc[v][0], mx = acc[v][0];
+#pragma unroll
+            for (int c = 1; c < CPL; ++c) {
+                mn = fminf(mn, acc[v][c]);
+                mx = fmaxf(mx, acc[v][c]);
+            }
+            mn = warp_min(mn);
+            mx = warp_max(mx);
+            float scale = __fdiv_rn(__fsub_rn(mx, mn), 7.f);
+            if (scale == 0.f) scale = 1.f;
+            uint32_t cw = 0;
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) {
+                float q = rintf(__fdiv_rn(__fsub_rn(acc[v][c], mn), scale));
+                q = fminf(fmaxf(q, 0.f), 7.f);
+                const float deq = __fadd_rn(__fmul_rn(q, scale), mn);
+                xs[v * D + lane * CPL + c] = __fsub_rn(acc[v][c], deq);  // residual
+                cw |= (uint32_t)q << (4 * c);
+            }
+            codes[v] = cw;
+            vscale[v] = scale;
+            vmin[v] = mn;
+        }
+        __syncwarp();
+        warp_matvec<D, TQ_VPW>(sP, xs, lane, acc);  // residual P
+#pragma unroll
+        for (int v = 0; v < TQ_VPW; ++v) {
+            const long vi = v0 + v;
+            if (vi >= nvec) break;
+            const int which = vi >= per ? 1 : 0;
+            const long r = vi - which * per;  // (b H + h) T + t
+            const size_t slot = (size_t)(r / p.T) * p.cap + p.len + (size_t)(r % p.T);
+            uint32_t cw = codes[v];
+#pragma unroll
+            for (int c = 0; c < CPL; ++c)
+                if (acc[v][c] > 0.f) cw |= 8u << (4 * c);
+            uint8_t* dst = (which ? p.packed[1] : p.packed[0]) + slot * (D / 2) + lane * (CPL / 2);
+            if constexpr (CPL == 4)
+                *reinterpret_cast<uint16_t*>(dst) = (uint16_t)cw;
+            else
+                *dst = (uint8_t)cw;
+            if (lane == 0) {
+                (which ? p.scale[1] : p.scale[0])[slot] = vscale[v];
+                (which ? p.zero[1] : p.zero[0])[slot] = vmin[v];
+            }
+        }
+        __syncwarp();
+    }
+}
+
+template <int D>
+__global__ void __launch_bounds__(TQ_WARPS * 32, 1) tq_dequant_kernel(TqVecParams p) {
+    constexpr int CPL = D / 32;
+    extern __shared__ float4 tq_sm[];
+    float* sRT = reinterpret_cast<float*>(tq_sm);  // R^T
+    float* xs = sRT + D * D + (threadIdx.x >> 5) * TQ_VPW * D;
+    for (int i = threadIdx.x; i < D * D; i += blockDim.x) sRT[(i % D) * D + i / D] = p.R[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long nvec = (long)p.B * p.H * p.len;
+    const long stride = (long)gridDim.x * TQ_WARPS * TQ_VPW;
+    const uint8_t* packed = p.which ? p.packed[1] : p.packed[0];
+    const float* scale = p.which ? p.scale[1] : p.scale[0];
+    const float* zero = p.which ? p.zero[1] : p.zero[0];
+    for (long v0 = ((long)blockIdx.x * TQ_WARPS + warp) * TQ_VPW; v0 < nvec; v0 += stride) {
+#pragma unroll
+        for (int v = 0; v < TQ_VPW; ++v) {
+            const long vi = v0 + v;
+            if (vi < nvec) {
+                const size_t slot = (size_t)(vi / p.len) * p.cap + (size_t)(vi % p.len);
+                const uint8_t* src = packed + slot * (D / 2) + lane * (CPL / 2);
+                const uint32_t cw = CPL == 4 ? (uint32_t)*reinterpret_cast<const uint16_t*>(src) : (uint32_t)*src;
+                const float s = scale[slot], z = zero[slot];
+                const float corr = __fdiv_rn(s, 4.f);
+#pragma unroll
+                for (int c = 0; c < CPL; ++c) {
+                    const uint32_t nib = (cw >> (4 * c)) & 15u;
+                    const float deq = __fadd_rn(__fmul_rn((float)(nib & 7u), s), z);
+                    xs[v * D + lane * CPL + c] = __fadd_rn(deq, (nib & 8u) ? corr : -corr);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < CPL; ++c) xs[v * D + lane * CPL + c] = 0.f;
+            }
+        }
+        __syncwarp();
+        float acc[TQ_VPW][CPL];
+        warp_matvec<D, TQ_VPW>(sRT, xs, lane, acc);  // corrected R^T
+#pragma unroll
+        for (int v = 0; v < TQ_VPW; ++v) {
+            const long vi = v0 + v;
+            if (vi >= nvec) break;
+            __half* o = p.out + (size_t)vi * D + lane * CPL;
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) o[c] = __float2half_rn(acc[v][c]);
+        }
+        __syncwarp();
+    }
+}
+
+__global__ void tq_export_kernel(const uint8_t* __restrict__ packed, const float* __restrict__ scale,
+                                 const float* __restrict__ zero, int D, int BH, int cap, int len, int8_t* codes,
+                                 int8_t* signs, float* scales, float* zeros) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;  // element index [BH][len][D]
+    const long n = (long)BH * len * D;
+    if (i >= n) return;
+    const long vec = i / D;
+    const int d = (int)(i % D);
+    const size_t slot = (size_t)(vec / len) * cap + (size_t)(vec % len);
+    const uint32_t nib = (packed[slot * (D / 2) + d / 2] >> (4 * (d & 1))) & 15u;
+    if (codes) codes[i] = (int8_t)(nib & 7u);
+    if (signs) signs[i] = (int8_t)(nib >> 3);
+    if (d == 0) {
+        if (scales) scales[vec] = scale[slot];
+        if (zeros) zeros[vec] = zero[slot];
+    }
+}
+
+// ---- attention ---------------------------------------------------------------------------------
+
+constexpr int TQ_ATT_THREADS = 128;
+constexpr int TQ_CHUNK = 512;  // tokens per CTA
+constexpr int TQ_MAXG = 8;     // query heads per KV head
+
+struct TqAttParams {
+    const uint8_t* packed[2];
+    const float* scale[2];
+    const float* zero[2];
+    const float* R;
+    const void* q;
+    int q_dtype;
+    int B, H, G, cap, len, nchunk;
+    float* part;    // [B][Hq][nchunk][D + 2]: sum p V~ (rotated), chunk max, sum p
+    float* scores;  // [B][Hq][len] or null
+    float* out;     // [B][Hq][D]
+};
+
+template <int D>
+__global__ void __launch_bounds__(TQ_ATT_THREADS) tq_attend_kernel(TqAttParams p) {
+    constexpr int TPT = D / 16;                    // threads per token (16 elements = 8 packed bytes each)
+    constexpr int TPP = TQ_ATT_THREADS / TPT;      // tokens per pass
+    constexpr int NW = TQ_ATT_THREADS / 32;
+    __shared__ float qr[TQ_MAXG][D];
+    __shared__ float qsum[TQ_MAXG];
+    __shared__ float sc[TQ_MAXG][TQ_CHUNK];
+    __shared__ float accs[TPP][D];
+    __shared__ float red[NW];
+    __shared__ float bval;
+    const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int sub = tid % TPT, slot = tid / TPT;
+    const int G = p.G, Hq = p.H * G;
+    const int t0 = chunk * TQ_CHUNK, t1 = min(t0 + TQ_CHUNK, p.len);
+    const size_t bh = (size_t)b * p.H + h;
+    const float sqrt_d = sqrtf((float)D);
+
+    // rotated queries q' = q R and their sums
+    for (int g = 0; g < G; ++g) {
+        const size_t qoff = ((size_t)b * Hq + (size_t)h * G + g) * D;
+        for (int j = tid; j < D; j += TQ_ATT_THREADS) {
+            float a = 0.f;
+            for (int d = 0; d < D; ++d) a = fmaf(load_as_float(p.q, p.q_dtype, qoff + d), p.R[d * D + j], a);
+            qr[g][j] = a;
+        }
+    }
+    __syncthreads();
+    if (tid < G) {
+        float s = 0.f;
+        for (int j = 0; j < D; ++j) s += qr[tid][j];
+        qsum[tid] = s;
+    }
+    __syncthreads();
+
+    // scores on the codes
+    const int npass = (t1 - t0 + TPP - 1) / TPP;
+    for (int i = 0; i < npass; ++i) {
+        const int t = t0 + i * TPP + slot;
+        const bool act = t < t1;
+        const size_t vs = bh * p.cap + (size_t)(act ? t : t0);
+        const uint2 pk = *reinterpret_cast<const uint2*>(p.packed[0] + vs * (D / 2) + sub * 8);
+        const float s = p.scale[0][vs], lo = p.zero[0][vs];
+        for (int g = 0; g < G; ++g) {
+            float dc = 0.f, ds = 0.f;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const uint32_t nib = ((e < 8 ? pk.x : pk.y) >> (4 * (e & 7))) & 15u;
+                const float qv = qr[g][sub * 16 + e];
+                dc = fmaf(qv, (float)(nib & 7u), dc);
+                ds += (nib & 8u) ? qv : -qv;
+            }
+#pragma unroll
+            for (int o = TPT / 2; o > 0; o >>= 1) {
+                dc += __shfl_xor_sync(0xffffffffu, dc, o);
+                ds += __shfl_xor_sync(0xffffffffu, ds, o);
+            }
+            const float score = __fdiv_rn(fmaf(s, dc, fmaf(lo, qsum[g], 0.25f * s * ds)), sqrt_d);
+            if (act && sub == 0) {
+                sc[g][t - t0] = score;
+                if (p.scores) p.scores[((size_t)b * Hq + (size_t)h * G + g) * p.len + t] = score;
+            }
+        }
+    }
+    __syncthreads();
+
+    const int n = t1 - t0;
+    for (int g = 0; g < G; ++g) {
+        // chunk max and exponentials
+        float m = -INFINITY;
+        for (int i = tid; i < n; i += TQ_ATT_THREADS) m = fmaxf(m, sc[g][i]);
+        m = warp_max(m);
+        if (lane == 0) red[wid] = m;
+        __syncthreads();
+        if (tid == 0) {
+            float mm = red[0];
+            for (int w = 1; w < NW; ++w) mm = fmaxf(mm, red[w]);
+            bval = mm;
+        }
+        __syncthreads();
+        m = bval;
+        float l = 0.f;
+        for (int i = tid; i < n; i += TQ_ATT_THREADS) {
+            const float e = expf(sc[g][i] - m);
+            sc[g][i] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        __syncthreads();
+        if (lane == 0) red[wid] = l;
+        __syncthreads();
+        if (tid == 0) {
+            float ll = 0.f;
+            for (int w = 0; w < NW; ++w) ll += red[w];
+            bval = ll;
+        }
+        __syncthreads();
+        l = bval;
+
+        // values in the rotated domain: sum_t p_t (s_t c_t + z_t + (s_t/4)(2 sigma_t - 1))
+        float acc[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+        float plo = 0.f;
+        for (int i = 0; i < npass; ++i) {
+            const int t = t0 + i * TPP + slot;
+            if (t >= t1) break;
+            const size_t vs = bh * p.cap + (size_t)t;
+            const uint2 pk = *reinterpret_cast<const uint2*>(p.packed[1] + vs * (D / 2) + sub * 8);
+            const float pt = sc[g][t - t0];
+            const float w1 = pt * p.scale[1][vs], w2 = 0.25f * w1;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const uint32_t nib = ((e < 8 ? pk.x : pk.y) >> (4 * (e & 7))) & 15u;
+                acc[e] = fmaf(w1, (float)(nib & 7u), acc[e]) + ((nib & 8u) ? w2 : -w2);
+            }
+            if (sub == 0) plo = fmaf(pt, p.zero[1][vs], plo);
+        }
+#pragma unroll
+        for (int e = 0; e < 16; ++e) accs[slot][sub * 16 + e] = acc[e];
+        plo = warp_sum(plo);
+        if (lane == 0) red[wid] = plo;
+        __syncthreads();
+        if (tid == 0) {
+            float pl = 0.f;
+            for (int w = 0; w < NW; ++w) pl += red[w];
+            bval = pl;
+        }
+        __syncthreads();
+        float* part = p.part + (((size_t)b * Hq + (size_t)h * G + g) * p.nchunk + chunk) * (D + 2);
+        for (int d = tid; d < D; d += TQ_ATT_THREADS) {
+            float a = bval;
+            for (int sl = 0; sl < TPP; ++sl) a += accs[sl][d];
+            part[d] = a;
+        }
+        if (tid == 0) {
+            part[D] = m;
+            part[D + 1] = l;
+        }
+        __syncthreads();
+    }
+}
+
+template <int D>
+__global__ void __launch_bounds__(D) tq_combine_kernel(TqAttParams p) {
+    __shared__ float orot[D];
+    const int qh = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const int Hq = p.H * p.G;
+    const float* part = p.part + ((size_t)b * Hq + qh) * p.nchunk * (D + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < p.nchunk; ++c) M = fmaxf(M, part[c * (D + 2) + D]);
+    float L = 0.f, A = 0.f;
+    for (int c = 0; c < p.nchunk; ++c) {
+        const float f = expf(part[c * (D + 2) + D] - M);
+        L = fmaf(part[c * (D + 2) + D + 1], f, L);
+        A = fmaf(part[c * (D + 2) + d], f, A);
+    }
+    orot[d] = A / L;
+    __syncthreads();
+    float o = 0.f;  // un-rotate: out[d] = sum_k orot[k] R^T[k][d] = sum_k orot[k] R[d][k]
+    for (int k = 0; k < D; ++k) o = fmaf(orot[k], p.R[d * D + k], o);
+    p.out[((size_t)b * Hq + qh) * D + d] = o;
+}
+
+// ---- host ----------------------------------------------------------------------------------------
+
+static void free_planes(kq_tq_cache* c) {
+    for (int w = 0; w < 2; ++w) {
+        cudaFree(c->packed[w]);
+        cudaFree(c->scale[w]);
+        cudaFree(c->zero[w]);
+        c->packed[w] = nullptr;
+        c->scale[w] = c->zero[w] = nullptr;
+    }
+}
+
+static bool alloc_planes(const kq_tq_cache* c, int cap, uint8_t* (&packed)[2], float* (&scale)[2],
+                         float* (&zero)[2]) {
+    const size_t nv = (size_t)c->B * c->H * (size_t)(cap > 0 ? cap : 1);
+    for (int w = 0; w < 2; ++w) {
+        packed[w] = nullptr;
+        scale[w] = zero[w] = nullptr;
+    }
+    for (int w = 0; w < 2; ++w) {
+        if (cudaMalloc(&packed[w], nv * (c->D / 2)) != cudaSuccess || cudaMalloc(&scale[w], nv * 4) != cudaSuccess ||
+            cudaMalloc(&zero[w], nv * 4) != cudaSuccess) {
+            for (int v = 0; v < 2; ++v) {
+                cudaFree(packed[v]);
+                cudaFree(scale[v]);
+                cudaFree(zero[v]);
+            }
+            return false;
+        }
+    }
+    return true;
+}
+
+static int sm_count() {
+    int dev = 0, n = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+
+template <typename K>
+static cudaError_t smem_attr_once(K kern, size_t smem, int* configured) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if ((size_t)configured[dev] >= smem) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) configured[dev] = (int)smem;
+    return e;
+}
+
+template <int D>
+static cudaError_t launch_append(const TqVecParams& p, cudaStream_t s) {
+    static int configured[64] = {0};
+    const size_t smem = ((size_t)2 * D * D + (size_t)TQ_WARPS * TQ_VPW * D) * 4;
+    cudaError_t e = smem_attr_once(tq_append_kernel<D>, smem, configured);
+    if (e != cudaSuccess) return e;
+    const long nvec = 2L * p.B * p.H * p.T;
+    const long per_cta = (long)TQ_WARPS * TQ_VPW;
+    const int grid = (int)std::min<long>((nvec + per_cta - 1) / per_cta, (long)sm_count());
+    tq_append_kernel<D><<<grid, TQ_WARPS * 32, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
+template <int D>
+static cudaError_t launch_dequant(const TqVecParams& p, cudaStream_t s) {
+    static int configured[64] = {0};
+    const size_t smem = ((size_t)D * D + (size_t)TQ_WARPS * TQ_VPW * D) * 4;
+    cudaError_t e = smem_attr_once(tq_dequant_kernel<D>, smem, configured);
+    if (e != cudaSuccess) return e;
+    const long nvec = (long)p.B * p.H * p.len;
+    const long per_cta = (long)TQ_WARPS * TQ_VPW;
+    const int grid = (int)std::min<long>((nvec + per_cta - 1) / per_cta, (long)sm_count());
+    tq_dequant_kernel<D><<<grid, TQ_WARPS * 32, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace kq
+
+using namespace kq;
+
+extern "C" int kq_tq_create(int head_dim, int num_heads, int batch, int capacity, const float* rotation,
+                            const float* qjl, kq_tq_cache** out) {
+    if (!out) return KQ_ERR_ARG;
+    *out = nullptr;
+    if ((head_dim != 64 && head_dim != 128) || num_heads <= 0 || batch <= 0 || capacity < 0 || !rotation || !qjl)
+        return KQ_ERR_ARG;
+    kq_tq_cache* c = new (std::nothrow) kq_tq_cache();
+    if (!c) return KQ_ERR_ALLOC;
+    c->D = head_dim;
+    c->H = num_heads;
+    c->B = batch;
+    const size_t mb = (size_t)head_dim * head_dim * 4;
+    if (cudaMalloc(&c->R, mb) != cudaSuccess || cudaMalloc(&c->P, mb) != cudaSuccess ||
+        !alloc_planes(c, capacity, c->packed, c->scale, c->zero)) {
+        cudaFree(c->R);
+        cudaFree(c->P);
+        delete c;
+        return KQ_ERR_ALLOC;
+    }
+    c->cap = capacity;
+    if (cudaMemcpy(c->R, rotation, mb, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(c->P, qjl, mb, cudaMemcpyHostToDevice) != cudaSuccess) {
+        kq_tq_destroy(c);
+        return KQ_ERR_CUDA;
+    }
+    *out = c;
+    return KQ_OK;
+}
+
+extern "C" int kq_tq_destroy(kq_tq_cache* c) {
+    if (!c) return KQ_OK;
+    free_planes(c);
+    cudaFree(c->R);
+    cudaFree(c->P);
+    delete c;
+    return KQ_OK;
+}
+
+extern "C" int kq_tq_seq_len(const kq_tq_cache* c) { return c ? c->len : -1; }
+extern "C" int kq_tq_capacity(const kq_tq_cache* c) { return c ? c->cap : -1; }
+
+extern "C" int kq_tq_reserve(kq_tq_cache* c, int capacity, void* stream) {
+    if (!c || capacity < 0) return KQ_ERR_ARG;
+    if (capacity <= c->cap) return KQ_OK;
+    uint8_t* packed[2];
+    float *scale[2], *zero[2];
+    if (!alloc_planes(c, capacity, packed, scale, zero)) return KQ_ERR_ALLOC;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t rows = (size_t)c->B * c->H;
+    bool ok = true;
+    if (c->len > 0) {
+        for (int w = 0; w < 2 && ok; ++w) {
+            const size_t pb = (size_t)c->D / 2;
+            ok = cudaMemcpy2DAsync(packed[w], capacity * pb, c->packed[w], c->cap * pb, c->len * pb, rows,
+                                   cudaMemcpyDeviceToDevice, s) == cudaSuccess &&
+                 cudaMemcpy2DAsync(scale[w], capacity * 4, c->scale[w], c->cap * 4ull, c->len * 4ull, rows,
+                                   cudaMemcpyDeviceToDevice, s) == cudaSuccess &&
+                 cudaMemcpy2DAsync(zero[w], capacity * 4, c->zero[w], c->cap * 4ull, c->len * 4ull, rows,
+                                   cudaMemcpyDeviceToDevice, s) == cudaSuccess;
+        }
+    }
+    if (ok) ok = cudaStreamSynchronize(s) == cudaSuccess;
+    if (!ok) {
+        for (int w = 0; w < 2; ++w) {
+            cudaFree(packed[w]);
+            cudaFree(scale[w]);
+            cudaFree(zero[w]);
+        }
+        return KQ_ERR_CUDA;
+    }
+    free_planes(c);
+    for (int w = 0; w < 2; ++w) {
+        c->packed[w] = packed[w];
+        c->scale[w] = scale[w];
+        c->zero[w] = zero[w];
+    }
+    c->cap = capacity;
+    return KQ_OK;
+}
+
+extern "C" int kq_tq_append(kq_tq_cache* c, const void* keys, const void* values, int dtype, int T, void* stream) {
+    if (!c || T < 0) return KQ_ERR_ARG;
+    if (dtype != KQ_DT_F16 && dtype != KQ_DT_BF16 && dtype != KQ_DT_F32) return KQ_ERR_ARG;
+    if (T == 0) return KQ_OK;
+    if (!keys || !values) return KQ_ERR_ARG;
+    if ((long)c->len + T > c->cap) return KQ_ERR_CAPACITY;
+    TqVecParams p{};
+    p.src[0] = keys;
+    p.src[1] = values;
+    p.dtype = dtype;
+    p.B = c->B;
+    p.H = c->H;
+    p.T = T;
+    p.cap = c->cap;
+    p.len = c->len;
+    p.R = c->R;
+    p.P = c->P;
+    for (int w = 0; w < 2; ++w) {
+        p.packed[w] = c->packed[w];
+        p.scale[w] = c->scale[w];
+        p.zero[w] = c->zero[w];
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const cudaError_t e = c->D == 128 ? launch_append<128>(p, s) : launch_append<64>(p, s);
+    if (e != cudaSuccess) return KQ_ERR_CUDA;
+    c->len += T;
+    return KQ_OK;
+}
+
+extern "C" int kq_tq_dequant(const kq_tq_cache* c, int which, void* out_f16, void* stream) {
+    if (!c || (which != 0 && which != 1)) return KQ_ERR_ARG;
+    if (c->len == 0) return KQ_OK;
+    if (!out_f16) return KQ_ERR_ARG;
+    TqVecParams p{};
+    p.B = c->B;
+    p.H = c->H;
+    p.cap = c->cap;
+    p.len = c->len;
+    p.R = c->R;
+    for (int w = 0; w < 2; ++w) {
+        p.packed[w] = c->packed[w];
+        p.scale[w] = c->scale[w];
+        p.zero[w] = c->zero[w];
+    }
+    p.out = static_cast<__half*>(out_f16);
+    p.which = which;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const cudaError_t e = c->D == 128 ? launch_dequant<128>(p, s) : launch_dequant<64>(p, s);
+    return e == cudaSuccess ? KQ_OK : KQ_ERR_CUDA;
+}
+
+extern "C" int kq_tq_export(const kq_tq_cache* c, int which, int8_t* codes, int8_t* signs, float* scales,
+                            float* zeros, void* stream) {
+    if (!c || (which != 0 && which != 1)) return KQ_ERR_ARG;
+    if (c->len == 0) return KQ_OK;
+    const long n = (long)c->B * c->H * c->len * c->D;
+    const int threads = 256;
+    tq_export_kernel<<<(int)((n + threads - 1) / threads), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+        c->packed[which], c->scale[which], c->zero[which], c->D, c->B * c->H, c->cap, c->len, codes, signs, scales,
+        zeros);
+    return cudaGetLastError() == cudaSuccess ? KQ_OK : KQ_ERR_CUDA;
+}
+
+extern "C" size_t kq_tq_attend_workspace_size(const kq_tq_cache* c, int q_heads) {
+    if (!c || q_heads <= 0) return 0;
+    const size_t nchunk = ((size_t)(c->cap > 0 ? c->cap : 1) + TQ_CHUNK - 1) / TQ_CHUNK;
+    return (size_t)c->B * q_heads * nchunk * (c->D + 2) * 4;
+}
+
+extern "C" int kq_tq_attend(const kq_tq_cache* c, const void* q, int q_dtype, int q_heads, float* out,
+                            float* scores, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!c || !q || !out || q_heads <= 0 || q_heads % c->H) return KQ_ERR_ARG;
+    if (q_dtype != KQ_DT_F16 && q_dtype != KQ_DT_BF16 && q_dtype != KQ_DT_F32) return KQ_ERR_ARG;
+    const int G = q_heads / c->H;
+    if (G > TQ_MAXG) return KQ_ERR_UNSUPPORTED;
+    if (c->len == 0) return KQ_ERR_ARG;  // softmax over an empty sequence
+    const int nchunk = (c->len + TQ_CHUNK - 1) / TQ_CHUNK;
+    const size_t need = (size_t)c->B * q_heads * nchunk * (c->D + 2) * 4;
+    if (!workspace || workspace_bytes < need) return KQ_ERR_WORKSPACE;
+    TqAttParams p{};
+    for (int w = 0; w < 2; ++w) {
+        p.packed[w] = c->packed[w];
+        p.scale[w] = c->scale[w];
+        p.zero[w] = c->zero[w];
+    }
+    p.R = c->R;
+    p.q = q;
+    p.q_dtype = q_dtype;
+    p.B = c->B;
+    p.H = c->H;
+    p.G = G;
+    p.cap = c->cap;
+    p.len = c->len;
+    p.nchunk = nchunk;
+    p.part = static_cast<float*>(workspace);
+    p.scores = scores;
+    p.out = out;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const dim3 grid(nchunk, c->H, c->B), cgrid(q_heads, c->B);
+    if (c->D == 128) {
+        tq_attend_kernel<128><<<grid, TQ_ATT_THREADS, 0, s>>>(p);
+        tq_combine_kernel<128><<<cgrid, 128, 0, s>>>(p);
+    } else {
+        tq_attend_kernel<64><<<grid, TQ_ATT_THREADS, 0, s>>>(p);
+        tq_combine_kernel<64><<<cgrid, 64, 0, s>>>(p);
+    }
+    return cudaGetLastError() == cudaSuccess ? KQ_OK : KQ_ERR_CUDA;
+}

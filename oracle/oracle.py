@@ -441,10 +441,9 @@ class TurboQuantRef:
         kh = self.dequantize(k_codes, k_scale, k_zero, k_signs).astype(np.float32)
         D = q.shape[-1]
         scores = np.einsum("hd,hsd->hs", q.astype(np.float32), kh) / np.float32(math.sqrt(D))
-        scores = scores - scores.max(-1, keepdims=True)
-        p = np.exp(scores)
+        p = np.exp(scores - scores.max(-1, keepdims=True))
         p /= p.sum(-1, keepdims=True)
-        return np.einsum("hs,hsd->hd", p, v.astype(np.float32)), scores
+        return np.einsum("hs,hsd->hd", p, v.astype(np.float32)), scores  # scores: the scaled logits
 
 
 # ---------------------------------------------------------------------------
