@@ -244,7 +244,7 @@ int kq_dense_gemv(const kq_qmat* m, const void* x, int x_dtype, int T, const voi
  * (kandiga/kv_compress.py:22-57): `rotation` (R, x_rot = x R) and `qjl`
  * (P) are the caller's D x D fp32 host matrices, built as in
  * kandiga/kv_compress.py:34-44.  Per vector the cache holds, for K and for V,
- * one nibble per element (3-bit code | QJL sign << 3) and fp32 scale and zero
+ * one nibble per element (3-bit code << 1 | QJL sign) and fp32 scale and zero
  * (the reference's int8 codes, int8 signs, fp32 scales/zeros, packed). */
 typedef struct kq_tq_cache kq_tq_cache;
 #define KQ_ERR_CAPACITY 8

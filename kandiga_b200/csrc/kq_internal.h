@@ -49,8 +49,9 @@ MoeWs moe_ws_layout(const kq_table* t, int T, int K);
 struct kq_tq_cache {
     int D = 0, H = 0, B = 0, cap = 0, len = 0;
     float* R = nullptr;              // [D][D] rotation: x_rot = x R
+    float* RT = nullptr;             // [D][D] R transposed
     float* P = nullptr;              // [D][D] QJL projection
     uint8_t* packed[2] = {nullptr, nullptr};  // K, V: [B][H][cap][D/2], nibble = code | sign << 3
-    float* scale[2] = {nullptr, nullptr};     // [B][H][cap]
+    float* scale[2] = {nullptr, nullptr};     // [B][H][cap] (+ 16 floats of tail padding)
     float* zero[2] = {nullptr, nullptr};
 };

@@ -8,13 +8,14 @@
 //                      in shared memory, 8 vectors per warp share every R/P
 //                      load), per-vector min/max, 3-bit codes, residual,
 //                      residual P, signs; packed as one nibble per element
-//                      (code | sign << 3) into a preallocated cache.
+//                      (code << 1 | sign) into a preallocated cache.
 //   tq_dequant_kernel  the reference's reconstruction ((q s + z) +- s/4) R^T
 //                      -> fp16, for the `keys` / `values` accessors.
 //   tq_attend_kernel   single-query attention straight on the codes, split
-//                      over the sequence (flash-decoding): with q' = q R,
-//                      q.K_t = s_t (q'.c_t) + z_t sum(q') + (s_t/4) (q'.(2 sigma_t - 1)),
-//                      values accumulated in the rotated domain;
+//                      over the sequence (flash-decoding): with q' = q R and
+//                      v = c + sigma/2 (half the stored nibble),
+//                      q.K_t = s_t (q'.v_t) + (z_t - s_t/4) sum(q'),
+//                      values accumulated in the rotated domain the same way;
 //   tq_combine_kernel  merges the per-chunk softmax partials and un-rotates
 //                      once per query head: out = (sum p V~) R^T.
 //
@@ -40,6 +41,7 @@ struct TqVecParams {
     int dtype;
     int B, H, T, cap, len;  // append: T new tokens written at len; dequant: T = len
     const float* R;
+    const float* RT;
     const float* P;
     uint8_t* packed[2];
     float* scale[2];
@@ -92,7 +94,8 @@ __global__ void __launch_bounds__(TQ_WARPS * 32, 1) tq_append_kernel(TqVecParams
     float* sR = reinterpret_cast<float*>(tq_sm);
     float* sP = sR + D * D;
     float* xs = sP + D * D + (threadIdx.x >> 5) * TQ_VPW * D;
-    for (int i = threadIdx.x; i < D * D / 4; i += blockDim.x) {
+#pragma unroll 8
+    for (int i = threadIdx.x; i < D * D / 4; i += blockDim.x) {  // loads of several rows in flight
         reinterpret_cast<float4*>(sR)[i] = reinterpret_cast<const float4*>(p.R)[i];
         reinterpret_cast<float4*>(sP)[i] = reinterpret_cast<const float4*>(p.P)[i];
     }
@@ -139,7 +142,7 @@ __global__ void __launch_bounds__(TQ_WARPS * 32, 1) tq_append_kernel(TqVecParams
                 q = fminf(fmaxf(q, 0.f), 7.f);
                 const float deq = __fadd_rn(__fmul_rn(q, scale), mn);
                 xs[v * D + lane * CPL + c] = __fsub_rn(acc[v][c], deq);  // residual
-                cw |= (uint32_t)q << (4 * c);
+                cw |= (uint32_t)q << (4 * c + 1);
             }
             codes[v] = cw;
             vscale[v] = scale;
@@ -157,7 +160,7 @@ __global__ void __launch_bounds__(TQ_WARPS * 32, 1) tq_append_kernel(TqVecParams
             uint32_t cw = codes[v];
 #pragma unroll
             for (int c = 0; c < CPL; ++c)
-                if (acc[v][c] > 0.f) cw |= 8u << (4 * c);
+                if (acc[v][c] > 0.f) cw |= 1u << (4 * c);
             uint8_t* dst = (which ? p.packed[1] : p.packed[0]) + slot * (D / 2) + lane * (CPL / 2);
             if constexpr (CPL == 4)
                 *reinterpret_cast<uint16_t*>(dst) = (uint16_t)cw;
@@ -178,7 +181,9 @@ __global__ void __launch_bounds__(TQ_WARPS * 32, 1) tq_dequant_kernel(TqVecParam
     extern __shared__ float4 tq_sm[];
     float* sRT = reinterpret_cast<float*>(tq_sm);  // R^T
     float* xs = sRT + D * D + (threadIdx.x >> 5) * TQ_VPW * D;
-    for (int i = threadIdx.x; i < D * D; i += blockDim.x) sRT[(i % D) * D + i / D] = p.R[i];
+#pragma unroll 8
+    for (int i = threadIdx.x; i < D * D / 4; i += blockDim.x)
+        reinterpret_cast<float4*>(sRT)[i] = reinterpret_cast<const float4*>(p.RT)[i];
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long nvec = (long)p.B * p.H * p.len;
@@ -199,8 +204,8 @@ __global__ void __launch_bounds__(TQ_WARPS * 32, 1) tq_dequant_kernel(TqVecParam
 #pragma unroll
                 for (int c = 0; c < CPL; ++c) {
                     const uint32_t nib = (cw >> (4 * c)) & 15u;
-                    const float deq = __fadd_rn(__fmul_rn((float)(nib & 7u), s), z);
-                    xs[v * D + lane * CPL + c] = __fadd_rn(deq, (nib & 8u) ? corr : -corr);
+                    const float deq = __fadd_rn(__fmul_rn((float)(nib >> 1), s), z);
+                    xs[v * D + lane * CPL + c] = __fadd_rn(deq, (nib & 1u) ? corr : -corr);
                 }
             } else {
 #pragma unroll
@@ -232,8 +237,8 @@ __global__ void tq_export_kernel(const uint8_t* __restrict__ packed, const float
     const int d = (int)(i % D);
     const size_t slot = (size_t)(vec / len) * cap + (size_t)(vec % len);
     const uint32_t nib = (packed[slot * (D / 2) + d / 2] >> (4 * (d & 1))) & 15u;
-    if (codes) codes[i] = (int8_t)(nib & 7u);
-    if (signs) signs[i] = (int8_t)(nib >> 3);
+    if (codes) codes[i] = (int8_t)(nib >> 1);
+    if (signs) signs[i] = (int8_t)(nib & 1u);
     if (d == 0) {
         if (scales) scales[vec] = scale[slot];
         if (zeros) zeros[vec] = zero[slot];
@@ -242,8 +247,15 @@ __global__ void tq_export_kernel(const uint8_t* __restrict__ packed, const float
 
 // ---- attention ---------------------------------------------------------------------------------
 
+// Nibble k of w (2c + sigma) as the float 1 + (c + sigma/2)/8: the four bits
+// placed in the mantissa under the exponent of 1.0 (no int-to-float convert).
+__device__ __forceinline__ float nib_1p(uint32_t w, int k) {
+    const uint32_t b = k <= 4 ? (w << (19 - 4 * k)) : (w >> (4 * k - 19));
+    return __uint_as_float((b & 0x00780000u) | 0x3F800000u);
+}
+
 constexpr int TQ_ATT_THREADS = 128;
-constexpr int TQ_CHUNK = 512;  // tokens per CTA
+constexpr int TQ_CHUNK = 256;  // tokens per CTA
 constexpr int TQ_MAXG = 8;     // query heads per KV head
 
 struct TqAttParams {
@@ -251,100 +263,148 @@ struct TqAttParams {
     const float* scale[2];
     const float* zero[2];
     const float* R;
+    const float* RT;
     const void* q;
     int q_dtype;
     int B, H, G, cap, len, nchunk;
+    float* qrot;    // [B][Hq][D + 1]: q R and its sum
     float* part;    // [B][Hq][nchunk][D + 2]: sum p V~ (rotated), chunk max, sum p
     float* scores;  // [B][Hq][len] or null
     float* out;     // [B][Hq][D]
+    uint32_t* status;
 };
 
+// q' = q R and sum(q'), once per query head: 256 threads, thread (half, j)
+// sums half of the rows of column j
+template <int D>
+__global__ void __launch_bounds__(256) tq_rotate_q_kernel(TqAttParams p) {
+    constexpr int SPLIT = 256 / D;
+    __shared__ float qs[D];
+    __shared__ float part[SPLIT][D];
+    __shared__ float red[D / 32];
+    const int qh = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const int j = tid % D, half = tid / D;
+    const int Hq = p.H * p.G;
+    const size_t qoff = ((size_t)b * Hq + qh) * D;
+    if (tid < D) qs[tid] = load_as_float(p.q, p.q_dtype, qoff + tid);
+    __syncthreads();
+    float a = 0.f;
+    const int d0 = half * (D / SPLIT);
+#pragma unroll 16
+    for (int d = d0; d < d0 + D / SPLIT; ++d) a = fmaf(qs[d], p.R[d * D + j], a);
+    part[half][j] = a;
+    __syncthreads();
+    if (tid < D) {
+        float v = 0.f;
+        for (int h2 = 0; h2 < SPLIT; ++h2) v += part[h2][tid];
+        float* dst = p.qrot + ((size_t)b * Hq + qh) * (D + 1);
+        dst[tid] = v;
+        const float w = warp_sum(v);
+        if ((tid & 31) == 0) red[tid >> 5] = w;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float t = 0.f;
+        for (int i = 0; i < D / 32; ++i) t += red[i];
+        p.qrot[((size_t)b * Hq + qh) * (D + 1) + D] = t;
+    }
+}
+
+template <int D>
+__host__ __device__ constexpr size_t tq_att_smem(int G) {
+    // K, V codes + K, V scale/zero + scores + per-slot value partials + q' + barrier
+    return (size_t)2 * TQ_CHUNK * (D / 2) + (size_t)4 * TQ_CHUNK * 4 + (size_t)G * TQ_CHUNK * 4 +
+           (size_t)(TQ_ATT_THREADS / (D / 16)) * D * 4 + (size_t)G * (D + 1) * 4 + 64;
+}
+
+// One CTA per (chunk of TQ_CHUNK tokens, KV head, batch).  Thread 0 brings the
+// chunk's codes, scales and zeros of K and V into shared memory with bulk
+// copies on one mbarrier; every thread then works from shared memory.
 template <int D>
 __global__ void __launch_bounds__(TQ_ATT_THREADS) tq_attend_kernel(TqAttParams p) {
-    constexpr int TPT = D / 16;                    // threads per token (16 elements = 8 packed bytes each)
-    constexpr int TPP = TQ_ATT_THREADS / TPT;      // tokens per pass
+    constexpr int TPT = D / 16;                // threads per token (16 elements = 8 packed bytes each)
+    constexpr int TPP = TQ_ATT_THREADS / TPT;  // tokens per pass
     constexpr int NW = TQ_ATT_THREADS / 32;
-    __shared__ float qr[TQ_MAXG][D];
-    __shared__ float qsum[TQ_MAXG];
-    __shared__ float sc[TQ_MAXG][TQ_CHUNK];
-    __shared__ float accs[TPP][D];
+    constexpr int CB = D / 2;                  // packed bytes per vector
+    extern __shared__ __align__(128) uint8_t att_sm[];
+    const int G = p.G, Hq = p.H * G;
+    uint8_t* kc = att_sm;                                           // [TQ_CHUNK][CB]
+    uint8_t* vc = kc + TQ_CHUNK * CB;
+    float* ksc = reinterpret_cast<float*>(vc + TQ_CHUNK * CB);      // [TQ_CHUNK]
+    float* kze = ksc + TQ_CHUNK;
+    float* vsc = kze + TQ_CHUNK;
+    float* vze = vsc + TQ_CHUNK;
+    float* sc = vze + TQ_CHUNK;                                     // [G][TQ_CHUNK]
+    float* accs = sc + G * TQ_CHUNK;                                // [TPP][D]
+    float* qr = accs + TPP * D;                                     // [G][D + 1]
+    uint64_t* bar = reinterpret_cast<uint64_t*>(qr + G * (D + 1) + 1);  // 8-byte aligned below
+    bar = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(bar) + 7) & ~uintptr_t(7));
     __shared__ float red[NW];
-    __shared__ float bval;
+    __shared__ float cmax[TQ_MAXG], csum[TQ_MAXG];
     const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int sub = tid % TPT, slot = tid / TPT;
-    const int G = p.G, Hq = p.H * G;
     const int t0 = chunk * TQ_CHUNK, t1 = min(t0 + TQ_CHUNK, p.len);
-    const size_t bh = (size_t)b * p.H + h;
+    const int n = t1 - t0;
+    const size_t row = ((size_t)b * p.H + h) * p.cap + t0;
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+        const uint32_t cbytes = (uint32_t)n * CB;              // multiple of 16
+        const uint32_t fbytes = (uint32_t)((n + 3) & ~3) * 4;  // scale / zero rows carry tail padding
+        mbar_expect_tx(bar, 2 * cbytes + 4 * fbytes);
+        const uint64_t pol = policy_evict_first();
+        bulk_g2s(kc, p.packed[0] + row * CB, cbytes, bar, pol);
+        bulk_g2s(vc, p.packed[1] + row * CB, cbytes, bar, pol);
+        bulk_g2s(ksc, p.scale[0] + row, fbytes, bar, pol);
+        bulk_g2s(kze, p.zero[0] + row, fbytes, bar, pol);
+        bulk_g2s(vsc, p.scale[1] + row, fbytes, bar, pol);
+        bulk_g2s(vze, p.zero[1] + row, fbytes, bar, pol);
+    }
+    for (int i = tid; i < G * (D + 1); i += TQ_ATT_THREADS)
+        qr[i] = p.qrot[((size_t)b * Hq + (size_t)h * G) * (D + 1) + i];
+    __syncthreads();
+    mbar_wait(bar, 0, p.status);
     const float sqrt_d = sqrtf((float)D);
 
-    // rotated queries q' = q R and their sums
-    for (int g = 0; g < G; ++g) {
-        const size_t qoff = ((size_t)b * Hq + (size_t)h * G + g) * D;
-        for (int j = tid; j < D; j += TQ_ATT_THREADS) {
-            float a = 0.f;
-            for (int d = 0; d < D; ++d) a = fmaf(load_as_float(p.q, p.q_dtype, qoff + d), p.R[d * D + j], a);
-            qr[g][j] = a;
-        }
-    }
-    __syncthreads();
-    if (tid < G) {
-        float s = 0.f;
-        for (int j = 0; j < D; ++j) s += qr[tid][j];
-        qsum[tid] = s;
-    }
-    __syncthreads();
-
     // scores on the codes
-    const int npass = (t1 - t0 + TPP - 1) / TPP;
+    const int npass = (n + TPP - 1) / TPP;
     for (int i = 0; i < npass; ++i) {
-        const int t = t0 + i * TPP + slot;
-        const bool act = t < t1;
-        const size_t vs = bh * p.cap + (size_t)(act ? t : t0);
-        const uint2 pk = *reinterpret_cast<const uint2*>(p.packed[0] + vs * (D / 2) + sub * 8);
-        const float s = p.scale[0][vs], lo = p.zero[0][vs];
+        const int tl = i * TPP + slot;
+        const int tc = tl < n ? tl : 0;
+        const uint2 pk = *reinterpret_cast<const uint2*>(kc + tc * CB + sub * 8);
+        const float s = ksc[tc], lo = kze[tc];
         for (int g = 0; g < G; ++g) {
-            float dc = 0.f, ds = 0.f;
+            const float* q = qr + g * (D + 1) + sub * 16;
+            // a = sum q (1 + v/8) with v = c + sigma/2; q.v = 8 (a - sum q)
+            float a = 0.f;
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                const uint32_t nib = ((e < 8 ? pk.x : pk.y) >> (4 * (e & 7))) & 15u;
-                const float qv = qr[g][sub * 16 + e];
-                dc = fmaf(qv, (float)(nib & 7u), dc);
-                ds += (nib & 8u) ? qv : -qv;
-            }
+            for (int e = 0; e < 16; ++e) a = fmaf(q[e], nib_1p(e < 8 ? pk.x : pk.y, e & 7), a);
 #pragma unroll
-            for (int o = TPT / 2; o > 0; o >>= 1) {
-                dc += __shfl_xor_sync(0xffffffffu, dc, o);
-                ds += __shfl_xor_sync(0xffffffffu, ds, o);
-            }
-            const float score = __fdiv_rn(fmaf(s, dc, fmaf(lo, qsum[g], 0.25f * s * ds)), sqrt_d);
-            if (act && sub == 0) {
-                sc[g][t - t0] = score;
-                if (p.scores) p.scores[((size_t)b * Hq + (size_t)h * G + g) * p.len + t] = score;
+            for (int o = TPT / 2; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+            const float qs = qr[g * (D + 1) + D];
+            const float score = __fdiv_rn(fmaf(s, 8.f * (a - qs), (lo - 0.25f * s) * qs), sqrt_d);
+            if (tl < n && sub == 0) {
+                sc[g * TQ_CHUNK + tl] = score;
+                if (p.scores) p.scores[((size_t)b * Hq + (size_t)h * G + g) * p.len + t0 + tl] = score;
             }
         }
     }
     __syncthreads();
 
-    const int n = t1 - t0;
     for (int g = 0; g < G; ++g) {
-        // chunk max and exponentials
+        float* sg = sc + g * TQ_CHUNK;
         float m = -INFINITY;
-        for (int i = tid; i < n; i += TQ_ATT_THREADS) m = fmaxf(m, sc[g][i]);
+        for (int i = tid; i < n; i += TQ_ATT_THREADS) m = fmaxf(m, sg[i]);
         m = warp_max(m);
         if (lane == 0) red[wid] = m;
         __syncthreads();
-        if (tid == 0) {
-            float mm = red[0];
-            for (int w = 1; w < NW; ++w) mm = fmaxf(mm, red[w]);
-            bval = mm;
-        }
-        __syncthreads();
-        m = bval;
+        m = red[0];
+        for (int w = 1; w < NW; ++w) m = fmaxf(m, red[w]);
         float l = 0.f;
         for (int i = tid; i < n; i += TQ_ATT_THREADS) {
-            const float e = expf(sc[g][i] - m);
-            sc[g][i] = e;
+            const float e = expf(sg[i] - m);
+            sg[i] = e;
             l += e;
         }
         l = warp_sum(l);
@@ -354,74 +414,99 @@ __global__ void __launch_bounds__(TQ_ATT_THREADS) tq_attend_kernel(TqAttParams p
         if (tid == 0) {
             float ll = 0.f;
             for (int w = 0; w < NW; ++w) ll += red[w];
-            bval = ll;
+            cmax[g] = m;
+            csum[g] = ll;
         }
         __syncthreads();
-        l = bval;
+    }
 
-        // values in the rotated domain: sum_t p_t (s_t c_t + z_t + (s_t/4)(2 sigma_t - 1))
+    // values in the rotated domain: sum_t p_t (s_t c_t + z_t + (s_t/4)(2 sigma_t - 1))
+    for (int g = 0; g < G; ++g) {
+        const float* sg = sc + g * TQ_CHUNK;
         float acc[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) acc[e] = 0.f;
         float plo = 0.f;
         for (int i = 0; i < npass; ++i) {
-            const int t = t0 + i * TPP + slot;
-            if (t >= t1) break;
-            const size_t vs = bh * p.cap + (size_t)t;
-            const uint2 pk = *reinterpret_cast<const uint2*>(p.packed[1] + vs * (D / 2) + sub * 8);
-            const float pt = sc[g][t - t0];
-            const float w1 = pt * p.scale[1][vs], w2 = 0.25f * w1;
+            const int tl = i * TPP + slot;
+            if (tl >= n) break;
+            const uint2 pk = *reinterpret_cast<const uint2*>(vc + tl * CB + sub * 8);
+            const float pt = sg[tl];
+            // p (s c + z + (s/4)(2 sigma - 1)) = p s v + p (z - s/4) = 8 p s (1 + v/8) + p (z - s/4 - 8 s)
+            const float w1 = 8.f * pt * vsc[tl];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                const uint32_t nib = ((e < 8 ? pk.x : pk.y) >> (4 * (e & 7))) & 15u;
-                acc[e] = fmaf(w1, (float)(nib & 7u), acc[e]) + ((nib & 8u) ? w2 : -w2);
-            }
-            if (sub == 0) plo = fmaf(pt, p.zero[1][vs], plo);
+            for (int e = 0; e < 16; ++e) acc[e] = fmaf(w1, nib_1p(e < 8 ? pk.x : pk.y, e & 7), acc[e]);
+            if (sub == 0) plo = fmaf(pt, fmaf(-8.25f, vsc[tl], vze[tl]), plo);
         }
+        __syncthreads();  // accs / red of the previous head are consumed
 #pragma unroll
-        for (int e = 0; e < 16; ++e) accs[slot][sub * 16 + e] = acc[e];
-        plo = warp_sum(plo);
-        if (lane == 0) red[wid] = plo;
+        for (int e = 0; e < 16; ++e) accs[slot * D + sub * 16 + e] = acc[e];
+        const float pl = warp_sum(plo);
+        if (lane == 0) red[wid] = pl;
         __syncthreads();
-        if (tid == 0) {
-            float pl = 0.f;
-            for (int w = 0; w < NW; ++w) pl += red[w];
-            bval = pl;
-        }
-        __syncthreads();
+        float plsum = 0.f;
+        for (int w = 0; w < NW; ++w) plsum += red[w];
         float* part = p.part + (((size_t)b * Hq + (size_t)h * G + g) * p.nchunk + chunk) * (D + 2);
         for (int d = tid; d < D; d += TQ_ATT_THREADS) {
-            float a = bval;
-            for (int sl = 0; sl < TPP; ++sl) a += accs[sl][d];
+            float a = plsum;
+            for (int sl = 0; sl < TPP; ++sl) a += accs[sl * D + d];
             part[d] = a;
         }
         if (tid == 0) {
-            part[D] = m;
-            part[D + 1] = l;
+            part[D] = cmax[g];
+            part[D + 1] = csum[g];
         }
-        __syncthreads();
     }
 }
 
+// Merge the chunk partials of one query head and un-rotate: out = (sum p V~ / sum p) R^T.
+// 256 threads: warp w sums chunks c % 8 == w, lane covers dims lane + 32 i.
 template <int D>
-__global__ void __launch_bounds__(D) tq_combine_kernel(TqAttParams p) {
+__global__ void __launch_bounds__(256) tq_combine_kernel(TqAttParams p) {
+    constexpr int NWC = 8, DPL = D / 32;
     __shared__ float orot[D];
-    const int qh = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    __shared__ float pacc[NWC][D];
+    __shared__ float pl[NWC], pm[NWC];
+    const int qh = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int Hq = p.H * p.G;
     const float* part = p.part + ((size_t)b * Hq + qh) * p.nchunk * (D + 2);
     float M = -INFINITY;
-    for (int c = 0; c < p.nchunk; ++c) M = fmaxf(M, part[c * (D + 2) + D]);
-    float L = 0.f, A = 0.f;
-    for (int c = 0; c < p.nchunk; ++c) {
-        const float f = expf(part[c * (D + 2) + D] - M);
-        L = fmaf(part[c * (D + 2) + D + 1], f, L);
-        A = fmaf(part[c * (D + 2) + d], f, A);
-    }
-    orot[d] = A / L;
+    for (int c = tid; c < p.nchunk; c += 256) M = fmaxf(M, part[(size_t)c * (D + 2) + D]);
+    M = warp_max(M);
+    if (lane == 0) pm[w] = M;
     __syncthreads();
-    float o = 0.f;  // un-rotate: out[d] = sum_k orot[k] R^T[k][d] = sum_k orot[k] R[d][k]
-    for (int k = 0; k < D; ++k) o = fmaf(orot[k], p.R[d * D + k], o);
-    p.out[((size_t)b * Hq + qh) * D + d] = o;
+    M = pm[0];
+    for (int i = 1; i < NWC; ++i) M = fmaxf(M, pm[i]);
+    float L = 0.f, A[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) A[i] = 0.f;
+#pragma unroll 4
+    for (int c = w; c < p.nchunk; c += NWC) {
+        const float* pc = part + (size_t)c * (D + 2);
+        const float f = expf(pc[D] - M);
+        L = fmaf(pc[D + 1], f, L);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) A[i] = fmaf(pc[lane + 32 * i], f, A[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) pacc[w][lane + 32 * i] = A[i];
+    if (lane == 0) pl[w] = L;
+    __syncthreads();
+    if (tid < D) {
+        float a = 0.f, l = 0.f;
+        for (int i = 0; i < NWC; ++i) {
+            a += pacc[i][tid];
+            l += pl[i];
+        }
+        orot[tid] = a / l;
+    }
+    __syncthreads();
+    if (tid < D) {
+        float o = 0.f;  // un-rotate: out[d] = sum_k orot[k] R^T[k][d]
+#pragma unroll 16
+        for (int k = 0; k < D; ++k) o = fmaf(orot[k], p.RT[k * D + tid], o);
+        p.out[((size_t)b * Hq + qh) * D + tid] = o;
+    }
 }
 
 // ---- host ----------------------------------------------------------------------------------------
@@ -438,7 +523,7 @@ static void free_planes(kq_tq_cache* c) {
 
 static bool alloc_planes(const kq_tq_cache* c, int cap, uint8_t* (&packed)[2], float* (&scale)[2],
                          float* (&zero)[2]) {
-    const size_t nv = (size_t)c->B * c->H * (size_t)(cap > 0 ? cap : 1);
+    const size_t nv = (size_t)c->B * c->H * (size_t)(cap > 0 ? cap : 1) + 16;  // tail padding
     for (int w = 0; w < 2; ++w) {
         packed[w] = nullptr;
         scale[w] = zero[w] = nullptr;
@@ -456,6 +541,9 @@ static bool alloc_planes(const kq_tq_cache* c, int cap, uint8_t* (&packed)[2], f
     }
     return true;
 }
+
+// capacities are multiples of 4 vectors so every row of scales / zeros starts 16-byte aligned
+static int round_cap(int cap) { return (cap + 3) & ~3; }
 
 static int sm_count() {
     int dev = 0, n = 148;
@@ -501,6 +589,18 @@ static cudaError_t launch_dequant(const TqVecParams& p, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+template <int D>
+static cudaError_t launch_attend(const TqAttParams& p, dim3 grid, dim3 cgrid, cudaStream_t s) {
+    static int configured[64] = {0};
+    const size_t smem = tq_att_smem<D>(TQ_MAXG);
+    cudaError_t e = smem_attr_once(tq_attend_kernel<D>, smem, configured);
+    if (e != cudaSuccess) return e;
+    tq_rotate_q_kernel<D><<<cgrid, 256, 0, s>>>(p);
+    tq_attend_kernel<D><<<grid, TQ_ATT_THREADS, tq_att_smem<D>(p.G), s>>>(p);
+    tq_combine_kernel<D><<<cgrid, 256, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
 }  // namespace kq
 
 using namespace kq;
@@ -516,16 +616,27 @@ extern "C" int kq_tq_create(int head_dim, int num_heads, int batch, int capacity
     c->D = head_dim;
     c->H = num_heads;
     c->B = batch;
+    capacity = round_cap(capacity);
     const size_t mb = (size_t)head_dim * head_dim * 4;
-    if (cudaMalloc(&c->R, mb) != cudaSuccess || cudaMalloc(&c->P, mb) != cudaSuccess ||
-        !alloc_planes(c, capacity, c->packed, c->scale, c->zero)) {
+    if (cudaMalloc(&c->R, mb) != cudaSuccess || cudaMalloc(&c->RT, mb) != cudaSuccess ||
+        cudaMalloc(&c->P, mb) != cudaSuccess || !alloc_planes(c, capacity, c->packed, c->scale, c->zero)) {
         cudaFree(c->R);
+        cudaFree(c->RT);
         cudaFree(c->P);
         delete c;
         return KQ_ERR_ALLOC;
     }
     c->cap = capacity;
-    if (cudaMemcpy(c->R, rotation, mb, cudaMemcpyHostToDevice) != cudaSuccess ||
+    float* rt = new (std::nothrow) float[(size_t)head_dim * head_dim];
+    if (!rt) {
+        kq_tq_destroy(c);
+        return KQ_ERR_ALLOC;
+    }
+    for (int i = 0; i < head_dim; ++i)
+        for (int j = 0; j < head_dim; ++j) rt[(size_t)j * head_dim + i] = rotation[(size_t)i * head_dim + j];
+    const bool up = cudaMemcpy(c->RT, rt, mb, cudaMemcpyHostToDevice) == cudaSuccess;
+    delete[] rt;
+    if (!up || cudaMemcpy(c->R, rotation, mb, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(c->P, qjl, mb, cudaMemcpyHostToDevice) != cudaSuccess) {
         kq_tq_destroy(c);
         return KQ_ERR_CUDA;
@@ -538,6 +649,7 @@ extern "C" int kq_tq_destroy(kq_tq_cache* c) {
     if (!c) return KQ_OK;
     free_planes(c);
     cudaFree(c->R);
+    cudaFree(c->RT);
     cudaFree(c->P);
     delete c;
     return KQ_OK;
@@ -549,6 +661,7 @@ extern "C" int kq_tq_capacity(const kq_tq_cache* c) { return c ? c->cap : -1; }
 extern "C" int kq_tq_reserve(kq_tq_cache* c, int capacity, void* stream) {
     if (!c || capacity < 0) return KQ_ERR_ARG;
     if (capacity <= c->cap) return KQ_OK;
+    capacity = round_cap(capacity);
     uint8_t* packed[2];
     float *scale[2], *zero[2];
     if (!alloc_planes(c, capacity, packed, scale, zero)) return KQ_ERR_ALLOC;
@@ -624,6 +737,7 @@ extern "C" int kq_tq_dequant(const kq_tq_cache* c, int which, void* out_f16, voi
     p.cap = c->cap;
     p.len = c->len;
     p.R = c->R;
+    p.RT = c->RT;
     for (int w = 0; w < 2; ++w) {
         p.packed[w] = c->packed[w];
         p.scale[w] = c->scale[w];
@@ -651,7 +765,7 @@ extern "C" int kq_tq_export(const kq_tq_cache* c, int which, int8_t* codes, int8
 extern "C" size_t kq_tq_attend_workspace_size(const kq_tq_cache* c, int q_heads) {
     if (!c || q_heads <= 0) return 0;
     const size_t nchunk = ((size_t)(c->cap > 0 ? c->cap : 1) + TQ_CHUNK - 1) / TQ_CHUNK;
-    return (size_t)c->B * q_heads * nchunk * (c->D + 2) * 4;
+    return 16 + (size_t)c->B * q_heads * ((c->D + 1) + nchunk * (c->D + 2)) * 4;
 }
 
 extern "C" int kq_tq_attend(const kq_tq_cache* c, const void* q, int q_dtype, int q_heads, float* out,
@@ -662,7 +776,7 @@ extern "C" int kq_tq_attend(const kq_tq_cache* c, const void* q, int q_dtype, in
     if (G > TQ_MAXG) return KQ_ERR_UNSUPPORTED;
     if (c->len == 0) return KQ_ERR_ARG;  // softmax over an empty sequence
     const int nchunk = (c->len + TQ_CHUNK - 1) / TQ_CHUNK;
-    const size_t need = (size_t)c->B * q_heads * nchunk * (c->D + 2) * 4;
+    const size_t need = 16 + (size_t)c->B * q_heads * ((c->D + 1) + (size_t)nchunk * (c->D + 2)) * 4;
     if (!workspace || workspace_bytes < need) return KQ_ERR_WORKSPACE;
     TqAttParams p{};
     for (int w = 0; w < 2; ++w) {
@@ -671,6 +785,7 @@ extern "C" int kq_tq_attend(const kq_tq_cache* c, const void* q, int q_dtype, in
         p.zero[w] = c->zero[w];
     }
     p.R = c->R;
+    p.RT = c->RT;
     p.q = q;
     p.q_dtype = q_dtype;
     p.B = c->B;
@@ -679,17 +794,15 @@ extern "C" int kq_tq_attend(const kq_tq_cache* c, const void* q, int q_dtype, in
     p.cap = c->cap;
     p.len = c->len;
     p.nchunk = nchunk;
-    p.part = static_cast<float*>(workspace);
+    // workspace: status word (16 B), q R, chunk partials
+    p.status = static_cast<uint32_t*>(workspace);
+    p.qrot = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 16);
+    p.part = p.qrot + (size_t)c->B * q_heads * (c->D + 1);
     p.scores = scores;
     p.out = out;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const dim3 grid(nchunk, c->H, c->B), cgrid(q_heads, c->B);
-    if (c->D == 128) {
-        tq_attend_kernel<128><<<grid, TQ_ATT_THREADS, 0, s>>>(p);
-        tq_combine_kernel<128><<<cgrid, 128, 0, s>>>(p);
-    } else {
-        tq_attend_kernel<64><<<grid, TQ_ATT_THREADS, 0, s>>>(p);
-        tq_combine_kernel<64><<<cgrid, 64, 0, s>>>(p);
-    }
+    cudaError_t e = c->D == 128 ? launch_attend<128>(p, grid, cgrid, s) : launch_attend<64>(p, grid, cgrid, s);
+    if (e != cudaSuccess) return KQ_ERR_CUDA;
     return cudaGetLastError() == cudaSuccess ? KQ_OK : KQ_ERR_CUDA;
 }
