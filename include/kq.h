@@ -237,6 +237,25 @@ int kq_qmat_unpack_mlx(const kq_qmat* m, int which, void* weight, void* scales, 
 int kq_dense_gemv(const kq_qmat* m, const void* x, int x_dtype, int T, const void* norm_w,
                   float eps, int activation, void* y, int y_dtype, void* stream);
 
+/* ---- TQ3_1S dense GEMV --------------------------------------------------------- */
+
+/* A TQ3_1S matrix [rows][cols] (cols % 32 == 0): the reference's block stream
+ * (kandiga/tq3/quantize.py:122-145, 390-461) uploaded unchanged, 20-byte
+ * blocks (fp16 d0 d1 m0 m1 + 12 bytes of 3-bit indices) or the 16-byte
+ * variant without means (kandiga/tq3/quantize.py:483-516). */
+typedef struct kq_tq3_mat kq_tq3_mat;
+int kq_tq3_create(int rows, int cols, int block_bytes, const void* host_blocks, size_t nbytes, kq_tq3_mat** out);
+int kq_tq3_destroy(kq_tq3_mat* m);
+size_t kq_tq3_bytes(const kq_tq3_mat* m);
+/* y[t] = W x[t] (+ bias, fp32 [rows] or NULL) for T tokens: x [T][cols], y [T][rows].
+ * Scores the codes against the Walsh-Hadamard-rotated input (w . x = r . WHT(x)).
+ * replaces tq3_gemv (kandiga/tq3/fused_kernel.py:289-341) and TQ3Linear.forward
+ * (kandiga/tq3/engine.py:61-73). */
+int kq_tq3_gemv(const kq_tq3_mat* m, const void* x, int x_dtype, int T, const float* bias, void* y, int y_dtype,
+                void* stream);
+/* Reconstructed weights, fp32 [rows][cols] (kandiga/tq3/quantize.py:483-516). */
+int kq_tq3_dequant(const kq_tq3_mat* m, float* w, void* stream);
+
 /* ---- TurboQuant KV cache (PolarQuant 3-bit + 1-bit QJL) ----------------------- */
 
 /* A compressed K/V cache of `batch` x `num_heads` x capacity vectors of

@@ -82,6 +82,11 @@ SIGNATURES = {
     "kq_gemm_f16_tc": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "kq_dense_gemv": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_float, c_int, c_void_p, c_int,
                               c_void_p]),
+    "kq_tq3_create": (c_int, [c_int, c_int, c_int, c_void_p, c_size_t, ctypes.POINTER(c_void_p)]),
+    "kq_tq3_destroy": (c_int, [c_void_p]),
+    "kq_tq3_bytes": (c_size_t, [c_void_p]),
+    "kq_tq3_gemv": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p]),
+    "kq_tq3_dequant": (c_int, [c_void_p, c_void_p, c_void_p]),
     "kq_tq_create": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p, ctypes.POINTER(c_void_p)]),
     "kq_tq_destroy": (c_int, [c_void_p]),
     "kq_tq_seq_len": (c_int, [c_void_p]),

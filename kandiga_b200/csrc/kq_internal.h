@@ -55,3 +55,9 @@ struct kq_tq_cache {
     float* scale[2] = {nullptr, nullptr};     // [B][H][cap] (+ 16 floats of tail padding)
     float* zero[2] = {nullptr, nullptr};
 };
+
+struct kq_tq3_mat {
+    int rows = 0, cols = 0, block_bytes = 0;  // 20 (d0 d1 m0 m1 + codes) or 16 (d0 d1 + codes)
+    size_t bytes = 0;
+    uint8_t* data = nullptr;                  // the reference's block stream, row-major
+};
