@@ -47,22 +47,34 @@ __global__ void __launch_bounds__(TQ3_THREADS) tq3_gemv_kernel(const uint8_t* __
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid < 64) lut[tid] = make_float2(tq3_centroids[tid & 7], tq3_centroids[tid >> 3]);
     const float inv = sqrtf(32.f);
-    // rotate x: warp per (token, block), lane = element
-    for (int job = warp; job < TT * nb; job += TQ3_THREADS / 32) {
-        const int t = job / nb, b = job % nb;
-        float v = t < T ? load_as_float(x, x_dtype, (size_t)t * cols + (size_t)b * 32 + lane) : 0.f;
-        v *= tq3_signs[lane];
+    // rotate x: warp per (token, block), lane = element; four blocks' loads in flight per warp
+    constexpr int NWARP = TQ3_THREADS / 32;
+    for (int j0 = warp; j0 < TT * nb; j0 += 4 * NWARP) {
+        float v[4];
 #pragma unroll
-        for (int step = 1; step < 32; step <<= 1) {
-            const float o = __shfl_xor_sync(0xffffffffu, v, step);
-            v = (lane & step) ? o - v : v + o;
+        for (int u = 0; u < 4; ++u) {
+            const int job = j0 + u * NWARP;
+            const int t = job / nb, b = job % nb;
+            v[u] = (job < TT * nb && t < T) ? load_as_float(x, x_dtype, (size_t)t * cols + (size_t)b * 32 + lane) : 0.f;
         }
-        v = __fdiv_rn(v, inv);
-        xr[((size_t)t * nb + b) * TQ3_XSTRIDE + lane] = v;
-        float h = v;
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) h += __shfl_xor_sync(0xffffffffu, h, o);
-        if ((lane & 15) == 0) hs[(size_t)t * 2 * nb + 2 * b + (lane >> 4)] = h;
+        for (int u = 0; u < 4; ++u) {
+            const int job = j0 + u * NWARP;
+            if (job >= TT * nb) break;
+            const int t = job / nb, b = job % nb;
+            float w = v[u] * tq3_signs[lane];
+#pragma unroll
+            for (int step = 1; step < 32; step <<= 1) {
+                const float o = __shfl_xor_sync(0xffffffffu, w, step);
+                w = (lane & step) ? o - w : w + o;
+            }
+            w = __fdiv_rn(w, inv);
+            xr[((size_t)t * nb + b) * TQ3_XSTRIDE + lane] = w;
+            float h = w;
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) h += __shfl_xor_sync(0xffffffffu, h, o);
+            if ((lane & 15) == 0) hs[(size_t)t * 2 * nb + 2 * b + (lane >> 4)] = h;
+        }
     }
     __syncthreads();
     const size_t row_bytes = (size_t)nb * BB;
