@@ -216,6 +216,18 @@ int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x_dtype, int
                    void* out, int out_dtype, const void* residual, void* workspace,
                    size_t workspace_bytes, void* stream);
 
+/* Shared expert gate of a MoE block (kandiga/metal/moe_block.metal:335-404):
+ * gate[t] = sigmoid(w_gate . x[t]), w_gate one MLX-layout row of H weights
+ * (bits 3/4, fp16/bf16 scales and biases).  The shared expert itself is stored
+ * as expert `shared_id` of the layer's table; this call writes the routed
+ * assignments extended by it, idx_out / weights_out [T][K+1] = (idx[t], shared_id)
+ * / (weights[t], gate[t]), so kq_moe_decode / kq_moe_prefill with K+1 compute
+ * [res] + sum_k w_k y_k + gate * y_shared, the reference's blend
+ * (moe_block.metal:515-584), in their own combine.  gate_out [T] may be NULL. */
+int kq_shared_gate(const void* x, int x_dtype, int T, int H, const void* gate_weight, const void* gate_scales,
+                   const void* gate_biases, int bits, int sb_dtype, const int32_t* idx, const float* weights, int K,
+                   int shared_id, int32_t* idx_out, float* weights_out, float* gate_out, void* stream);
+
 /* Read and clear the device status word of a workspace (synchronises `stream`). */
 int kq_status_read(void* workspace, uint32_t* status, void* stream);
 

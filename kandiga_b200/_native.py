@@ -82,6 +82,8 @@ SIGNATURES = {
     "kq_gemm_f16_tc": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "kq_dense_gemv": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_float, c_int, c_void_p, c_int,
                               c_void_p]),
+    "kq_shared_gate": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                               c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "kq_tq3_create": (c_int, [c_int, c_int, c_int, c_void_p, c_size_t, ctypes.POINTER(c_void_p)]),
     "kq_tq3_destroy": (c_int, [c_void_p]),
     "kq_tq3_bytes": (c_size_t, [c_void_p]),

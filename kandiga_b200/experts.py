@@ -161,6 +161,31 @@ class ExpertTable:
                     weights=weights)
 
 
+    def moe_block(self, layer, x, logits, top_k, shared_gate, shared_id=None, gate_bits=4, gate_sb="f16",
+                  residual=None, out_dtype=None, path="auto"):
+        """MoE block with a shared expert (kandiga/metal/moe_block.metal:134-584):
+        out = [res] + sum_k w_k expert_k(x) + sigmoid(w_gate . x) shared(x).
+
+        The shared expert is expert `shared_id` of this layer (default: the last
+        one; `logits` cover the routed experts before it).  shared_gate =
+        (weight, scales, biases): the gate row [1, H] in MLX layout.
+        Returns dict(out, idx [T, K+1], weights [T, K+1], gate [T])."""
+        T, E = logits.shape
+        sid = self.num_experts - 1 if shared_id is None else shared_id
+        dev = x.device
+        idx, w = router_topk(logits, top_k)
+        idx2 = torch.empty(T, top_k + 1, dtype=torch.int32, device=dev)
+        w2 = torch.empty(T, top_k + 1, dtype=torch.float32, device=dev)
+        gate = torch.empty(T, dtype=torch.float32, device=dev)
+        gw, gs, gb = shared_gate
+        N.check(self.lib.kq_shared_gate(_ptr(x), _DT[x.dtype], T, self.hidden, _ptr(gw), _ptr(gs), _ptr(gb),
+                                        gate_bits, N.DT_F16 if gate_sb == "f16" else N.DT_BF16, _ptr(idx), _ptr(w),
+                                        top_k, sid, _ptr(idx2), _ptr(w2), _ptr(gate), _stream()), "kq_shared_gate")
+        r = self.moe(layer, x, idx=idx2, weights=w2, combine=True, residual=residual, out_dtype=out_dtype,
+                     path=path)
+        return dict(out=r["out"], idx=idx2, weights=w2, gate=gate)
+
+
 def router_topk(logits: torch.Tensor, k: int):
     """softmax -> top-k (strict '>', lowest index on ties) -> renormalised weights."""
     lib = N.load()

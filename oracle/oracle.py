@@ -326,6 +326,15 @@ def combine(y, w, res=None, shared=None, gate=None):
     return out
 
 
+def shared_gate(x: np.ndarray, packed, scales, biases, bits, sb_dtype="f16", gs=64) -> np.ndarray:
+    """sigmoid(w_gate . x) per token, w_gate one quantized row
+    (kandiga/metal/moe_block.metal:335-404: sum of fma(q, s, b) * x in fp32)."""
+    H = x.shape[-1]
+    w = dequantize_affine(packed, scales, biases, bits, H, gs, sb_dtype).reshape(H).astype(np.float32)
+    logit = (x.astype(np.float32) * w[None, :]).sum(-1, dtype=np.float32)
+    return (1.0 / (1.0 + np.exp(-logit))).astype(np.float32)
+
+
 def group_by_expert(idx: np.ndarray):
     """Stable grouping of the T*K assignments by expert id
     (kandiga/engine.py:407-418: mergesort argsort, boundaries via diff)."""
