@@ -228,6 +228,14 @@ int kq_shared_gate(const void* x, int x_dtype, int T, int H, const void* gate_we
                    const void* gate_biases, int bits, int sb_dtype, const int32_t* idx, const float* weights, int K,
                    int shared_id, int32_t* idx_out, float* weights_out, float* gate_out, void* stream);
 
+/* Blend of a MoE block from per-expert outputs (kandiga/metal/moe_block.metal:515-584):
+ * out[t] = [res[t]] + sum_k w[t][k] y[t][k] + [gate[t] * shared[t]] (gate NULL = 1).
+ * y [T][K][H] in y_dtype, residual [T][H] in out_dtype, shared [T][H] in shared_dtype;
+ * residual / shared may be NULL.  The last step of the expert-parallel path,
+ * where the per-expert rows come back from other GPUs. */
+int kq_combine(const void* y, int y_dtype, const float* weights, int T, int K, int H, const void* residual,
+               const void* shared, int shared_dtype, const float* gate, void* out, int out_dtype, void* stream);
+
 /* Read and clear the device status word of a workspace (synchronises `stream`). */
 int kq_status_read(void* workspace, uint32_t* status, void* stream);
 

@@ -84,6 +84,8 @@ SIGNATURES = {
                               c_void_p]),
     "kq_shared_gate": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "kq_combine": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p,
+                           c_void_p, c_int, c_void_p]),
     "kq_tq3_create": (c_int, [c_int, c_int, c_int, c_void_p, c_size_t, ctypes.POINTER(c_void_p)]),
     "kq_tq3_destroy": (c_int, [c_void_p]),
     "kq_tq3_bytes": (c_size_t, [c_void_p]),

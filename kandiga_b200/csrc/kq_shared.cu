@@ -85,3 +85,36 @@ extern "C" int kq_shared_gate(const void* x, int x_dtype, int T, int H, const vo
 #undef KQ_SG
     return cudaGetLastError() == cudaSuccess ? KQ_OK : KQ_ERR_CUDA;
 }
+
+namespace kq {
+
+// out[t][h] = [res[t][h]] + sum_k w[t][k] y[t][k][h] + [gate[t] shared[t][h]]
+__global__ void blend_kernel(const void* __restrict__ y, int y_dtype, const float* __restrict__ w, int T, int K,
+                             int H, const void* __restrict__ residual, const void* __restrict__ shared,
+                             int shared_dtype, const float* __restrict__ gate, void* out, int out_dtype) {
+    const int t = blockIdx.y, h = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T || h >= H) return;
+    float acc = 0.f;
+    for (int k = 0; k < K; ++k) acc = fmaf(load_as_float(y, y_dtype, ((size_t)t * K + k) * H + h), w[(size_t)t * K + k], acc);
+    if (shared) acc = fmaf(gate ? gate[t] : 1.f, load_as_float(shared, shared_dtype, (size_t)t * H + h), acc);
+    if (residual) acc = load_as_float(residual, out_dtype, (size_t)t * H + h) + acc;
+    store_from_float(out, out_dtype, (size_t)t * H + h, acc);
+}
+
+}  // namespace kq
+
+extern "C" int kq_combine(const void* y, int y_dtype, const float* weights, int T, int K, int H, const void* residual,
+                          const void* shared, int shared_dtype, const float* gate, void* out, int out_dtype,
+                          void* stream) {
+    if (T < 0 || K < 0 || H <= 0) return KQ_ERR_ARG;
+    for (int dt : {y_dtype, out_dtype})
+        if (dt != KQ_DT_F16 && dt != KQ_DT_BF16 && dt != KQ_DT_F32) return KQ_ERR_ARG;
+    if (shared && shared_dtype != KQ_DT_F16 && shared_dtype != KQ_DT_BF16 && shared_dtype != KQ_DT_F32)
+        return KQ_ERR_ARG;
+    if (T == 0) return KQ_OK;
+    if (!out || (K > 0 && (!y || !weights))) return KQ_ERR_ARG;
+    dim3 grid((H + 255) / 256, T);
+    blend_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(y, y_dtype, weights, T, K, H, residual, shared,
+                                                                      shared_dtype, gate, out, out_dtype);
+    return cudaGetLastError() == cudaSuccess ? KQ_OK : KQ_ERR_CUDA;
+}

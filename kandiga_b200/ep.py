@@ -1,0 +1,167 @@
+"""Expert-parallel MoE layers across the GPUs of one node (one process per GPU).
+
+The routed experts of a layer are partitioned over the ranks (each rank's
+kq_table holds only its own experts); tokens are data-parallel (each rank owns
+its own tokens).  Per layer and rank:
+
+1. route the local tokens (kq_router_topk: softmax, top-K, renormalise);
+2. count the (token, k) assignments per destination rank, exchange the counts
+   (all-to-all of G int64);
+3. all-to-all-v of the assigned token rows (fp16/bf16) and of their expert ids
+   local to the destination;
+4. every rank runs its experts on the rows it received, grouped by expert
+   (kq_moe_prefill / kq_moe_decode with one assignment per row);
+5. all-to-all-v of the expert outputs back to the token owners;
+6. weighted combine with the residual and the gated shared expert, computed
+   on the owner (kq_combine).
+
+The exchanges are NCCL all-to-all-v through torch.distributed (gloo on CPU for
+the host-logic tests).  Router, expert compute and combine are pluggable so the
+same exchange code runs with the GPU kernels or, in CPU tests, with a
+restatement of them.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import _native as N
+
+_DT = {torch.float16: N.DT_F16, torch.bfloat16: N.DT_BF16, torch.float32: N.DT_F32}
+
+
+@dataclass
+class ExpertPlacement:
+    """owner[e]: rank holding routed expert e; local[e]: its index in that rank's table."""
+    owner: np.ndarray
+    local: np.ndarray
+    world: int
+
+    @classmethod
+    def contiguous(cls, num_experts: int, world: int) -> "ExpertPlacement":
+        per = (num_experts + world - 1) // world
+        e = np.arange(num_experts)
+        return cls((e // per).astype(np.int64), (e % per).astype(np.int64), world)
+
+    @classmethod
+    def balanced(cls, load: np.ndarray, world: int) -> "ExpertPlacement":
+        """Greedy bin packing by expected load (largest first onto the least loaded
+        rank with room), equal expert counts per rank (the expected routing
+        frequencies are static across a run)."""
+        E = len(load)
+        cap = (E + world - 1) // world
+        owner = np.zeros(E, np.int64)
+        local = np.zeros(E, np.int64)
+        tot = np.zeros(world)
+        used = np.zeros(world, np.int64)
+        for e in np.argsort(-np.asarray(load, np.float64), kind="stable"):
+            cand = [r for r in range(world) if used[r] < cap]
+            r = min(cand, key=lambda q: (tot[q], q))
+            owner[e], local[e] = r, used[r]
+            used[r] += 1
+            tot[r] += load[e]
+        return cls(owner, local, world)
+
+    def experts_of(self, rank: int) -> np.ndarray:
+        """Global ids of `rank`'s experts in local order."""
+        ids = np.nonzero(self.owner == rank)[0]
+        return ids[np.argsort(self.local[ids], kind="stable")]
+
+
+def zipf_bias(num_experts: int, s: float = 1.1, seed: int = 0) -> np.ndarray:
+    """Router-logit bias b_e = -s ln(rank_e + 1) with a seeded permutation of ranks."""
+    rank = np.random.RandomState(seed).permutation(num_experts)
+    return (-s * np.log(rank + 1.0)).astype(np.float32)
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def gpu_router(logits: torch.Tensor, k: int):
+    from .experts import router_topk
+    return router_topk(logits, k)
+
+
+def gpu_combine(per_k, weights, residual=None, shared=None, gate=None, out_dtype=None):
+    """kq_combine: [res] + sum_k w_k y_k + gate * shared."""
+    T, K, H = per_k.shape
+    out_dtype = out_dtype or per_k.dtype
+    out = torch.empty(T, H, dtype=out_dtype, device=per_k.device)
+    lib = N.load()
+    p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+    N.check(lib.kq_combine(p(per_k), _DT[per_k.dtype], p(weights), T, K, H, p(residual), p(shared),
+                           _DT[shared.dtype] if shared is not None else 0, p(gate), p(out), _DT[out_dtype],
+                           _stream()), "kq_combine")
+    return out
+
+
+def table_compute(table):
+    """Expert compute on this rank's kq_table: one assignment per received row."""
+    def run(layer: int, rows: torch.Tensor, local_ids: torch.Tensor) -> torch.Tensor:
+        R = rows.shape[0]
+        if R == 0:
+            return torch.empty(0, rows.shape[1], dtype=rows.dtype, device=rows.device)
+        r = table.moe(layer, rows, idx=local_ids.to(torch.int32).reshape(R, 1).contiguous(), per_k=True,
+                      combine=False, out_dtype=rows.dtype)
+        return r["per_k"].reshape(R, -1)
+    return run
+
+
+class ExpertParallelMoE:
+    """Expert-parallel routed MoE for the tokens this rank owns."""
+
+    def __init__(self, placement: ExpertPlacement, rank: int, top_k: int,
+                 compute: Callable, router: Callable = gpu_router, combine: Callable = gpu_combine,
+                 group=None):
+        self.pl, self.rank, self.k, self.group = placement, rank, top_k, group
+        self.compute, self.router, self.combine = compute, router, combine
+        self._owner = None
+        self._local = None
+
+    def _maps(self, dev):
+        if self._owner is None or self._owner.device != dev:
+            self._owner = torch.from_numpy(self.pl.owner).to(dev)
+            self._local = torch.from_numpy(self.pl.local).to(dev)
+        return self._owner, self._local
+
+    def forward(self, layer: int, x: torch.Tensor, logits: torch.Tensor, residual=None, shared=None, gate=None,
+                out_dtype=None, return_parts: bool = False):
+        """x [T, H] this rank's tokens, logits [T, E] over the routed experts.
+        shared [T, H] / gate [T]: the shared expert's output and gate (or None).
+        Returns out [T, H] (and a dict of intermediate tensors if return_parts)."""
+        G, K = self.pl.world, self.k
+        T, H = x.shape
+        dev = x.device
+        owner, local = self._maps(dev)
+        idx, w = self.router(logits, K)
+        flat = idx.reshape(-1).to(torch.int64)
+        dest = owner[flat]
+        order = torch.argsort(dest, stable=True)
+        send_counts = torch.bincount(dest, minlength=G).to(torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        s_split, r_split = send_counts.tolist(), recv_counts.tolist()
+        tok = torch.div(order, K, rounding_mode="floor")
+        send_x = x.index_select(0, tok).contiguous()
+        send_ids = local[flat].index_select(0, order).to(torch.int32).contiguous()
+        R = int(sum(r_split))
+        recv_x = torch.empty(R, H, dtype=x.dtype, device=dev)
+        recv_ids = torch.empty(R, dtype=torch.int32, device=dev)
+        dist.all_to_all_single(recv_x, send_x, r_split, s_split, group=self.group)
+        dist.all_to_all_single(recv_ids, send_ids, r_split, s_split, group=self.group)
+        y_recv = self.compute(layer, recv_x, recv_ids).to(x.dtype).contiguous()
+        y_back = torch.empty(T * K, H, dtype=x.dtype, device=dev)
+        dist.all_to_all_single(y_back, y_recv, s_split, r_split, group=self.group)
+        per_k = torch.empty_like(y_back)
+        per_k.index_copy_(0, order, y_back)
+        per_k = per_k.reshape(T, K, H)
+        out = self.combine(per_k, w, residual=residual, shared=shared, gate=gate, out_dtype=out_dtype)
+        if return_parts:
+            return out, dict(idx=idx, weights=w, per_k=per_k, send=s_split, recv=r_split)
+        return out
