@@ -143,21 +143,25 @@ class ExpertParallelMoE:
         flat = idx.reshape(-1).to(torch.int64)
         dest = owner[flat]
         order = torch.argsort(dest, stable=True)
-        send_counts = torch.bincount(dest, minlength=G).to(torch.int64)
-        recv_counts = torch.empty_like(send_counts)
-        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        s_split, r_split = send_counts.tolist(), recv_counts.tolist()
         tok = torch.div(order, K, rounding_mode="floor")
         send_x = x.index_select(0, tok).contiguous()
         send_ids = local[flat].index_select(0, order).to(torch.int32).contiguous()
-        R = int(sum(r_split))
-        recv_x = torch.empty(R, H, dtype=x.dtype, device=dev)
-        recv_ids = torch.empty(R, dtype=torch.int32, device=dev)
-        dist.all_to_all_single(recv_x, send_x, r_split, s_split, group=self.group)
-        dist.all_to_all_single(recv_ids, send_ids, r_split, s_split, group=self.group)
-        y_recv = self.compute(layer, recv_x, recv_ids).to(x.dtype).contiguous()
-        y_back = torch.empty(T * K, H, dtype=x.dtype, device=dev)
-        dist.all_to_all_single(y_back, y_recv, s_split, r_split, group=self.group)
+        if G == 1:  # one rank: no exchange
+            s_split = r_split = [T * K]
+            y_back = self.compute(layer, send_x, send_ids).to(x.dtype).contiguous()
+        else:
+            send_counts = torch.bincount(dest, minlength=G).to(torch.int64)
+            recv_counts = torch.empty_like(send_counts)
+            dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+            s_split, r_split = send_counts.tolist(), recv_counts.tolist()
+            R = int(sum(r_split))
+            recv_x = torch.empty(R, H, dtype=x.dtype, device=dev)
+            recv_ids = torch.empty(R, dtype=torch.int32, device=dev)
+            dist.all_to_all_single(recv_x, send_x, r_split, s_split, group=self.group)
+            dist.all_to_all_single(recv_ids, send_ids, r_split, s_split, group=self.group)
+            y_recv = self.compute(layer, recv_x, recv_ids).to(x.dtype).contiguous()
+            y_back = torch.empty(T * K, H, dtype=x.dtype, device=dev)
+            dist.all_to_all_single(y_back, y_recv, s_split, r_split, group=self.group)
         per_k = torch.empty_like(y_back)
         per_k.index_copy_(0, order, y_back)
         per_k = per_k.reshape(T, K, H)
