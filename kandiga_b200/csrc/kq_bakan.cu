@@ -35,7 +35,7 @@ struct Engine {
     size_t dout_bytes = 0;
     int32_t* didx = nullptr;
     size_t didx_bytes = 0;
-    std::vector<uint8_t> host_stage;
+    uint32_t* hstatus = nullptr;  // pinned host word the device status is copied into
 };
 
 bool grow(void** p, size_t* have, size_t need) {
@@ -64,6 +64,11 @@ size_t ws_need(const Engine* e, int T, int K) {
 
 bool ensure(Engine* e, int T, int K) {
     const int H = e->info.hidden;
+    if (!e->hstatus && cudaHostAlloc(reinterpret_cast<void**>(&e->hstatus), 4, cudaHostAllocDefault) != cudaSuccess) {
+        cudaGetLastError();
+        e->hstatus = nullptr;
+        return false;
+    }
     if (!grow(&e->dx, &e->dx_bytes, (size_t)T * H * 4)) return false;
     if (!grow(&e->dout, &e->dout_bytes, (size_t)T * K * H * 4)) return false;
     if (!grow(reinterpret_cast<void**>(&e->didx), &e->didx_bytes, (size_t)T * K * 4)) return false;
@@ -103,16 +108,14 @@ int check_call(Engine* e, int layer, const int32_t* idx, int n, int K) {
     return 0;
 }
 
-// Run T tokens x K experts: x host [T][H] in x_dtype -> out host [T][K][H] in out_dtype.
-int run(Engine* e, int layer, const void* x, int x_dtype, const int32_t* idx, int T, int K,
-        void* out, int out_dtype) {
+// Enqueue on e->stream: host -> device copy of x [T][H] and idx [T][K], the
+// expert kernels into e->dout [T][K][H] (out_dtype).  Nothing is copied back.
+int launch(Engine* e, int layer, const void* x, int x_dtype, const int32_t* idx, int T, int K, int out_dtype) {
     if (!ensure(e, T, K)) {
         fprintf(stderr, "[kandiga] ERROR: device allocation failed\n");
         return -1;
     }
-    const int H = e->info.hidden;
-    const size_t xb = (size_t)T * H * (x_dtype == KQ_DT_F32 ? 4 : 2);
-    const size_t ob = (size_t)T * K * H * (out_dtype == KQ_DT_F32 ? 4 : 2);
+    const size_t xb = (size_t)T * e->info.hidden * (x_dtype == KQ_DT_F32 ? 4 : 2);
     cudaStream_t s = e->stream;
     if (cudaMemcpyAsync(e->dx, x, xb, cudaMemcpyHostToDevice, s) != cudaSuccess ||
         cudaMemcpyAsync(e->didx, idx, (size_t)T * K * 4, cudaMemcpyHostToDevice, s) != cudaSuccess) {
@@ -126,17 +129,42 @@ int run(Engine* e, int layer, const void* x, int x_dtype, const int32_t* idx, in
         fprintf(stderr, "[kandiga] ERROR: expert kernels failed for layer %d (code %d)\n", layer, rc);
         return -1;
     }
-    if (cudaMemcpyAsync(out, e->dout, ob, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
-        cudaStreamSynchronize(s) != cudaSuccess) {
+    return 0;
+}
+
+// Copy rows [r0, r1) of e->dout (row = one (token, k) output of `row` bytes) to host `out`.
+int copy_rows(Engine* e, int layer, void* out, size_t row, size_t r0, size_t r1) {
+    if (cudaMemcpyAsync(static_cast<uint8_t*>(out) + r0 * row, static_cast<const uint8_t*>(e->dout) + r0 * row,
+                        (r1 - r0) * row, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess) {
         fprintf(stderr, "[kandiga] ERROR: Expert computation failed for layer %d\n", layer);
         return -1;
     }
-    uint32_t st = 0;
-    if (kq_status_read(e->ws, &st, s) != KQ_OK || st != 0) {
-        fprintf(stderr, "[kandiga] ERROR: device status 0x%x for layer %d\n", st, layer);
+    return 0;
+}
+
+// Copy and clear the kernels' device status word behind the output copies,
+// wait for the stream once, then check the word.
+int finish(Engine* e, int layer) {
+    *e->hstatus = 0;
+    if (cudaMemcpyAsync(e->hstatus, e->ws, 4, cudaMemcpyDeviceToHost, e->stream) != cudaSuccess ||
+        cudaMemsetAsync(e->ws, 0, 4, e->stream) != cudaSuccess || cudaStreamSynchronize(e->stream) != cudaSuccess) {
+        fprintf(stderr, "[kandiga] ERROR: Expert computation failed for layer %d\n", layer);
+        return -1;
+    }
+    if (*e->hstatus != 0) {
+        fprintf(stderr, "[kandiga] ERROR: device status 0x%x for layer %d\n", *e->hstatus, layer);
         return -1;
     }
     return 0;
+}
+
+// Run T tokens x K experts: x host [T][H] in x_dtype -> out host [T][K][H] in out_dtype.
+int run(Engine* e, int layer, const void* x, int x_dtype, const int32_t* idx, int T, int K,
+        void* out, int out_dtype) {
+    if (launch(e, layer, x, x_dtype, idx, T, K, out_dtype)) return -1;
+    const size_t row = (size_t)e->info.hidden * (out_dtype == KQ_DT_F32 ? 4 : 2);
+    if (copy_rows(e, layer, out, row, 0, (size_t)T * K)) return -1;
+    return finish(e, layer);
 }
 
 }  // namespace
@@ -283,14 +311,22 @@ extern "C" int bakan_cpu_expert_mlp_prefill_f16(void* engine, int layer_idx, con
         }
     }
     (void)sorted_expert_indices;
-    const size_t row = (size_t)hidden_size * 2;
-    e->host_stage.resize((size_t)num_tokens * K * row);
-    if (run(e, layer_idx, x_f16, KQ_DT_F16, idx.data(), num_tokens, K, e->host_stage.data(), KQ_DT_F16))
-        return -1;
-    uint8_t* out = static_cast<uint8_t*>(output_f16);
-    for (size_t i = 0; i < covered.size(); ++i)
-        if (covered[i]) memcpy(out + i * row, e->host_stage.data() + i * row, row);
-    return 0;
+    // Covered (token, k) rows are copied straight from HBM into the caller's
+    // buffer, one copy per run of consecutive covered rows (one copy in total
+    // when the groups cover every pair).
+    if (launch(e, layer_idx, x_f16, KQ_DT_F16, idx.data(), num_tokens, K, KQ_DT_F16)) return -1;
+    const size_t row = (size_t)hidden_size * 2, n = covered.size();
+    for (size_t i = 0; i < n;) {
+        if (!covered[i]) {
+            ++i;
+            continue;
+        }
+        size_t j = i;
+        while (j < n && covered[j]) ++j;
+        if (copy_rows(e, layer_idx, output_f16, row, i, j)) return -1;
+        i = j;
+    }
+    return finish(e, layer_idx);
 }
 
 extern "C" int bakan_cpu_expert_pread_batch(void* engine, int layer_idx, const int32_t* expert_ids,
@@ -337,6 +373,7 @@ extern "C" void bakan_cpu_expert_destroy(void* engine_ptr) {
     if (e->dx) cudaFree(e->dx);
     if (e->dout) cudaFree(e->dout);
     if (e->didx) cudaFree(e->didx);
+    if (e->hstatus) cudaFreeHost(e->hstatus);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
     fprintf(stderr, "[kandiga] Engine destroyed\n");

@@ -100,6 +100,23 @@ def test_fp32_api_batch_prefill_and_pread(packed):
                                                   *[a.ctypes.data_as(N.c_i32p) for a in arrs], len(uniq),
                                                   op.ctypes.data_as(ctypes.c_void_p)) == 0
         assert np.array_equal(op, ob)
+        # CSR prefill on the tensor-core path (T >= 16) with the last group left
+        # out: its (token, k) rows keep their previous contents
+        T2 = 40
+        x2 = rng.randn(T2, 2048).astype(np.float16)
+        i2 = np.stack([rng.choice(6, K, replace=False) for _ in range(T2)]).astype(np.int32)
+        ref2 = layers[1].moe(x2.astype(np.float32), i2)
+        s_tok, s_exp, s_k, starts, uniq = O.group_by_expert(i2)
+        ng = len(uniq) - 1
+        arrs = [np.ascontiguousarray(a, np.int32) for a in (s_tok, s_exp, s_k, starts, uniq)]
+        o2 = np.full((T2, K, 2048), 7, np.float16)
+        assert L.bakan_cpu_expert_mlp_prefill_f16(eng, 1, x2.ctypes.data_as(ctypes.c_void_p), T2, K, 2048,
+                                                  *[a.ctypes.data_as(N.c_i32p) for a in arrs], ng,
+                                                  o2.ctypes.data_as(ctypes.c_void_p)) == 0
+        left_out = i2 == uniq[-1]
+        assert left_out.any() and (~left_out).any()
+        assert np.all(o2[left_out] == 7)
+        assert rel_l2(o2[~left_out].astype(np.float32), ref2[~left_out]) < 2e-3
         # pread_batch reconstructs the BKEX bytes bit-exactly from HBM
         ids = np.array([5, 1], np.int32)
         esz = layers[0].expert_size()
