@@ -4,12 +4,14 @@
 // experts from the BKEX layer files on every call and computes them on CPU
 // cores.  Here init reads every layer file once into the HBM table, and each
 // call is: host -> device copy of x and the expert ids, the sm_100a decode
-// kernels, device -> host copy of the per-expert outputs.  Calls are
+// (one token) or grouped prefill kernels, device -> host copy of the
+// per-expert outputs; a single-token call replays one CUDA graph.  Calls are
 // synchronous and, like the reference, not re-entrant per engine.
 // Errors: -1 with a "[kandiga] ERROR: ..." line on stderr, as the reference.
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <vector>
 
 #include "kq_internal.h"
@@ -36,7 +38,18 @@ struct Engine {
     int32_t* didx = nullptr;
     size_t didx_bytes = 0;
     uint32_t* hstatus = nullptr;  // pinned host word the device status is copied into
+    // Single-token calls: pinned staging [x: H*4 | ids: kMaxExperts*4 | out: kMaxExperts*H*4]
+    // and one instantiated CUDA graph per (layer, K, x dtype, out dtype) doing
+    // copy in -> decode kernels -> copy out -> status copy + clear.  The graphs
+    // hold the device buffers' addresses, so any reallocation drops them.
+    uint8_t* hstage = nullptr;
+    std::map<uint64_t, cudaGraphExec_t> graphs;
 };
+
+void drop_graphs(Engine* e) {
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+}
 
 bool grow(void** p, size_t* have, size_t need) {
     if (*have >= need) return true;
@@ -69,6 +82,16 @@ bool ensure(Engine* e, int T, int K) {
         e->hstatus = nullptr;
         return false;
     }
+    if (!e->hstage && cudaHostAlloc(reinterpret_cast<void**>(&e->hstage),
+                                    (size_t)H * 4 + kMaxExperts * 4 + (size_t)kMaxExperts * H * 4,
+                                    cudaHostAllocDefault) != cudaSuccess) {
+        cudaGetLastError();
+        e->hstage = nullptr;
+        return false;
+    }
+    if (e->dx_bytes < (size_t)T * H * 4 || e->dout_bytes < (size_t)T * K * H * 4 ||
+        e->didx_bytes < (size_t)T * K * 4 || T > e->ws_tokens || e->ws_bytes < ws_need(e, T, K))
+        drop_graphs(e);
     if (!grow(&e->dx, &e->dx_bytes, (size_t)T * H * 4)) return false;
     if (!grow(&e->dout, &e->dout_bytes, (size_t)T * K * H * 4)) return false;
     if (!grow(reinterpret_cast<void**>(&e->didx), &e->didx_bytes, (size_t)T * K * 4)) return false;
@@ -167,6 +190,63 @@ int run(Engine* e, int layer, const void* x, int x_dtype, const int32_t* idx, in
     return finish(e, layer);
 }
 
+// One token x K experts through the engine's CUDA graph for (layer, K, dtypes):
+// the caller's x and ids are staged in pinned memory, one graph launch, one
+// synchronize, the outputs copied out of the pinned stage.
+int run_one(Engine* e, int layer, const void* x, int x_dtype, const int32_t* idx, int K, void* out,
+            int out_dtype) {
+    if (!ensure(e, 1, K)) {
+        fprintf(stderr, "[kandiga] ERROR: device allocation failed\n");
+        return -1;
+    }
+    const int H = e->info.hidden;
+    const size_t xb = (size_t)H * (x_dtype == KQ_DT_F32 ? 4 : 2);
+    const size_t ob = (size_t)K * H * (out_dtype == KQ_DT_F32 ? 4 : 2);
+    uint8_t* hx = e->hstage;
+    int32_t* hidx = reinterpret_cast<int32_t*>(e->hstage + (size_t)H * 4);
+    uint8_t* hout = e->hstage + (size_t)H * 4 + kMaxExperts * 4;
+    const uint64_t key = ((uint64_t)layer << 24) | ((uint64_t)K << 16) | ((uint64_t)x_dtype << 8) | (uint64_t)out_dtype;
+    auto it = e->graphs.find(key);
+    if (it == e->graphs.end()) {
+        cudaStream_t s = e->stream;
+        cudaGraph_t graph = nullptr;
+        if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+            fprintf(stderr, "[kandiga] ERROR: graph capture failed for layer %d\n", layer);
+            return -1;
+        }
+        bool ok = cudaMemcpyAsync(e->dx, hx, xb, cudaMemcpyHostToDevice, s) == cudaSuccess &&
+                  cudaMemcpyAsync(e->didx, hidx, (size_t)K * 4, cudaMemcpyHostToDevice, s) == cudaSuccess;
+        ok = ok && kq_moe_decode(e->table, layer, e->dx, x_dtype, 1, nullptr, e->didx, nullptr, K, e->dout, nullptr,
+                                 out_dtype, nullptr, e->ws, e->ws_bytes, s) == KQ_OK;
+        ok = ok && cudaMemcpyAsync(hout, e->dout, ob, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
+             cudaMemcpyAsync(e->hstatus, e->ws, 4, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
+             cudaMemsetAsync(e->ws, 0, 4, s) == cudaSuccess;
+        const bool ended = cudaStreamEndCapture(s, &graph) == cudaSuccess;
+        cudaGraphExec_t exec = nullptr;
+        ok = ok && ended && graph && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
+        if (graph) cudaGraphDestroy(graph);
+        if (!ok) {
+            cudaGetLastError();
+            fprintf(stderr, "[kandiga] ERROR: graph capture failed for layer %d\n", layer);
+            return -1;
+        }
+        it = e->graphs.emplace(key, exec).first;
+    }
+    memcpy(hx, x, xb);
+    memcpy(hidx, idx, (size_t)K * 4);
+    *e->hstatus = 0;
+    if (cudaGraphLaunch(it->second, e->stream) != cudaSuccess || cudaStreamSynchronize(e->stream) != cudaSuccess) {
+        fprintf(stderr, "[kandiga] ERROR: Expert computation failed for layer %d\n", layer);
+        return -1;
+    }
+    if (*e->hstatus != 0) {
+        fprintf(stderr, "[kandiga] ERROR: device status 0x%x for layer %d\n", *e->hstatus, layer);
+        return -1;
+    }
+    memcpy(out, hout, ob);
+    return 0;
+}
+
 }  // namespace
 
 extern "C" void bakan_cpu_expert_destroy(void* engine_ptr);
@@ -249,7 +329,7 @@ extern "C" int bakan_cpu_expert_mlp(void* engine, int layer_idx, const float* x_
                                     const int32_t* expert_indices, int num_experts, float* output_f32) {
     Engine* e = static_cast<Engine*>(engine);
     if (check_call(e, layer_idx, expert_indices, num_experts, num_experts)) return -1;
-    return run(e, layer_idx, x_f32, KQ_DT_F32, expert_indices, 1, num_experts, output_f32, KQ_DT_F32);
+    return run_one(e, layer_idx, x_f32, KQ_DT_F32, expert_indices, num_experts, output_f32, KQ_DT_F32);
 }
 
 extern "C" int bakan_cpu_expert_mlp_f16(void* engine, int layer_idx, const void* x_f16,
@@ -257,7 +337,7 @@ extern "C" int bakan_cpu_expert_mlp_f16(void* engine, int layer_idx, const void*
                                         void* output_f16) {
     Engine* e = static_cast<Engine*>(engine);
     if (check_call(e, layer_idx, expert_indices, num_experts, num_experts)) return -1;
-    return run(e, layer_idx, x_f16, KQ_DT_F16, expert_indices, 1, num_experts, output_f16, KQ_DT_F16);
+    return run_one(e, layer_idx, x_f16, KQ_DT_F16, expert_indices, num_experts, output_f16, KQ_DT_F16);
 }
 
 extern "C" int bakan_cpu_expert_mlp_bf16(void* engine, int layer_idx, const void* x_bf16,
@@ -265,7 +345,7 @@ extern "C" int bakan_cpu_expert_mlp_bf16(void* engine, int layer_idx, const void
                                          void* output_f16) {
     Engine* e = static_cast<Engine*>(engine);
     if (check_call(e, layer_idx, expert_indices, num_experts, num_experts)) return -1;
-    return run(e, layer_idx, x_bf16, KQ_DT_BF16, expert_indices, 1, num_experts, output_f16, KQ_DT_F16);
+    return run_one(e, layer_idx, x_bf16, KQ_DT_BF16, expert_indices, num_experts, output_f16, KQ_DT_F16);
 }
 
 extern "C" int bakan_cpu_expert_mlp_batch_f16(void* engine, int layer_idx, const void* x_f16_batch,
@@ -374,6 +454,8 @@ extern "C" void bakan_cpu_expert_destroy(void* engine_ptr) {
     if (e->dout) cudaFree(e->dout);
     if (e->didx) cudaFree(e->didx);
     if (e->hstatus) cudaFreeHost(e->hstatus);
+    drop_graphs(e);
+    if (e->hstage) cudaFreeHost(e->hstage);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
     fprintf(stderr, "[kandiga] Engine destroyed\n");

@@ -137,6 +137,44 @@ def test_fp32_api_batch_prefill_and_pread(packed):
         L.bakan_cpu_expert_destroy(eng)
 
 
+def test_single_token_graph_replays_and_reallocation(packed):
+    """Single-token calls replay one CUDA graph per (layer, K, dtypes): new
+    inputs each call, and correct results again after a batch call grew the
+    device buffers (which drops the graphs)."""
+    from kandiga_b200 import _native as N
+    d, layers = packed
+    L = N.load()
+    eng = L.bakan_cpu_expert_init(d.encode(), 2)
+    assert eng
+    try:
+        rng = np.random.RandomState(7)
+
+        def one(layer, K):
+            x = rng.randn(2048).astype(np.float16)
+            idx = rng.choice(6, K, replace=False).astype(np.int32)
+            out = np.zeros((K, 2048), np.float16)
+            assert L.bakan_cpu_expert_mlp_f16(eng, layer, x.ctypes.data_as(ctypes.c_void_p),
+                                              idx.ctypes.data_as(N.c_i32p), K,
+                                              out.ctypes.data_as(ctypes.c_void_p)) == 0
+            ref = layers[layer].moe(x.astype(np.float32)[None], idx[None])[0]
+            assert rel_l2(out.astype(np.float32), ref) < 2e-3
+
+        for i in range(6):
+            one(i % 2, 1 + i % 3)
+        T, K = 96, 4
+        xb = rng.randn(T, 2048).astype(np.float16)
+        ib = np.stack([rng.choice(6, K, replace=False) for _ in range(T)]).astype(np.int32)
+        ob = np.zeros((T, K, 2048), np.float16)
+        assert L.bakan_cpu_expert_mlp_batch_f16(eng, 0, xb.ctypes.data_as(ctypes.c_void_p),
+                                                ib.ctypes.data_as(N.c_i32p), T, K,
+                                                ob.ctypes.data_as(ctypes.c_void_p)) == 0
+        assert rel_l2(ob.astype(np.float32), layers[0].moe(xb.astype(np.float32), ib)) < 2e-3
+        for i in range(6):
+            one(i % 2, 1 + i % 3)
+    finally:
+        L.bakan_cpu_expert_destroy(eng)
+
+
 def test_init_missing_dir_returns_null(gpu, tmp_path):
     from kandiga_b200 import _native as N
     L = N.load()
