@@ -52,15 +52,19 @@ constexpr int GROUP_MAX_E = 4096;  // experts per layer the one-CTA grouping sup
 // Grouping in one CTA (the T*K assignments of a prefill batch are a few
 // thousand ids; one CTA avoids grid-wide synchronisation):
 //   1. rank[a] = atomicAdd(&cnt[idx[a]], 1) in shared memory (kept in inv_pos)
-//   2. exclusive scans of cnt (offsets) and of ceil(cnt/128) (work chunks)
+//   2. exclusive scans of the padded counts roundup(cnt, pad) (offsets) and of
+//      ceil(cnt/chunk) (work chunks)
 //   3. pos = offset[e] + rank[a]; s_tok[pos] = a / K; inv_pos[a] = pos
-// The order of an expert's assignments inside its segment is unspecified; each
-// position is an independent MMA column, so results do not depend on it.
+// Expert segments start on multiples of `pad` positions; the pad positions get
+// s_tok = -1 and *n_pos is the padded total.  The order of an expert's
+// assignments inside its segment is unspecified; each position is an
+// independent MMA column, so results do not depend on it.
 // Ids outside [0, E) get inv_pos = -1 and latch KQ_DEV_BAD_EXPERT.
 __global__ void __launch_bounds__(GROUP_THREADS, 1)
-    group_kernel(const int32_t* __restrict__ idx, int A, int K, int E, int* __restrict__ count,
+    group_kernel(const int32_t* __restrict__ idx, int A, int K, int E, int chunk, int pad, int* __restrict__ count,
                  int* __restrict__ offset, int32_t* __restrict__ s_tok, int32_t* __restrict__ inv_pos,
-                 int4* __restrict__ chunk_list, int* __restrict__ n_chunks, uint32_t* status) {
+                 int4* __restrict__ chunk_list, int* __restrict__ n_chunks, int* __restrict__ n_pos,
+                 uint32_t* status) {
     __shared__ int cnt[GROUP_MAX_E];
     __shared__ int off_s[GROUP_MAX_E];
     __shared__ int wsum[2][32];
@@ -82,8 +86,8 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1)
     const int e0 = min(tid * per, E), e1 = min(e0 + per, E);
     int n_loc = 0, c_loc = 0;
     for (int e = e0; e < e1; ++e) {
-        n_loc += cnt[e];
-        c_loc += (cnt[e] + 127) >> 7;
+        n_loc += (cnt[e] + pad - 1) / pad * pad;
+        c_loc += (cnt[e] + chunk - 1) / chunk;
     }
     int n_inc = n_loc, c_inc = c_loc;  // inclusive warp scans
 #pragma unroll
@@ -116,15 +120,20 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1)
     int n_run = n_inc - n_loc + (warp ? wsum[0][warp - 1] : 0);
     int c_run = c_inc - c_loc + (warp ? wsum[1][warp - 1] : 0);
     for (int e = e0; e < e1; ++e) {
-        const int ne = cnt[e], nch = (ne + 127) >> 7;
+        const int ne = cnt[e], nch = (ne + chunk - 1) / chunk, np = (ne + pad - 1) / pad * pad;
         off_s[e] = n_run;
         offset[e] = n_run;
         count[e] = ne;
-        for (int c = 0; c < nch; ++c) chunk_list[c_run + c] = make_int4(e, min(128, ne - c * 128), n_run + c * 128, c);
-        n_run += ne;
+        for (int c = 0; c < nch; ++c)
+            chunk_list[c_run + c] = make_int4(e, min(chunk, ne - c * chunk), n_run + c * chunk, c);
+        for (int i = ne; i < np; ++i) s_tok[n_run + i] = -1;
+        n_run += np;
         c_run += nch;
     }
-    if (tid == GROUP_THREADS - 1) *n_chunks = c_run;
+    if (tid == GROUP_THREADS - 1) {
+        *n_chunks = c_run;
+        *n_pos = n_run;
+    }
     __syncthreads();
     for (int a = tid; a < A; a += GROUP_THREADS) {
         const int r = inv_pos[a];  // written by this thread above
@@ -137,13 +146,14 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1)
 
 // Xs[pos] = fp16(x[s_tok[pos]] * scale[tok]); one warp per position.  fp16
 // inputs are copied unscaled (xinv == nullptr); other types get a power-of-two
-// scale so every value fits fp16, and xinv[pos] = 1/scale.
+// scale so every value fits fp16, and xinv[pos] = 1/scale.  Pad positions
+// (s_tok < 0) are left unwritten.
 __global__ void gather_kernel(const void* __restrict__ x, int x_dtype, int H, const int32_t* __restrict__ s_tok,
-                              const int* __restrict__ count, const int* __restrict__ offset, int E,
-                              __half* __restrict__ Xs, float* __restrict__ xinv) {
+                              const int* __restrict__ n_pos, __half* __restrict__ Xs, float* __restrict__ xinv) {
     const int pos = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (pos >= offset[E - 1] + count[E - 1]) return;  // only placed positions
+    if (pos >= *n_pos) return;
     const int tok = s_tok[pos];
+    if (tok < 0) return;
     const size_t src = (size_t)tok * H;
     float scale = 1.f;
     if (x_dtype != KQ_DT_F16) {
@@ -252,7 +262,7 @@ __device__ __forceinline__ void dq_pairs(const uint32_t* wd, const uint32_t* sh,
 }
 
 template <int BITS, int SB_DT>
-__device__ __forceinline__ void dequant_row(const uint8_t* tile, int r16, int g, uint8_t* a_stage, int m) {
+__device__ __forceinline__ void dequant_row(const uint8_t* tile, int r16, int g, uint32_t (&out)[32]) {
     constexpr int W = TileT<BITS>::W;  // words per (lane, set); the scale/bias chunk is chunk W
     const int l = 4 * (r16 & 7) + (g & 3);
     const int set = 2 * (r16 >> 3) + (g >> 2);
@@ -275,8 +285,11 @@ __device__ __forceinline__ void dequant_row(const uint8_t* tile, int r16, int g,
     const __half2 c1024 = __hmul2(s2, __float2half2_rn(-1024.f));
     const __half2 c_mid = __hmul2(s2, __float2half2_rn(BITS == 3 ? -128.f : -64.f));
     const __half2 c_lo = __hmul2(s2, __float2half2_rn(-16.f));
-    uint32_t out[32];
     dq_pairs<BITS, SB_DT, 0>(wd, sh, s2, b2, c1024, c_mid, c_lo, out);
+}
+
+// out[32] as row m (one swizzled 128-byte row) of an A stage
+__device__ __forceinline__ void a_row_store(const uint32_t (&out)[32], uint8_t* a_stage, int m) {
 #pragma unroll
     for (int c = 0; c < 8; ++c)
         *reinterpret_cast<uint4*>(a_stage + tc::sw128_offset(m, c * 8)) =
@@ -432,8 +445,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 for (int g = 0; g < 8; ++g) {
                     if ((st * 8 + g) % TC_NMMA != ds) continue;
                     const int gs = ds * TC_SLOTS + (int)(lc % TC_SLOTS);
+                    uint32_t out[32];  // computed before the stage is awaited: a stage is held only for its stores
+                    dequant_row<BITS, SB_DT>(tile, r16, g, out);
                     mbar_wait_sleep(&a_empty[gs], ((lc / TC_SLOTS) & 1) ^ 1, p.status);
-                    dequant_row<BITS, SB_DT>(tile, r16, g, sA + (size_t)gs * TC_STAGE_BYTES, m);
+                    a_row_store(out, sA + (size_t)gs * TC_STAGE_BYTES, m);
                     fence_proxy_async_smem();
                     tc::mbar_arrive(&a_full[gs]);
                     ++lc;
@@ -588,14 +603,23 @@ __global__ void combine_kernel(const float* __restrict__ ys, const int32_t* __re
 
 // ---- host ---------------------------------------------------------------------------------------
 
+// Work chunks hold at most PF_CHUNK tokens of one expert (one MMA N box);
+// expert segments in the sorted order start on multiples of PF_PAD positions.
+// Positions: at most A + (PF_PAD - 1) E.
+constexpr int PF_CHUNK = 128;
+constexpr int PF_PAD = 1;
+
 struct PrefillWs {
-    size_t status, idx, w, count, offset, chunks, n_chunks, s_tok, inv_pos, xinv, Xs, act_s, ys, total;
+    size_t status, idx, w, count, offset, chunks, n_chunks, n_pos, s_tok, inv_pos, xinv, Xs, act_s, ys, total;
+    size_t pcap;  // position rows
 };
 
 static PrefillWs prefill_ws_layout(const kq_table* t, int T, int K) {
     auto al = [](size_t v) { return (v + 255) / 256 * 256; };
-    const size_t A = (size_t)T * K;
+    const size_t A = (size_t)T * K, E = (size_t)t->d.num_experts;
+    const size_t P = A + (PF_PAD - 1) * E;
     PrefillWs L{};
+    L.pcap = P;
     size_t o = 0;
     L.status = o;
     o += 256;
@@ -604,25 +628,27 @@ static PrefillWs prefill_ws_layout(const kq_table* t, int T, int K) {
     L.w = o;
     o = al(o + A * 4);
     L.count = o;
-    o = al(o + (size_t)t->d.num_experts * 4);
+    o = al(o + E * 4);
     L.offset = o;
-    o = al(o + (size_t)t->d.num_experts * 4);
-    L.chunks = o;  // at most E + A/128 live chunks
-    o = al(o + ((size_t)t->d.num_experts + A / 128 + 1) * 16);
+    o = al(o + E * 4);
+    L.chunks = o;  // at most E + A / PF_CHUNK live chunks
+    o = al(o + (E + A / PF_CHUNK + 1) * 16);
     L.n_chunks = o;
     o = al(o + 4);
+    L.n_pos = o;
+    o = al(o + 4);
     L.s_tok = o;
-    o = al(o + A * 4);
+    o = al(o + P * 4);
     L.inv_pos = o;
     o = al(o + A * 4);
     L.xinv = o;
-    o = al(o + A * 4);
+    o = al(o + P * 4);
     L.Xs = o;
-    o = al(o + A * t->d.hidden * 2);
+    o = al(o + P * t->d.hidden * 2);
     L.act_s = o;
-    o = al(o + A * t->d.inter * 2);
+    o = al(o + P * t->d.inter * 2);
     L.ys = o;
-    o = al(o + A * t->d.hidden * 4);
+    o = al(o + P * t->d.hidden * 4);
     L.total = o;
     return L;
 }
@@ -694,6 +720,13 @@ static cudaError_t launch_tc(int bits, int sb, const TcParams& p, const CUtensor
 
 int launch_router_ext(const float* logits, int T, int E, int K, int32_t* idx, float* w, cudaStream_t s);
 
+// A failed launch or tensor-map encode of the prefill path: one stderr line, KQ_ERR_CUDA.
+static int pf_fail(const char* what, cudaError_t e = cudaSuccess) {
+    fprintf(stderr, "[kq] prefill: %s failed%s%s\n", what, e != cudaSuccess ? ": " : "",
+            e != cudaSuccess ? cudaGetErrorString(e) : "");
+    return KQ_ERR_CUDA;
+}
+
 }  // namespace kq
 
 using namespace kq;
@@ -731,43 +764,38 @@ extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x
     int* offset = reinterpret_cast<int*>(ws + L.offset);
     int4* chunk_list = reinterpret_cast<int4*>(ws + L.chunks);
     int* n_chunks = reinterpret_cast<int*>(ws + L.n_chunks);
+    int* n_pos = reinterpret_cast<int*>(ws + L.n_pos);
     int32_t* s_tok = reinterpret_cast<int32_t*>(ws + L.s_tok);
     int32_t* inv_pos = reinterpret_cast<int32_t*>(ws + L.inv_pos);
     float* xinv = reinterpret_cast<float*>(ws + L.xinv);
     __half* Xs = reinterpret_cast<__half*>(ws + L.Xs);
     __half* act_s = reinterpret_cast<__half*>(ws + L.act_s);
     float* ys = reinterpret_cast<float*>(ws + L.ys);
+    const int P = (int)L.pcap;
 
     if (logits && launch_router_ext(logits, T, E, K, idx_use, w_use, s) != KQ_OK) return KQ_ERR_CUDA;
     {
         const int threads = 256;
-        group_kernel<<<1, GROUP_THREADS, 0, s>>>(idx_use, A, K, E, count, offset, s_tok, inv_pos, chunk_list,
-                                                 n_chunks, status);
-        gather_kernel<<<(A * 32 + threads - 1) / threads, threads, 0, s>>>(x, x_dtype, H, s_tok, count, offset, E,
-                                                                             Xs, xinv);
-        if (cudaGetLastError() != cudaSuccess) return KQ_ERR_CUDA;
+        group_kernel<<<1, GROUP_THREADS, 0, s>>>(idx_use, A, K, E, PF_CHUNK, PF_PAD, count, offset, s_tok, inv_pos,
+                                                 chunk_list, n_chunks, n_pos, status);
+        gather_kernel<<<(P * 32 + threads - 1) / threads, threads, 0, s>>>(x, x_dtype, H, s_tok, n_pos, Xs, xinv);
+        if (cudaError_t e = cudaGetLastError()) return pf_fail("grouping", e);
     }
-    // Rows of Xs / act_s past the assigned positions are never written; the
-    // epilogues ignore the MMA columns that read them.
+    // Rows of Xs / act_s at pad positions or past the placed ones are never
+    // written; the epilogues ignore the MMA columns that read them.
     int nsm = 148;
     {
         int dev = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     }
-    CUtensorMap tx[4], ta[4];
-    const int boxes[4] = {16, 32, 64, 128};
-    for (int i = 0; i < 4; ++i) {
-        if (!make_tmap(&tx[i], Xs, A, H, boxes[i]) || !make_tmap(&ta[i], act_s, A, I, boxes[i])) return KQ_ERR_CUDA;
-    }
     CUtensorMap tkq;
     const uint8_t* layer_base = t->base + (size_t)layer * t->layer_bytes;
     if ((reinterpret_cast<uintptr_t>(layer_base) & 127) || (t->layer_bytes & 127) || (t->expert_bytes & 127) ||
         (t->gateup_bytes & 127) || (t->tb & 127))
         return KQ_ERR_UNSUPPORTED;  // tiles must start on 128-byte rows
-    if (!make_kq_tmap(&tkq, layer_base, t->layer_bytes, (int)t->tb)) return KQ_ERR_CUDA;
-    // live chunks: sum over experts of ceil(n_e / 128) <= E + A / 128
-    const int max_chunks = E + A / 128;
+    if (!make_kq_tmap(&tkq, layer_base, t->layer_bytes, (int)t->tb)) return pf_fail("tile tensor map");
+    const int max_chunks = E + A / PF_CHUNK + 1;  // live chunks: sum over experts of ceil(n_e / PF_CHUNK)
     TcParams p{};
     p.base = layer_base;
     p.expert_bytes = t->expert_bytes;
@@ -783,20 +811,29 @@ extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x
     p.xinv = x_dtype == KQ_DT_F16 ? nullptr : xinv;
     p.act_kind = t->d.activation;
     p.status = status;
+    const int boxes[4] = {16, 32, 64, 128};
+    // One grouped GEMM over `src` [P][Kdim].
+    auto gemm = [&](const __half* src, int Kdim) -> int {
+        p.nst = Kdim / 512;
+        const int items = max_chunks * p.n_mt;  // upper bound; the kernel reads the live count
+        const int grid = std::min(items, nsm);
+        CUtensorMap tm[4];
+        for (int i = 0; i < 4; ++i)
+            if (!make_tmap(&tm[i], src, P, Kdim, boxes[i])) return pf_fail("token tensor map");
+        if (cudaError_t e = launch_tc(t->d.bits, t->d.sb_dtype, p, tm, tkq, s, grid))
+            return pf_fail("grouped GEMM", e);
+        return KQ_OK;
+    };
     // gate/up + activation
     p.mode = 0;
     p.mat_off = 0;
-    p.nst = H / 512;
     p.n_mt = I / 64;
-    int items = max_chunks * p.n_mt;  // upper bound; the kernel reads the live count
-    if (launch_tc(t->d.bits, t->d.sb_dtype, p, tx, tkq, s, std::min(items, nsm)) != cudaSuccess) return KQ_ERR_CUDA;
+    if (int rc = gemm(Xs, H)) return rc;
     // down
     p.mode = 1;
     p.mat_off = t->gateup_bytes;
-    p.nst = I / 512;
     p.n_mt = H / 128;
-    items = max_chunks * p.n_mt;
-    if (launch_tc(t->d.bits, t->d.sb_dtype, p, ta, tkq, s, std::min(items, nsm)) != cudaSuccess) return KQ_ERR_CUDA;
+    if (int rc = gemm(act_s, I)) return rc;
     // combine / per-k outputs
     dim3 grid((H + 255) / 256, T);
     combine_kernel<<<grid, 256, 0, s>>>(ys, inv_pos, w_use, T, K, H, out, out_per_k, out_dtype, residual);

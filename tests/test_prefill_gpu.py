@@ -83,6 +83,21 @@ def test_prefill_matches_decode_path(gpu):
     assert rel_l2(a.cpu().numpy(), b.cpu().numpy()) < RTOL_L2
 
 
+@pytest.mark.parametrize("H,I", [(2560, 512), (1024, 2560)])
+def test_prefill_wide_k(gpu, H, I):
+    """K = 2560 in gate/up (H = 2560) or in down (I = 2560): five 512-wide
+    super-tiles per item, bf16 scales."""
+    E, K, T = 8, 2, 40
+    layer = get_layer(4, H, I, E, "bf16", seed=H + I)
+    t = make_table(layer)
+    rng = np.random.RandomState(H)
+    x = torch.from_numpy(rng.randn(T, H).astype(np.float16)).cuda()
+    logits = torch.from_numpy(rng.randn(T, E).astype(np.float32)).cuda()
+    r = t.moe(0, x, logits=logits, top_k=K, per_k=True, combine=True, out_dtype=torch.float32, path="prefill")
+    check(layer, t, x, r["idx"].cpu().numpy(), r["weights"].cpu().numpy(), r)
+    assert t.status() == 0
+
+
 def test_prefill_bad_expert(gpu):
     from kandiga_b200 import _native as N
     E, H, I, K, T = 8, 1024, 512, 2, 20
