@@ -108,6 +108,44 @@ void bakan_cpu_expert_destroy(void* engine);
 /* replaces kandiga/metal/kandiga_cpu_expert.h:96 */
 int bakan_cpu_expert_num_layers(void* engine);
 
+/* ---- 1b. MoE block engine (kandiga/metal/bakan_forward.h) -----------------------
+ * The reference declares this ABI (bakan_forward.h:55-151) without an
+ * implementation; here it runs the arithmetic of kandiga/metal/moe_block.metal
+ * on the GPU.  Host pointers, synchronous, not re-entrant per engine; 0 / -1
+ * with a "[kandiga] ERROR" line on stderr.  The routed experts come from the
+ * BKEX layer files; the other tensors of a layer from set_weight. */
+
+/* replaces kandiga/metal/bakan_forward.h:64 */
+void* bakan_forward_init(const char* packed_expert_dir, int num_layers);
+
+/* replaces kandiga/metal/bakan_forward.h:83.  weight_type: WT_* of
+ * bakan_forward.h:35-53 (0 post-attention norm [H]; 1-3 router weight /
+ * scales / biases; 4-6 shared-expert gate row; 7-9 shared up_proj; 10-12
+ * shared gate_proj; 13-15 shared down_proj), MLX layout; dtype 0 fp16,
+ * 1 uint32 (packed 3- or 4-bit codes), 2 bf16; size = rows * cols * element
+ * bytes.  A matrix is repacked into HBM once its weight, scales and biases
+ * are all set. */
+int bakan_forward_set_weight(void* engine, int layer_idx, int weight_type, const void* data, size_t size, int rows,
+                             int cols, int dtype);
+
+/* replaces kandiga/metal/bakan_forward.h:110: output = h + MoE(rmsnorm(h)),
+ * h and output fp16 [hidden]. */
+int bakan_forward_moe_block(void* engine, int layer_idx, const void* h_f16, void* output_f16);
+
+/* replaces kandiga/metal/bakan_forward.h:135: output = MoE(x), x already normed. */
+int bakan_forward_moe_block_normed(void* engine, int layer_idx, const void* x_f16, void* output_f16);
+
+/* replaces kandiga/metal/bakan_forward.h:145 */
+void bakan_forward_destroy(void* engine);
+
+/* replaces kandiga/metal/bakan_forward.h:150 */
+int bakan_forward_num_layers(void* engine);
+
+/* Block parameters the reference fixes in MoeBlockParams
+ * (kandiga/metal/moe_block.metal:114-121): top-K (default 8) and the RMSNorm
+ * epsilon (default 1e-6).  KQ_OK or KQ_ERR_ARG. */
+int kq_forward_set_params(void* engine, int top_k, float rms_norm_eps);
+
 /* ---- 2. device ABI ------------------------------------------------------------ */
 
 typedef struct kq_table kq_table; /* HBM-resident routed-expert table (all layers) */

@@ -53,6 +53,13 @@ SIGNATURES = {
     "bakan_cpu_expert_pread_batch": (c_int, [c_void_p, c_int, c_i32p, c_int, c_void_p]),
     "bakan_cpu_expert_destroy": (None, [c_void_p]),
     "bakan_cpu_expert_num_layers": (c_int, [c_void_p]),
+    "bakan_forward_init": (c_void_p, [ctypes.c_char_p, c_int]),
+    "bakan_forward_set_weight": (c_int, [c_void_p, c_int, c_int, c_void_p, ctypes.c_size_t, c_int, c_int, c_int]),
+    "bakan_forward_moe_block": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
+    "bakan_forward_moe_block_normed": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
+    "bakan_forward_destroy": (None, [c_void_p]),
+    "bakan_forward_num_layers": (c_int, [c_void_p]),
+    "kq_forward_set_params": (c_int, [c_void_p, c_int, ctypes.c_float]),
     # device ABI
     "kq_table_create": (c_int, [ctypes.POINTER(kq_table_desc), ctypes.POINTER(c_void_p)]),
     "kq_table_destroy": (c_int, [c_void_p]),

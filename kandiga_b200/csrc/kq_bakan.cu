@@ -16,6 +16,64 @@
 
 #include "kq_internal.h"
 
+namespace kq {
+
+int load_bkex_dir(const char* packed_dir, int num_layers, cudaStream_t s, kq_table** out, BkexInfo* info) {
+    *out = nullptr;
+    kq_table* table = nullptr;
+    auto fail = [&]() {
+        if (table) kq_table_destroy(table);
+        return -1;
+    };
+    std::vector<uint8_t> file;
+    for (int l = 0; l < num_layers; ++l) {
+        char path[1024];
+        snprintf(path, sizeof(path), "%s/layer_%02d.bin", packed_dir, l);
+        FILE* f = fopen(path, "rb");
+        if (!f) {
+            fprintf(stderr, "[kandiga] ERROR: Cannot open %s\n", path);
+            return fail();
+        }
+        fseek(f, 0, SEEK_END);
+        const long n = ftell(f);
+        fseek(f, 0, SEEK_SET);
+        file.resize(n > 0 ? (size_t)n : 0);
+        const size_t got = n > 0 ? fread(file.data(), 1, (size_t)n, f) : 0;
+        fclose(f);
+        if (n <= 0 || got != (size_t)n) {
+            fprintf(stderr, "[kandiga] ERROR: read failed for %s\n", path);
+            return fail();
+        }
+        if (l == 0) {
+            if (bkex_parse(file.data(), file.size(), info) != KQ_OK) {
+                fprintf(stderr, "[kandiga] ERROR: %s is not a BKEX layer file\n", path);
+                return fail();
+            }
+            kq_table_desc d{};
+            d.num_layers = num_layers;
+            d.num_experts = info->num_experts;
+            d.hidden = info->hidden;
+            d.inter = info->inter;
+            d.bits = info->bits;
+            d.group_size = 64;
+            d.sb_dtype = info->sb_dtype;
+            d.activation = info->activation;
+            if (kq_table_create(&d, &table) != KQ_OK) {
+                fprintf(stderr, "[kandiga] ERROR: cannot create the HBM expert table\n");
+                return fail();
+            }
+        }
+        if (kq_table_load_bkex(table, l, file.data(), file.size(), s) != KQ_OK) {
+            fprintf(stderr, "[kandiga] ERROR: cannot load %s\n", path);
+            return fail();
+        }
+    }
+    *out = table;
+    return 0;
+}
+
+}  // namespace kq
+
 using namespace kq;
 
 namespace {
@@ -267,53 +325,9 @@ extern "C" void* bakan_cpu_expert_init(const char* packed_dir, int num_layers) {
         delete e;
         return nullptr;
     }
-    std::vector<uint8_t> file;
-    for (int l = 0; l < num_layers; ++l) {
-        char path[1024];
-        snprintf(path, sizeof(path), "%s/layer_%02d.bin", packed_dir, l);
-        FILE* f = fopen(path, "rb");
-        if (!f) {
-            fprintf(stderr, "[kandiga] ERROR: Cannot open %s\n", path);
-            bakan_cpu_expert_destroy(e);
-            return nullptr;
-        }
-        fseek(f, 0, SEEK_END);
-        const long n = ftell(f);
-        fseek(f, 0, SEEK_SET);
-        file.resize(n > 0 ? (size_t)n : 0);
-        const size_t got = n > 0 ? fread(file.data(), 1, (size_t)n, f) : 0;
-        fclose(f);
-        if (n <= 0 || got != (size_t)n) {
-            fprintf(stderr, "[kandiga] ERROR: read failed for %s\n", path);
-            bakan_cpu_expert_destroy(e);
-            return nullptr;
-        }
-        if (l == 0) {
-            if (bkex_parse(file.data(), file.size(), &e->info) != KQ_OK) {
-                fprintf(stderr, "[kandiga] ERROR: %s is not a BKEX layer file\n", path);
-                bakan_cpu_expert_destroy(e);
-                return nullptr;
-            }
-            kq_table_desc d{};
-            d.num_layers = num_layers;
-            d.num_experts = e->info.num_experts;
-            d.hidden = e->info.hidden;
-            d.inter = e->info.inter;
-            d.bits = e->info.bits;
-            d.group_size = 64;
-            d.sb_dtype = e->info.sb_dtype;
-            d.activation = e->info.activation;
-            if (kq_table_create(&d, &e->table) != KQ_OK) {
-                fprintf(stderr, "[kandiga] ERROR: cannot create the HBM expert table\n");
-                bakan_cpu_expert_destroy(e);
-                return nullptr;
-            }
-        }
-        if (kq_table_load_bkex(e->table, l, file.data(), file.size(), e->stream) != KQ_OK) {
-            fprintf(stderr, "[kandiga] ERROR: cannot load %s\n", path);
-            bakan_cpu_expert_destroy(e);
-            return nullptr;
-        }
+    if (load_bkex_dir(packed_dir, num_layers, e->stream, &e->table, &e->info)) {
+        bakan_cpu_expert_destroy(e);
+        return nullptr;
     }
     if (!ensure(e, 1, kMaxExperts)) {
         fprintf(stderr, "[kandiga] ERROR: device allocation failed\n");

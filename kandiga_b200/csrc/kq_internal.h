@@ -38,6 +38,11 @@ struct BkexInfo {
 };
 int bkex_parse(const uint8_t* hdr, size_t n, BkexInfo* info);
 
+// Read packed_dir/layer_XX.bin for XX < num_layers into a new HBM table on
+// stream s.  0 on success; -1 after a "[kandiga] ERROR: ..." line on stderr,
+// with nothing left allocated.
+int load_bkex_dir(const char* packed_dir, int num_layers, cudaStream_t s, kq_table** out, BkexInfo* info);
+
 // Workspace carve-up for kq_moe_* (offsets in bytes, 256-aligned).
 struct MoeWs {
     size_t status, idx, w, act, amax, total;

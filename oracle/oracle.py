@@ -335,6 +335,15 @@ def shared_gate(x: np.ndarray, packed, scales, biases, bits, sb_dtype="f16", gs=
     return (1.0 / (1.0 + np.exp(-logit))).astype(np.float32)
 
 
+def rms_norm(x_f16: np.ndarray, w: np.ndarray, eps: float = 1e-6) -> np.ndarray:
+    """fp16(x * (1 / sqrt(mean(x^2) + eps)) * w) in fp32 arithmetic
+    (kandiga/metal/moe_block.metal:134-178); x fp16 [H], w the norm weight as fp32."""
+    x = np.asarray(x_f16, np.float16).astype(np.float32)
+    ss = np.float32((x * x).sum(dtype=np.float32))
+    scale = np.float32(1.0) / np.sqrt(np.float32(ss / np.float32(x.shape[-1])) + np.float32(eps))
+    return ((x * scale) * np.asarray(w, np.float32)).astype(np.float16)
+
+
 def group_by_expert(idx: np.ndarray):
     """Stable grouping of the T*K assignments by expert id
     (kandiga/engine.py:407-418: mergesort argsort, boundaries via diff)."""
