@@ -346,7 +346,16 @@ int kq_tq_dequant(const kq_tq_cache* c, int which, void* out_f16, void* stream);
  * storage layout; any pointer may be NULL. */
 int kq_tq_export(const kq_tq_cache* c, int which, int8_t* codes, int8_t* signs, float* scales, float* zeros,
                  void* stream);
-/* Single-query attention over the compressed cache: q [batch][q_heads][head_dim]
+/* Session persistence of the compressed cache (kandiga/engine.py:1342-1479
+ * saves and restores a session's caches).  kq_tq_save copies keys' (which = 0)
+ * or values' (1) packed storage, compact: packed [batch][heads][seq_len][head_dim/2]
+ * bytes (two nibbles a byte), scales and zeros fp32 [batch][heads][seq_len]
+ * (device).  kq_tq_restore sets the cache to `len` vectors per head from
+ * arrays in that layout, growing the capacity if needed. */
+int kq_tq_save(const kq_tq_cache* c, int which, uint8_t* packed, float* scales, float* zeros, void* stream);
+int kq_tq_restore(kq_tq_cache* c, int len, const uint8_t* k_packed, const float* k_scales, const float* k_zeros,
+                  const uint8_t* v_packed, const float* v_scales, const float* v_zeros, void* stream);
+/* Single-query attention over the compressed cache: q [batch][q_heads][head_dim]/* Single-query attention over the compressed cache: q [batch][q_heads][head_dim]
  * (q_heads a multiple of num_heads, grouped-query), out fp32 [batch][q_heads][head_dim]
  * = softmax(q K^T / sqrt(D)) V with K, V the reconstructions.  Scores are taken
  * on the codes in the rotated domain, values are accumulated there and

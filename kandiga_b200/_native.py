@@ -105,6 +105,9 @@ SIGNATURES = {
     "kq_tq_reserve": (c_int, [c_void_p, c_int, c_void_p]),
     "kq_tq_append": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "kq_tq_dequant": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
+    "kq_tq_save": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "kq_tq_restore": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                              c_void_p]),
     "kq_tq_export": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "kq_tq_attend_workspace_size": (c_size_t, [c_void_p, c_int]),
     "kq_tq_attend": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),

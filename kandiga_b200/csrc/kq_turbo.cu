@@ -762,6 +762,52 @@ extern "C" int kq_tq_export(const kq_tq_cache* c, int which, int8_t* codes, int8
     return cudaGetLastError() == cudaSuccess ? KQ_OK : KQ_ERR_CUDA;
 }
 
+// Compact copies of the packed storage (session persistence): rows of the
+// cache are `cap` vectors apart, rows of the saved arrays `len` apart.
+extern "C" int kq_tq_save(const kq_tq_cache* c, int which, uint8_t* packed, float* scales, float* zeros,
+                          void* stream) {
+    if (!c || (which != 0 && which != 1)) return KQ_ERR_ARG;
+    if (c->len == 0) return KQ_OK;
+    if (!packed || !scales || !zeros) return KQ_ERR_ARG;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t rows = (size_t)c->B * c->H, vb = (size_t)c->D / 2;
+    const bool ok =
+        cudaMemcpy2DAsync(packed, c->len * vb, c->packed[which], (size_t)c->cap * vb, c->len * vb, rows,
+                          cudaMemcpyDeviceToDevice, s) == cudaSuccess &&
+        cudaMemcpy2DAsync(scales, c->len * 4, c->scale[which], (size_t)c->cap * 4, c->len * 4, rows,
+                          cudaMemcpyDeviceToDevice, s) == cudaSuccess &&
+        cudaMemcpy2DAsync(zeros, c->len * 4, c->zero[which], (size_t)c->cap * 4, c->len * 4, rows,
+                          cudaMemcpyDeviceToDevice, s) == cudaSuccess;
+    return ok ? KQ_OK : KQ_ERR_CUDA;
+}
+
+extern "C" int kq_tq_restore(kq_tq_cache* c, int len, const uint8_t* k_packed, const float* k_scales,
+                             const float* k_zeros, const uint8_t* v_packed, const float* v_scales,
+                             const float* v_zeros, void* stream) {
+    if (!c || len < 0) return KQ_ERR_ARG;
+    if (len > 0 && (!k_packed || !k_scales || !k_zeros || !v_packed || !v_scales || !v_zeros)) return KQ_ERR_ARG;
+    if (len > c->cap) {
+        const int rc = kq_tq_reserve(c, len, stream);
+        if (rc != KQ_OK) return rc;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t rows = (size_t)c->B * c->H, vb = (size_t)c->D / 2;
+    const uint8_t* pk[2] = {k_packed, v_packed};
+    const float* sc[2] = {k_scales, v_scales};
+    const float* zr[2] = {k_zeros, v_zeros};
+    for (int w = 0; w < 2 && len > 0; ++w) {
+        if (cudaMemcpy2DAsync(c->packed[w], (size_t)c->cap * vb, pk[w], (size_t)len * vb, (size_t)len * vb, rows,
+                              cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
+            cudaMemcpy2DAsync(c->scale[w], (size_t)c->cap * 4, sc[w], (size_t)len * 4, (size_t)len * 4, rows,
+                              cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
+            cudaMemcpy2DAsync(c->zero[w], (size_t)c->cap * 4, zr[w], (size_t)len * 4, (size_t)len * 4, rows,
+                              cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+            return KQ_ERR_CUDA;
+    }
+    c->len = len;
+    return KQ_OK;
+}
+
 extern "C" size_t kq_tq_attend_workspace_size(const kq_tq_cache* c, int q_heads) {
     if (!c || q_heads <= 0) return 0;
     const size_t nchunk = ((size_t)(c->cap > 0 ? c->cap : 1) + TQ_CHUNK - 1) / TQ_CHUNK;

@@ -176,6 +176,48 @@ class TurboQuantCache:
                                        ctypes.c_void_p(zeros.data_ptr()), _stream()), "kq_tq_export")
         return codes, scales, zeros, signs
 
+    def state(self):
+        """The compressed contents: [k_packed, k_scales, k_zeros, v_packed, v_scales, v_zeros]
+        (packed uint8 [batch, heads, seq, head_dim/2], two nibbles a byte; scales and zeros
+        fp32 [batch, heads, seq]) on the cache's device, or [] when empty."""
+        if self._c is None or self.seq_len == 0:
+            return []
+        shp = (self._batch, self.num_heads, self.seq_len)
+        out = []
+        for which in (0, 1):
+            packed = torch.empty(*shp, self.head_dim // 2, dtype=torch.uint8, device=self._device)
+            scales = torch.empty(*shp, dtype=torch.float32, device=self._device)
+            zeros = torch.empty_like(scales)
+            N.check(self._lib.kq_tq_save(self._c, which, ctypes.c_void_p(packed.data_ptr()),
+                                         ctypes.c_void_p(scales.data_ptr()), ctypes.c_void_p(zeros.data_ptr()),
+                                         _stream()), "kq_tq_save")
+            out += [packed, scales, zeros]
+        return out
+
+    def load_state(self, state, device=None):
+        """Replace the contents with arrays from ``state()`` (torch or numpy, any device)."""
+        if len(state) != 6:
+            raise ValueError("a TurboQuantCache state holds six arrays")
+        kp = torch.as_tensor(state[0])
+        if kp.dim() != 4 or kp.shape[1] != self.num_heads or kp.shape[3] != self.head_dim // 2:
+            raise ValueError(f"packed codes must be [batch, {self.num_heads}, seq, {self.head_dim // 2}]")
+        b, _, t, _ = kp.shape
+        dev = torch.device(device) if device is not None else (self._device or torch.device("cuda"))
+        if self._c is None:
+            self._create(b, dev)
+        elif b != self._batch:
+            raise ValueError(f"batch {b} differs from the cache's batch {self._batch}")
+        arrs = []
+        for i, a in enumerate(state):
+            want = torch.uint8 if i % 3 == 0 else torch.float32
+            a = torch.as_tensor(a).to(self._device).contiguous()
+            if a.dtype != want or a.shape[:3] != (b, self.num_heads, t):
+                raise ValueError("state arrays do not match the cache")
+            arrs.append(a)
+        p = [ctypes.c_void_p(a.data_ptr()) for a in arrs]
+        N.check(self._lib.kq_tq_restore(self._c, t, *p, _stream()), "kq_tq_restore")
+        self.seq_len = int(self._lib.kq_tq_seq_len(self._c))
+
     def attend(self, q: torch.Tensor, return_scores: bool = False):
         """softmax(q K^T / sqrt(D)) V over the compressed cache for one query per head.
         q [batch, q_heads, head_dim] (q_heads a multiple of num_heads); returns fp32
@@ -197,3 +239,81 @@ class TurboQuantCache:
                                        ctypes.c_void_p(scores.data_ptr()) if scores is not None else None,
                                        ctypes.c_void_p(ws.data_ptr()), ws.numel(), _stream()), "kq_tq_attend")
         return (out, scores) if return_scores else out
+
+
+# ---- session persistence -----------------------------------------------------------------------
+
+_DTYPE_NAME = {torch.float16: "float16", torch.bfloat16: "bfloat16", torch.float32: "float32", torch.uint8: "uint8"}
+
+
+def save_session(path: str, caches, history=None, tokens_fed: int = 0, model: str = ""):
+    """Save per-layer caches in the reference's session layout (kandiga/engine.py:1342-1404):
+    ``np.savez_compressed(path, cache_{i}_{j}=...)`` and ``path.replace('.npz', '_meta.json')``
+    holding history, tokens_fed, model, dtype_map ({shape, dtype} per array) and layer_info
+    ({type, n, offset} per layer).  A layer is a TurboQuantCache (saved compressed: its six
+    packed arrays, with head_dim, num_heads and seed in layer_info) or a [keys, values] pair of
+    tensors [batch, heads, seq, head_dim] (saved as the reference saves a KVCache: float32 as
+    is, 16-bit dtypes as uint16 bit patterns)."""
+    import json
+    arrays, dtype_map, layer_info = {}, {}, {}
+    for i, layer in enumerate(caches):
+        if isinstance(layer, TurboQuantCache):
+            tensors = layer.state()
+            layer_info[str(i)] = {"type": "TurboQuantCache", "n": 6, "offset": layer.seq_len,
+                                  "head_dim": layer.head_dim, "num_heads": layer.num_heads, "seed": layer._seed}
+        elif layer is not None:
+            tensors = list(layer)
+            layer_info[str(i)] = {"type": "KVCache", "n": len(tensors),
+                                  "offset": int(tensors[0].shape[2]) if tensors else 0}
+        else:
+            continue
+        for j, t in enumerate(tensors):
+            t = torch.as_tensor(t).detach().cpu().contiguous()
+            key = f"cache_{i}_{j}"
+            if t.dtype in (torch.float16, torch.bfloat16):
+                arrays[key] = t.view(torch.int16).numpy().view(np.uint16)
+            else:
+                arrays[key] = t.numpy()
+            dtype_map[key] = {"shape": list(t.shape), "dtype": _DTYPE_NAME[t.dtype]}
+    np.savez_compressed(path, **arrays)
+    with open(path.replace(".npz", "_meta.json"), "w") as f:
+        json.dump({"history": list(history or []), "tokens_fed": int(tokens_fed), "model": model,
+                   "dtype_map": dtype_map, "layer_info": layer_info}, f)
+
+
+def load_session(path: str, model: str = None, device="cuda"):
+    """Read a session written by save_session: (caches, meta).  TurboQuantCache layers are
+    rebuilt on `device` from their packed arrays; other layers come back as lists of tensors
+    on `device` with their saved dtypes.  Raises ValueError if `model` is given and differs
+    from the saved one (kandiga/engine.py:1421-1422)."""
+    import json
+    with open(path.replace(".npz", "_meta.json")) as f:
+        meta = json.load(f)
+    if model is not None and meta["model"] != model:
+        raise ValueError(f"Session was for {meta['model']}, not {model}")
+    data = np.load(path)
+    dtype_map, layer_info = meta.get("dtype_map", {}), meta.get("layer_info", {})
+    n_layers = 1 + max((int(k) for k in layer_info), default=-1)
+    caches = [None] * n_layers
+    for k, info in layer_info.items():
+        i = int(k)
+        tensors = []
+        for j in range(info["n"]):
+            key = f"cache_{i}_{j}"
+            spec = dtype_map[key]
+            a = data[key]
+            if spec["dtype"] in ("float16", "bfloat16"):
+                t = torch.from_numpy(a.view(np.int16).copy()).view(
+                    torch.float16 if spec["dtype"] == "float16" else torch.bfloat16)
+            else:
+                t = torch.from_numpy(np.ascontiguousarray(a))
+            tensors.append(t.reshape(spec["shape"]))
+        if info["type"] == "TurboQuantCache":
+            c = TurboQuantCache(info["head_dim"], info["num_heads"], seed=info["seed"],
+                                capacity=max(info["offset"], 1), device=device)
+            if info["offset"] > 0:
+                c.load_state(tensors, device=device)
+            caches[i] = c
+        else:
+            caches[i] = [t.to(device) for t in tensors]
+    return caches, meta

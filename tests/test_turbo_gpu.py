@@ -177,3 +177,37 @@ def test_growth_preserves_contents(gpu):
     after = cache.export(0)
     for a, b_ in zip(before, after):
         assert torch.equal(a, b_[:, :, :7])
+
+
+def test_session_round_trip_of_compressed_cache(gpu, tmp_path):
+    """TurboQuantCache layers saved through save_session keep their packed codes:
+    after load_session the reconstructions and attention are bit-identical, and
+    appending more tokens gives what an unsaved cache gives."""
+    from kandiga_b200.kv_compress import TurboQuantCache, load_session, save_session
+    g = torch.Generator(device="cuda").manual_seed(3)
+    caches, ref = [], []
+    for seed, D, Hh, T in ((42, 128, 4, 300), (7, 64, 2, 17)):
+        k = torch.randn(1, Hh, T, D, generator=g, device="cuda").half()
+        v = torch.randn(1, Hh, T, D, generator=g, device="cuda").half()
+        c = TurboQuantCache(D, Hh, seed=seed, capacity=64)
+        c.update(k, v)
+        r = TurboQuantCache(D, Hh, seed=seed, capacity=64)
+        r.update(k, v)
+        caches.append(c)
+        ref.append(r)
+    path = str(tmp_path / "sess.npz")
+    save_session(path, caches, history=["x"], tokens_fed=317, model="tiny")
+    got, meta = load_session(path, model="tiny")
+    assert meta["layer_info"]["0"]["type"] == "TurboQuantCache" and meta["layer_info"]["0"]["offset"] == 300
+    for c, d, r in zip(caches, got, ref):
+        assert d.seq_len == c.seq_len and d.head_dim == c.head_dim and d.num_heads == c.num_heads
+        assert torch.equal(d.keys, c.keys) and torch.equal(d.values, c.values)
+        for a, b in zip(d.state(), c.state()):
+            assert torch.equal(a, b)
+        q = torch.randn(1, c.num_heads, c.head_dim, generator=g, device="cuda").half()
+        assert torch.equal(d.attend(q), c.attend(q))
+        k2 = torch.randn(1, c.num_heads, 40, c.head_dim, generator=g, device="cuda").half()
+        v2 = torch.randn(1, c.num_heads, 40, c.head_dim, generator=g, device="cuda").half()
+        d.update(k2, v2)
+        r.update(k2, v2)
+        assert torch.equal(d.keys, r.keys) and torch.equal(d.values, r.values)
