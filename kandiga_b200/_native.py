@@ -105,6 +105,8 @@ SIGNATURES = {
     "kq_tq_reserve": (c_int, [c_void_p, c_int, c_void_p]),
     "kq_tq_append": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "kq_tq_dequant": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
+    "kq_requantize_mlx": (c_int, [c_void_p, c_void_p, c_void_p, ctypes.c_long, c_int, c_int, c_int, c_int,
+                                  c_void_p, c_void_p, c_void_p, c_void_p]),
     "kq_tq_save": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "kq_tq_restore": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                               c_void_p]),
