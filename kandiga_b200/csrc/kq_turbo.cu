@@ -254,8 +254,14 @@ __device__ __forceinline__ float nib_1p(uint32_t w, int k) {
     return __uint_as_float((b & 0x00780000u) | 0x3F800000u);
 }
 
-constexpr int TQ_ATT_THREADS = 128;
-constexpr int TQ_CHUNK = 256;  // tokens per CTA
+#ifndef KQ_TQ_ATT_THREADS
+#define KQ_TQ_ATT_THREADS 128
+#endif
+#ifndef KQ_TQ_CHUNK
+#define KQ_TQ_CHUNK 256
+#endif
+constexpr int TQ_ATT_THREADS = KQ_TQ_ATT_THREADS;
+constexpr int TQ_CHUNK = KQ_TQ_CHUNK;  // tokens per CTA
 constexpr int TQ_MAXG = 8;     // query heads per KV head
 
 struct TqAttParams {
@@ -367,22 +373,24 @@ __global__ void __launch_bounds__(TQ_ATT_THREADS) tq_attend_kernel(TqAttParams p
     mbar_wait(bar, 0, p.status);
     const float sqrt_d = sqrtf((float)D);
 
-    // scores on the codes
+    // scores on the codes; a thread's 16 query elements stay in registers for all its tokens
     const int npass = (n + TPP - 1) / TPP;
-    for (int i = 0; i < npass; ++i) {
-        const int tl = i * TPP + slot;
-        const int tc = tl < n ? tl : 0;
-        const uint2 pk = *reinterpret_cast<const uint2*>(kc + tc * CB + sub * 8);
-        const float s = ksc[tc], lo = kze[tc];
-        for (int g = 0; g < G; ++g) {
-            const float* q = qr + g * (D + 1) + sub * 16;
+    for (int g = 0; g < G; ++g) {
+        float qv[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) qv[e] = qr[g * (D + 1) + sub * 16 + e];
+        const float qs = qr[g * (D + 1) + D];
+        for (int i = 0; i < npass; ++i) {
+            const int tl = i * TPP + slot;
+            const int tc = tl < n ? tl : 0;
+            const uint2 pk = *reinterpret_cast<const uint2*>(kc + tc * CB + sub * 8);
+            const float s = ksc[tc], lo = kze[tc];
             // a = sum q (1 + v/8) with v = c + sigma/2; q.v = 8 (a - sum q)
             float a = 0.f;
 #pragma unroll
-            for (int e = 0; e < 16; ++e) a = fmaf(q[e], nib_1p(e < 8 ? pk.x : pk.y, e & 7), a);
+            for (int e = 0; e < 16; ++e) a = fmaf(qv[e], nib_1p(e < 8 ? pk.x : pk.y, e & 7), a);
 #pragma unroll
             for (int o = TPT / 2; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-            const float qs = qr[g * (D + 1) + D];
             const float score = __fdiv_rn(fmaf(s, 8.f * (a - qs), (lo - 0.25f * s) * qs), sqrt_d);
             if (tl < n && sub == 0) {
                 sc[g * TQ_CHUNK + tl] = score;
