@@ -294,10 +294,14 @@ __global__ void __launch_bounds__(256) tq_rotate_q_kernel(TqAttParams p) {
     const size_t qoff = ((size_t)b * Hq + qh) * D;
     if (tid < D) qs[tid] = load_as_float(p.q, p.q_dtype, qoff + tid);
     __syncthreads();
-    float a = 0.f;
+    // all of this thread's R loads are issued before the first FMA: one memory round trip
     const int d0 = half * (D / SPLIT);
-#pragma unroll 16
-    for (int d = d0; d < d0 + D / SPLIT; ++d) a = fmaf(qs[d], p.R[d * D + j], a);
+    float r[D / SPLIT];
+#pragma unroll
+    for (int d = 0; d < D / SPLIT; ++d) r[d] = __ldg(p.R + (size_t)(d0 + d) * D + j);
+    float a = 0.f;
+#pragma unroll
+    for (int d = 0; d < D / SPLIT; ++d) a = fmaf(qs[d0 + d], r[d], a);
     part[half][j] = a;
     __syncthreads();
     if (tid < D) {
@@ -488,13 +492,28 @@ __global__ void __launch_bounds__(256) tq_combine_kernel(TqAttParams p) {
     float L = 0.f, A[DPL];
 #pragma unroll
     for (int i = 0; i < DPL; ++i) A[i] = 0.f;
-#pragma unroll 4
-    for (int c = w; c < p.nchunk; c += NWC) {
-        const float* pc = part + (size_t)c * (D + 2);
-        const float f = expf(pc[D] - M);
-        L = fmaf(pc[D + 1], f, L);
+    // warp w merges chunks w, w + NWC, ...: a batch of CB chunks' loads is issued
+    // before its arithmetic, in the same chunk order as one chunk at a time
+    constexpr int CB = 8;
+    for (int c0 = w; c0 < p.nchunk; c0 += NWC * CB) {
+        float mv[CB], lv[CB], av[CB][DPL];
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) A[i] = fmaf(pc[lane + 32 * i], f, A[i]);
+        for (int u = 0; u < CB; ++u) {
+            const int c = c0 + u * NWC;
+            const float* pc = part + (size_t)(c < p.nchunk ? c : 0) * (D + 2);
+            mv[u] = c < p.nchunk ? pc[D] : -INFINITY;
+            lv[u] = pc[D + 1];
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) av[u][i] = pc[lane + 32 * i];
+        }
+#pragma unroll
+        for (int u = 0; u < CB; ++u) {
+            if (c0 + u * NWC >= p.nchunk) break;
+            const float f = expf(mv[u] - M);
+            L = fmaf(lv[u], f, L);
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) A[i] = fmaf(av[u][i], f, A[i]);
+        }
     }
 #pragma unroll
     for (int i = 0; i < DPL; ++i) pacc[w][lane + 32 * i] = A[i];
@@ -509,11 +528,22 @@ __global__ void __launch_bounds__(256) tq_combine_kernel(TqAttParams p) {
         orot[tid] = a / l;
     }
     __syncthreads();
+    // un-rotate: out[d] = sum_k orot[k] R^T[k][d]; thread (d, half) takes half of k,
+    // its R^T loads issued together
+    constexpr int KS = 256 / D;
+    const int d = tid % D, hk = tid / D, k0 = hk * (D / KS);
+    float rt[D / KS];
+#pragma unroll
+    for (int k = 0; k < D / KS; ++k) rt[k] = __ldg(p.RT + (size_t)(k0 + k) * D + d);
+    float o = 0.f;
+#pragma unroll
+    for (int k = 0; k < D / KS; ++k) o = fmaf(orot[k0 + k], rt[k], o);
+    pacc[hk][d] = o;  // pacc is free again: its sums were read before the barrier above
+    __syncthreads();
     if (tid < D) {
-        float o = 0.f;  // un-rotate: out[d] = sum_k orot[k] R^T[k][d]
-#pragma unroll 16
-        for (int k = 0; k < D; ++k) o = fmaf(orot[k], p.RT[k * D + tid], o);
-        p.out[((size_t)b * Hq + qh) * D + tid] = o;
+        float v = 0.f;
+        for (int h2 = 0; h2 < KS; ++h2) v += pacc[h2][tid];
+        p.out[((size_t)b * Hq + qh) * D + tid] = v;
     }
 }
 
