@@ -47,20 +47,22 @@ __global__ void __launch_bounds__(TQ3_THREADS) tq3_gemv_kernel(const uint8_t* __
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid < 64) lut[tid] = make_float2(tq3_centroids[tid & 7], tq3_centroids[tid >> 3]);
     const float inv = sqrtf(32.f);
-    // rotate x: warp per (token, block), lane = element; four blocks' loads in flight per warp
-    constexpr int NWARP = TQ3_THREADS / 32;
-    for (int j0 = warp; j0 < TT * nb; j0 += 4 * NWARP) {
-        float v[4];
+    // rotate x: warp per (token, block) of the T real tokens, lane = element;
+    // XB blocks' loads in flight per warp (rows of slots t >= T are never stored)
+    constexpr int NWARP = TQ3_THREADS / 32, XB = 16;
+    const int jobs = min(T, TT) * nb;
+    for (int j0 = warp; j0 < jobs; j0 += XB * NWARP) {
+        float v[XB];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < XB; ++u) {
             const int job = j0 + u * NWARP;
             const int t = job / nb, b = job % nb;
-            v[u] = (job < TT * nb && t < T) ? load_as_float(x, x_dtype, (size_t)t * cols + (size_t)b * 32 + lane) : 0.f;
+            v[u] = job < jobs ? load_as_float(x, x_dtype, (size_t)t * cols + (size_t)b * 32 + lane) : 0.f;
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < XB; ++u) {
             const int job = j0 + u * NWARP;
-            if (job >= TT * nb) break;
+            if (job >= jobs) break;
             const int t = job / nb, b = job % nb;
             float w = v[u] * tq3_signs[lane];
 #pragma unroll
