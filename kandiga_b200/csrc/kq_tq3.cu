@@ -85,45 +85,57 @@ __global__ void __launch_bounds__(TQ3_THREADS) tq3_gemv_kernel(const uint8_t* __
         float acc[TT];
 #pragma unroll
         for (int t = 0; t < TT; ++t) acc[t] = 0.f;
-        for (int b = lane; b < nb; b += 32) {
-            const uint32_t* bw = reinterpret_cast<const uint32_t*>(rb + (size_t)b * BB);
-            uint32_t w[BB / 4];
+        // RB blocks per lane are loaded before any is used: one memory round trip per RB blocks
+        constexpr int RB = 4;
+        for (int b0 = lane; b0 < nb; b0 += 32 * RB) {
+            uint32_t wr[RB][BB / 4];
 #pragma unroll
-            for (int i = 0; i < BB / 4; ++i) w[i] = __ldg(bw + i);
-            const __half2 d01 = *reinterpret_cast<const __half2*>(&w[0]);
-            const float d0 = __low2float(d01), d1 = __high2float(d01);
-            float m0 = 0.f, m1 = 0.f;
-            constexpr int CW = BB == 20 ? 2 : 1;  // first word of the codes
-            if constexpr (BB == 20) {
-                const __half2 m01 = *reinterpret_cast<const __half2*>(&w[1]);
-                m0 = __low2float(m01);
-                m1 = __high2float(m01);
+            for (int u = 0; u < RB; ++u) {
+                const int b = b0 + 32 * u;
+                const uint32_t* bw = reinterpret_cast<const uint32_t*>(rb + (size_t)(b < nb ? b : 0) * BB);
+#pragma unroll
+                for (int i = 0; i < BB / 4; ++i) wr[u][i] = b < nb ? __ldg(bw + i) : 0u;
             }
-            uint32_t grp[4];
-            grp[0] = w[CW] & 0xFFFFFFu;
-            grp[1] = (w[CW] >> 24) | ((w[CW + 1] & 0xFFFFu) << 8);
-            grp[2] = (w[CW + 1] >> 16) | ((w[CW + 2] & 0xFFu) << 16);
-            grp[3] = w[CW + 2] >> 8;
 #pragma unroll
-            for (int t = 0; t < TT; ++t) {
-                const float* xb = xr + ((size_t)t * nb + b) * TQ3_XSTRIDE;
-                float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-                for (int g = 0; g < 4; ++g) {
-#pragma unroll
-                    for (int r = 0; r < 8; r += 4) {
-                        const float4 xv = *reinterpret_cast<const float4*>(xb + g * 8 + r);
-                        const float2 c0 = lut[(grp[g] >> (3 * r)) & 63u];
-                        const float2 c1 = lut[(grp[g] >> (3 * r + 6)) & 63u];
-                        float& a = g < 2 ? a0 : a1;
-                        a = fmaf(c0.x, xv.x, a);
-                        a = fmaf(c0.y, xv.y, a);
-                        a = fmaf(c1.x, xv.z, a);
-                        a = fmaf(c1.y, xv.w, a);
-                    }
+            for (int u = 0; u < RB; ++u) {
+                const int b = b0 + 32 * u;
+                if (b >= nb) break;
+                const uint32_t* w = wr[u];
+                const __half2 d01 = *reinterpret_cast<const __half2*>(&w[0]);
+                const float d0 = __low2float(d01), d1 = __high2float(d01);
+                float m0 = 0.f, m1 = 0.f;
+                constexpr int CW = BB == 20 ? 2 : 1;  // first word of the codes
+                if constexpr (BB == 20) {
+                    const __half2 m01 = *reinterpret_cast<const __half2*>(&w[1]);
+                    m0 = __low2float(m01);
+                    m1 = __high2float(m01);
                 }
-                const float* hb = hs + (size_t)t * 2 * nb + 2 * b;
-                acc[t] += fmaf(d0, a0, fmaf(m0, hb[0], fmaf(d1, a1, m1 * hb[1])));
+                uint32_t grp[4];
+                grp[0] = w[CW] & 0xFFFFFFu;
+                grp[1] = (w[CW] >> 24) | ((w[CW + 1] & 0xFFFFu) << 8);
+                grp[2] = (w[CW + 1] >> 16) | ((w[CW + 2] & 0xFFu) << 16);
+                grp[3] = w[CW + 2] >> 8;
+    #pragma unroll
+                for (int t = 0; t < TT; ++t) {
+                    const float* xb = xr + ((size_t)t * nb + b) * TQ3_XSTRIDE;
+                    float a0 = 0.f, a1 = 0.f;
+    #pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+    #pragma unroll
+                        for (int r = 0; r < 8; r += 4) {
+                            const float4 xv = *reinterpret_cast<const float4*>(xb + g * 8 + r);
+                            const float2 c0 = lut[(grp[g] >> (3 * r)) & 63u];
+                            const float2 c1 = lut[(grp[g] >> (3 * r + 6)) & 63u];
+                            float& a = g < 2 ? a0 : a1;
+                            a = fmaf(c0.x, xv.x, a);
+                            a = fmaf(c0.y, xv.y, a);
+                            a = fmaf(c1.x, xv.z, a);
+                            a = fmaf(c1.y, xv.w, a);
+                        }
+                    }
+                    const float* hb = hs + (size_t)t * 2 * nb + 2 * b;
+                    acc[t] += fmaf(d0, a0, fmaf(m0, hb[0], fmaf(d1, a1, m1 * hb[1])));
+                }
             }
         }
 #pragma unroll
