@@ -101,6 +101,14 @@ def gpu_combine(per_k, weights, residual=None, shared=None, gate=None, out_dtype
     return out
 
 
+def table_local_moe(table):
+    """One-rank path: the whole routed MLP of the layer on this rank's table
+    (grouped by expert inside kq_moe_prefill / kq_moe_decode), combined over K in fp32."""
+    def run(layer: int, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        return table.moe(layer, x, idx=idx, weights=w, combine=True, out_dtype=torch.float32)["out"]
+    return run
+
+
 def table_compute(table):
     """Expert compute on this rank's kq_table: one assignment per received row."""
     def run(layer: int, rows: torch.Tensor, local_ids: torch.Tensor) -> torch.Tensor:
@@ -118,9 +126,13 @@ class ExpertParallelMoE:
 
     def __init__(self, placement: ExpertPlacement, rank: int, top_k: int,
                  compute: Callable, router: Callable = gpu_router, combine: Callable = gpu_combine,
-                 group=None):
+                 group=None, local_moe: Optional[Callable] = None):
+        """compute(layer, rows, local_ids) -> rows' expert outputs (one assignment a row);
+        local_moe(layer, x, idx, w) -> [T, H] routed sum, used instead of the exchange when
+        there is one rank (no permutation of the T*K rows)."""
         self.pl, self.rank, self.k, self.group = placement, rank, top_k, group
         self.compute, self.router, self.combine = compute, router, combine
+        self.local_moe = local_moe
         self._owner = None
         self._local = None
 
@@ -140,6 +152,12 @@ class ExpertParallelMoE:
         dev = x.device
         owner, local = self._maps(dev)
         idx, w = self.router(logits, K)
+        if G == 1 and self.local_moe is not None and not return_parts:
+            local_idx = local[idx.to(torch.int64)].to(torch.int32).contiguous()
+            routed = self.local_moe(layer, x, local_idx, w)
+            ones = torch.ones(T, 1, dtype=torch.float32, device=dev)
+            return self.combine(routed.reshape(T, 1, H), ones, residual=residual, shared=shared, gate=gate,
+                                out_dtype=out_dtype)
         flat = idx.reshape(-1).to(torch.int64)
         dest = owner[flat]
         order = torch.argsort(dest, stable=True)
