@@ -277,6 +277,54 @@ int kq_combine(const void* y, int y_dtype, const float* weights, int T, int K, i
 /* Read and clear the device status word of a workspace (synchronises `stream`). */
 int kq_status_read(void* workspace, uint32_t* status, void* stream);
 
+/* ---- expert spill: tables larger than HBM ------------------------------------
+ * The reference streams experts that do not fit in memory from the SSD and
+ * warms the page cache ahead of use with a cross-layer predictor
+ * (kandiga/engine.py:577-668: the next layer's router applied to this layer's
+ * input, top-K per token, union over tokens).  Here the whole table
+ * (layers x experts, in the HBM tile layout) sits in pinned, device-mapped host
+ * memory, and every layer keeps `slots` experts in an HBM pool.  The pool is
+ * an ordinary kq_table with `slots` experts per layer, so kq_moe_decode /
+ * kq_moe_prefill run on it unchanged, given slot ids in place of expert ids.
+ * kq_spill_fetch turns expert ids into slot ids on the device and copies the
+ * experts that are not resident over the host link into the least recently
+ * used slots, with no host round trip (stream-ordered, graph-capturable).
+ * Calls for one layer must be ordered (one stream, or events); calls for
+ * different layers may overlap (each layer has its own slots and state). */
+typedef struct kq_spill kq_spill;
+#define KQ_DEV_CAPACITY 8u /* kq_spill_fetch: more distinct experts than slots; the rest got slot id -1 */
+/* slots <= 1024 and <= num_experts, num_experts <= 16384.  Allocates the host
+ * store (pinned, mapped) and the pool; residency starts empty. */
+int kq_spill_create(const kq_table_desc* desc, int slots, kq_spill** out);
+int kq_spill_destroy(kq_spill* s);
+/* The HBM pool: a kq_table of desc.num_layers layers x `slots` experts. */
+const kq_table* kq_spill_pool(const kq_spill* s);
+size_t kq_spill_host_bytes(const kq_spill* s);
+/* Copy layer `src_layer` of a device table of the same shape (experts,
+ * hidden, inter, bits, scale dtype, activation) into layer `layer` of the
+ * host store, and empty that layer's residency. */
+int kq_spill_store_layer(kq_spill* s, int layer, const kq_table* src, int src_layer, void* stream);
+/* ids [n]: expert ids of `layer` (any order, repeats allowed).  Writes
+ * slot_ids [n] (may be NULL) and makes every named expert resident: hits
+ * refresh the slot's use stamp, misses (in expert-id order) take the least
+ * recently used slots not named by this call (ties: lowest slot) and are
+ * copied from host memory.  An id outside [0, num_experts) gets slot -1 and
+ * latches KQ_DEV_BAD_EXPERT; more distinct ids than slots latches
+ * KQ_DEV_CAPACITY (the experts that did not fit get -1).  Two kernels. */
+int kq_spill_fetch(kq_spill* s, int layer, const int32_t* ids, int n, int32_t* slot_ids, void* stream);
+/* kq_spill_fetch without slot ids and without KQ_DEV_CAPACITY: brings
+ * predicted experts in ahead of use and stops when every slot holds an
+ * expert of this call (the background prefetch of kandiga/engine.py:577-616,
+ * issued on a second stream while the current layer computes). */
+int kq_spill_prefetch(kq_spill* s, int layer, const int32_t* ids, int n, void* stream);
+/* counters since the last reset: [0] hits (distinct resident experts named),
+ * [1] misses (experts copied), [2] bytes copied, [3] status bits.  Host
+ * array; synchronises `stream`; reset != 0 clears them. */
+int kq_spill_stats(kq_spill* s, uint64_t out[4], int reset, void* stream);
+/* Residency of `layer` (host arrays, synchronises `stream`):
+ * slot_of [num_experts] (slot or -1), owner [slots] (expert or -1). */
+int kq_spill_residency(const kq_spill* s, int layer, int32_t* slot_of, int32_t* owner, void* stream);
+
 /* ---- dense quantized GEMV (tq3 / shared-layer path) -------------------------- */
 
 /* Dense MLX-affine matrix [rows][cols].  With `pair` set, two matrices of the
@@ -365,7 +413,7 @@ int kq_tq_export(const kq_tq_cache* c, int which, int8_t* codes, int8_t* signs, 
 int kq_tq_save(const kq_tq_cache* c, int which, uint8_t* packed, float* scales, float* zeros, void* stream);
 int kq_tq_restore(kq_tq_cache* c, int len, const uint8_t* k_packed, const float* k_scales, const float* k_zeros,
                   const uint8_t* v_packed, const float* v_scales, const float* v_zeros, void* stream);
-/* Single-query attention over the compressed cache: q [batch][q_heads][head_dim]/* Single-query attention over the compressed cache: q [batch][q_heads][head_dim]
+/* Single-query attention over the compressed cache: q [batch][q_heads][head_dim]
  * (q_heads a multiple of num_heads, grouped-query), out fp32 [batch][q_heads][head_dim]
  * = softmax(q K^T / sqrt(D)) V with K, V the reconstructions.  Scores are taken
  * on the codes in the rotated domain, values are accumulated there and

@@ -21,7 +21,7 @@ KQ_ERR_CAPACITY = 8
 ERRORS_INV = {v: k for k, v in ERRORS.items()}
 DT_F16, DT_BF16, DT_F32 = 0, 1, 2
 ACT_SILU, ACT_GELU_TANH = 0, 1
-DEV_BAD_EXPERT, DEV_WAIT_TIMEOUT, DEV_BAD_INDEX = 1, 2, 4
+DEV_BAD_EXPERT, DEV_WAIT_TIMEOUT, DEV_BAD_INDEX, DEV_CAPACITY = 1, 2, 4, 8
 
 
 class KQError(RuntimeError):
@@ -111,6 +111,15 @@ SIGNATURES = {
     "kq_tq_restore": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                               c_void_p]),
     "kq_tq_export": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "kq_spill_create": (c_int, [ctypes.POINTER(kq_table_desc), c_int, ctypes.POINTER(c_void_p)]),
+    "kq_spill_destroy": (c_int, [c_void_p]),
+    "kq_spill_pool": (c_void_p, [c_void_p]),
+    "kq_spill_host_bytes": (c_size_t, [c_void_p]),
+    "kq_spill_store_layer": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p]),
+    "kq_spill_fetch": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p]),
+    "kq_spill_prefetch": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p]),
+    "kq_spill_stats": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_uint64), c_int, c_void_p]),
+    "kq_spill_residency": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "kq_tq_attend_workspace_size": (c_size_t, [c_void_p, c_int]),
     "kq_tq_attend": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
 }

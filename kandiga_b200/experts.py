@@ -53,13 +53,18 @@ class ExpertTable:
     """
 
     def __init__(self, num_layers, num_experts, hidden, inter, bits=3, sb_dtype="f16",
-                 activation="silu"):
+                 activation="silu", _handle=None):
         self.lib = N.load()
-        d = N.kq_table_desc(num_layers, num_experts, hidden, inter, bits, 64,
-                            N.DT_F16 if sb_dtype == "f16" else N.DT_BF16,
-                            N.ACT_GELU_TANH if activation == "gelu" else N.ACT_SILU)
-        h = ctypes.c_void_p()
-        N.check(self.lib.kq_table_create(ctypes.byref(d), ctypes.byref(h)), "kq_table_create")
+        if _handle is None:
+            d = N.kq_table_desc(num_layers, num_experts, hidden, inter, bits, 64,
+                                N.DT_F16 if sb_dtype == "f16" else N.DT_BF16,
+                                N.ACT_GELU_TANH if activation == "gelu" else N.ACT_SILU)
+            h = ctypes.c_void_p()
+            N.check(self.lib.kq_table_create(ctypes.byref(d), ctypes.byref(h)), "kq_table_create")
+            self._owned = True
+        else:  # a table owned by another object (the HBM pool of a SpillTable)
+            h = ctypes.c_void_p(_handle)
+            self._owned = False
         self.handle = h
         self.num_layers, self.num_experts, self.hidden, self.inter = num_layers, num_experts, hidden, inter
         self.bits, self.sb_dtype, self.activation = bits, sb_dtype, activation
@@ -68,7 +73,7 @@ class ExpertTable:
 
     def __del__(self):
         try:
-            if getattr(self, "handle", None):
+            if getattr(self, "handle", None) and getattr(self, "_owned", True):
                 self.lib.kq_table_destroy(self.handle)
                 self.handle = None
         except Exception:
