@@ -146,6 +146,49 @@ int bakan_forward_num_layers(void* engine);
  * epsilon (default 1e-6).  KQ_OK or KQ_ERR_ARG. */
 int kq_forward_set_params(void* engine, int top_k, float rms_norm_eps);
 
+/* Whole-model single-token decode step (kandiga/metal/full_forward.h:43-220,
+ * the reference's bakan_full_* ABI; its implementation full_forward_lg.m
+ * hard-codes one model).  The model shape comes from `packed_expert_dir`/config.json
+ * (hidden_size, intermediate_size, num_hidden_layers, num_attention_heads,
+ * num_key_value_heads, head_dim, vocab_size, rms_norm_eps, rope_theta,
+ * partial_rotary_factor; max_cache_len, default 4096, sizes the KV cache).
+ * Layers: input RMSNorm, q|k|v (separate q_proj/k_proj/v_proj or the
+ * reference's fused self_attn.combined_proj; a q_proj of 2 x heads x head_dim
+ * rows carries the per-head output gate), optional q_norm/k_norm, RoPE, GQA
+ * decode attention over the fp16 cache, o_proj + residual, post-attention
+ * RMSNorm, gate/up SwiGLU, down + residual; then norm and lm_head (or the tied
+ * quantized embedding).  Linears are MLX-affine 3/4-bit (weight uint32, scales
+ * and biases fp16/bf16); head_dim 64/128/256, 1/2/4/8 q heads per kv head,
+ * vocab_size a multiple of 16.  Names may carry the "language_model.model." /
+ * "model." prefixes.  Weight dtype codes: 0 fp16, 1 bf16, 2 fp32, 3 packed uint32.
+ * Host pointers throughout; calls are synchronous; 0 / -1 with a
+ * "[kandiga] ERROR" line, as the reference. */
+void* bakan_full_init(const char* packed_expert_dir, int num_layers);          /* full_forward.h:43 */
+int bakan_full_set_weight(void* engine, const char* name, const void* data, size_t size, int ndim,
+                          const int64_t* shape, int dtype);                     /* full_forward.h:61 */
+int bakan_full_build(void* engine);                                              /* full_forward.h:73 */
+int bakan_full_forward(void* engine, int token_id, int position, float* logits_out,
+                       int* vocab_size_out);                                     /* full_forward.h:90 */
+int bakan_full_prefill(void* engine, const int32_t* token_ids, int num_tokens, float* logits_out,
+                       int* vocab_size_out);                                     /* full_forward.h:114 */
+void bakan_full_reset_cache(void* engine);                                       /* full_forward.h:121 */
+void bakan_full_destroy(void* engine);                                           /* full_forward.h:126 */
+int bakan_full_num_layers(void* engine);                                         /* full_forward.h:131 */
+int bakan_full_vocab_size(void* engine);                                         /* full_forward.h:132 */
+void bakan_full_set_debug(void* engine, int enable);                             /* full_forward.h:138 */
+int bakan_full_set_kv_cache(void* engine, int attn_layer_idx, const void* keys_data, const void* values_data,
+                            int seq_len, int num_kv_heads, int head_dim);        /* full_forward.h:157 */
+int bakan_full_set_position(void* engine, int position);                         /* full_forward.h:214 */
+/* bakan_full_init with the config given as JSON text (no file). */
+void* kq_full_init_json(const char* config_json, const char* packed_dir, int num_layers);
+/* next position the engine expects (one past the last token run) */
+int kq_full_position(void* engine);
+/* `steps` decode steps of token_id at positions position.. (device-resident
+ * logits, no host copies but the 12-byte token/position upload per step),
+ * timed with CUDA events on the engine's stream: *device_ms.  For benchmarks;
+ * no counterpart in the reference. */
+int kq_full_time_steps(void* engine, int token_id, int position, int steps, float* device_ms);
+
 /* ---- 2. device ABI ------------------------------------------------------------ */
 
 typedef struct kq_table kq_table; /* HBM-resident routed-expert table (all layers) */

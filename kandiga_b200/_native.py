@@ -60,6 +60,22 @@ SIGNATURES = {
     "bakan_forward_destroy": (None, [c_void_p]),
     "bakan_forward_num_layers": (c_int, [c_void_p]),
     "kq_forward_set_params": (c_int, [c_void_p, c_int, ctypes.c_float]),
+    "bakan_full_init": (c_void_p, [ctypes.c_char_p, c_int]),
+    "bakan_full_set_weight": (c_int, [c_void_p, ctypes.c_char_p, c_void_p, ctypes.c_size_t, c_int,
+                                      ctypes.POINTER(ctypes.c_int64), c_int]),
+    "bakan_full_build": (c_int, [c_void_p]),
+    "bakan_full_forward": (c_int, [c_void_p, c_int, c_int, c_void_p, ctypes.POINTER(c_int)]),
+    "bakan_full_prefill": (c_int, [c_void_p, c_void_p, c_int, c_void_p, ctypes.POINTER(c_int)]),
+    "bakan_full_reset_cache": (None, [c_void_p]),
+    "bakan_full_destroy": (None, [c_void_p]),
+    "bakan_full_num_layers": (c_int, [c_void_p]),
+    "bakan_full_vocab_size": (c_int, [c_void_p]),
+    "bakan_full_set_debug": (None, [c_void_p, c_int]),
+    "bakan_full_set_kv_cache": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int]),
+    "bakan_full_set_position": (c_int, [c_void_p, c_int]),
+    "kq_full_init_json": (c_void_p, [ctypes.c_char_p, ctypes.c_char_p, c_int]),
+    "kq_full_position": (c_int, [c_void_p]),
+    "kq_full_time_steps": (c_int, [c_void_p, c_int, c_int, c_int, ctypes.POINTER(ctypes.c_float)]),
     # device ABI
     "kq_table_create": (c_int, [ctypes.POINTER(kq_table_desc), ctypes.POINTER(c_void_p)]),
     "kq_table_destroy": (c_int, [c_void_p]),

@@ -41,6 +41,11 @@ int bkex_parse(const uint8_t* hdr, size_t n, BkexInfo* info);
 // Read packed_dir/layer_XX.bin for XX < num_layers into a new HBM table on
 // stream s.  0 on success; -1 after a "[kandiga] ERROR: ..." line on stderr,
 // with nothing left allocated.
+// kq_dense_gemv with a residual added in the epilogue: y = residual + W x
+// (residual in y_dtype, may alias y; not for gate/up pairs).
+int dense_gemv_res(const kq_qmat* m, const void* x, int x_dtype, int T, const void* norm_w, float eps,
+                   int activation, void* y, int y_dtype, const void* residual, void* stream);
+
 int load_bkex_dir(const char* packed_dir, int num_layers, cudaStream_t s, kq_table** out, BkexInfo* info);
 
 // Workspace carve-up for kq_moe_* (offsets in bytes, 256-aligned).

@@ -372,8 +372,12 @@ __global__ void __launch_bounds__(NW * 32) qunit_kernel(const GemvParams p) {
     const float g = valid ? y0 * inv : 0.f, h = valid ? y1 * inv : 0.f;
     if (mode == MODE_DENSE) {
         if ((lane & 3) == 0) {
-            store_from_float(p.out, p.out_dtype, (size_t)tk * p.H + rt * 16 + r, g);
-            store_from_float(p.out, p.out_dtype, (size_t)tk * p.H + rt * 16 + r + 8, h);
+            const size_t o0 = (size_t)tk * p.H + rt * 16 + r, o1 = o0 + 8;
+            // residual (out_dtype, may alias out): out = residual + W x
+            const float r0 = p.residual ? load_as_float(p.residual, p.out_dtype, o0) : 0.f;
+            const float r1 = p.residual ? load_as_float(p.residual, p.out_dtype, o1) : 0.f;
+            store_from_float(p.out, p.out_dtype, o0, p.residual ? r0 + g : g);
+            store_from_float(p.out, p.out_dtype, o1, p.residual ? r1 + h : h);
         }
         return;
     }
@@ -746,7 +750,13 @@ extern "C" int kq_qmat_destroy(kq_qmat* m) {
 
 extern "C" int kq_dense_gemv(const kq_qmat* m, const void* x, int x_dtype, int T, const void* norm_w,
                              float eps, int activation, void* y, int y_dtype, void* stream) {
+    return kq::dense_gemv_res(m, x, x_dtype, T, norm_w, eps, activation, y, y_dtype, nullptr, stream);
+}
+
+int kq::dense_gemv_res(const kq_qmat* m, const void* x, int x_dtype, int T, const void* norm_w, float eps,
+                       int activation, void* y, int y_dtype, const void* residual, void* stream) {
     if (!m || !x || !y) return KQ_ERR_ARG;
+    if (residual && m->pair) return KQ_ERR_ARG;
     if (!valid_dtype(x_dtype) || !valid_dtype(y_dtype)) return KQ_ERR_ARG;
     if (norm_w && x_dtype == KQ_DT_F32) return KQ_ERR_ARG;
     if (activation != KQ_ACT_SILU && activation != KQ_ACT_GELU_TANH) return KQ_ERR_ARG;
@@ -768,6 +778,7 @@ extern "C" int kq_dense_gemv(const kq_qmat* m, const void* x, int x_dtype, int T
     p.out_dtype = y_dtype;
     p.act_kind = activation;
     p.H = m->rows;
+    p.residual = residual;
     p.mode = m->pair ? MODE_DENSE_PAIR : MODE_DENSE;
     return launch_qunit(m->bits, m->sb_dtype, p, static_cast<cudaStream_t>(stream)) == cudaSuccess
                ? KQ_OK
