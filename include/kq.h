@@ -152,12 +152,21 @@ int kq_forward_set_params(void* engine, int top_k, float rms_norm_eps);
  * (hidden_size, intermediate_size, num_hidden_layers, num_attention_heads,
  * num_key_value_heads, head_dim, vocab_size, rms_norm_eps, rope_theta,
  * partial_rotary_factor; max_cache_len, default 4096, sizes the KV cache).
- * Layers: input RMSNorm, q|k|v (separate q_proj/k_proj/v_proj or the
- * reference's fused self_attn.combined_proj; a q_proj of 2 x heads x head_dim
- * rows carries the per-head output gate), optional q_norm/k_norm, RoPE, GQA
- * decode attention over the fp16 cache, o_proj + residual, post-attention
- * RMSNorm, gate/up SwiGLU, down + residual; then norm and lm_head (or the tied
- * quantized embedding).  Linears are MLX-affine 3/4-bit (weight uint32, scales
+ * Token mixers: full attention -- input RMSNorm, q|k|v (separate
+ * q_proj/k_proj/v_proj or the reference's fused self_attn.combined_proj; a
+ * q_proj of 2 x heads x head_dim rows carries the per-head output gate),
+ * optional q_norm/k_norm, RoPE, GQA decode attention over the fp16 cache,
+ * o_proj + residual -- or GatedDeltaNet (layer_types "linear_attention", or
+ * all but every full_attention_interval-th layer when linear_num_value_heads
+ * is set; linear_num_key_heads, linear_key_head_dim (64/128/256),
+ * linear_value_head_dim, linear_conv_kernel_dim): in_proj_qkv|z|b|a (or
+ * linear_attn.combined_proj), conv1d + SiLU over a ring buffer, q/k RMSNorm
+ * and scaling, the gated delta rule on an fp32 state [v heads][v dim][k dim],
+ * RMSNormGated, out_proj + residual.  MLP: post-attention RMSNorm + gate/up
+ * SwiGLU + down, or, when num_experts > 0, the MoE block of the
+ * bakan_forward_* engine (experts from packed_expert_dir/layer_XX.bin; router
+ * mlp.gate, mlp.shared_expert.*, mlp.shared_expert_gate; num_experts_per_tok).
+ * Then norm and lm_head (or the tied quantized embedding).  Linears are MLX-affine 3/4-bit (weight uint32, scales
  * and biases fp16/bf16); head_dim 64/128/256, 1/2/4/8 q heads per kv head,
  * vocab_size a multiple of 16.  Names may carry the "language_model.model." /
  * "model." prefixes.  Weight dtype codes: 0 fp16, 1 bf16, 2 fp32, 3 packed uint32.
@@ -178,6 +187,10 @@ int bakan_full_vocab_size(void* engine);                                        
 void bakan_full_set_debug(void* engine, int enable);                             /* full_forward.h:138 */
 int bakan_full_set_kv_cache(void* engine, int attn_layer_idx, const void* keys_data, const void* values_data,
                             int seq_len, int num_kv_heads, int head_dim);        /* full_forward.h:157 */
+int bakan_full_set_linear_state(void* engine, int lin_layer_idx, const void* state_data,
+                                int state_bytes);                                /* full_forward.h:174 */
+int bakan_full_set_conv_state(void* engine, int lin_layer_idx, const void* conv_data,
+                              int conv_bytes);                                   /* full_forward.h:193 */
 int bakan_full_set_position(void* engine, int position);                         /* full_forward.h:214 */
 /* bakan_full_init with the config given as JSON text (no file). */
 void* kq_full_init_json(const char* config_json, const char* packed_dir, int num_layers);

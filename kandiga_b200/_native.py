@@ -73,6 +73,8 @@ SIGNATURES = {
     "bakan_full_set_debug": (None, [c_void_p, c_int]),
     "bakan_full_set_kv_cache": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int]),
     "bakan_full_set_position": (c_int, [c_void_p, c_int]),
+    "bakan_full_set_linear_state": (c_int, [c_void_p, c_int, c_void_p, c_int]),
+    "bakan_full_set_conv_state": (c_int, [c_void_p, c_int, c_void_p, c_int]),
     "kq_full_init_json": (c_void_p, [ctypes.c_char_p, ctypes.c_char_p, c_int]),
     "kq_full_position": (c_int, [c_void_p]),
     "kq_full_time_steps": (c_int, [c_void_p, c_int, c_int, c_int, ctypes.POINTER(ctypes.c_float)]),

@@ -257,14 +257,13 @@ bool ensure_ws(FwdEngine* e) {
     return kq_workspace_init(e->ws, need, e->stream) == KQ_OK;
 }
 
-// Enqueue one block on e->stream (input in e->dh, output in e->dout).
-int enqueue_block(FwdEngine* e, int layer, bool normed) {
+// Enqueue one block on stream s: out = [in] + MoE(x), x = in or rmsnorm(in).
+int enqueue_block_io(FwdEngine* e, int layer, bool normed, const __half* in, __half* out, cudaStream_t s) {
     const FwdLayer& L = e->layers[layer];
     const int H = e->info.hidden;
-    cudaStream_t s = e->stream;
-    const __half* x = e->dh;
+    const __half* x = in;
     if (!normed) {
-        fwd_rmsnorm_kernel<<<1, FWD_NORM_THREADS, 0, s>>>(e->dh, L.wt[WT_POST_ATTN_NORM].p,
+        fwd_rmsnorm_kernel<<<1, FWD_NORM_THREADS, 0, s>>>(in, L.wt[WT_POST_ATTN_NORM].p,
                                                           L.wt[WT_POST_ATTN_NORM].dtype == FWD_BF16 ? KQ_DT_BF16
                                                                                                      : KQ_DT_F16,
                                                           H, e->eps, e->dnorm);
@@ -284,9 +283,14 @@ int enqueue_block(FwdEngine* e, int layer, bool normed) {
         rc = kq_moe_decode(e->shared, layer, x, KQ_DT_F16, 1, nullptr, e->dzero, e->dones, 1, nullptr, e->dshared,
                            KQ_DT_F16, nullptr, e->ws, e->ws_bytes, s);
     if (rc == KQ_OK)
-        rc = kq_combine(e->droute, KQ_DT_F32, e->dones, 1, 1, H, normed ? nullptr : e->dh, e->dshared, KQ_DT_F16,
-                        e->dgate, e->dout, KQ_DT_F16, s);
+        rc = kq_combine(e->droute, KQ_DT_F32, e->dones, 1, 1, H, normed ? nullptr : in, e->dshared, KQ_DT_F16,
+                        e->dgate, out, KQ_DT_F16, s);
     return rc;
+}
+
+// Enqueue one block on e->stream (input in e->dh, output in e->dout).
+int enqueue_block(FwdEngine* e, int layer, bool normed) {
+    return enqueue_block_io(e, layer, normed, e->dh, e->dout, e->stream);
 }
 
 const char* block_missing(const FwdEngine* e, int layer, bool normed) {
@@ -447,6 +451,31 @@ extern "C" int kq_forward_set_params(void* engine, int top_k, float rms_norm_eps
     e->eps = rms_norm_eps;
     return KQ_OK;
 }
+
+// ---- the MoE layers of the whole-model decode step (kq_full.cu) ----------------
+namespace kq {
+
+int moe_block_prepare(void* engine, int layer) {
+    FwdEngine* e = static_cast<FwdEngine*>(engine);
+    if (!e || layer < 0 || layer >= e->num_layers) return -1;
+    if (const char* miss = block_missing(e, layer, false)) {
+        fprintf(stderr, "[kandiga] ERROR: layer %d has no %s weights\n", layer, miss);
+        return -1;
+    }
+    return ensure_ws(e) ? 0 : -1;
+}
+
+int moe_block_enqueue(void* engine, int layer, const __half* in, __half* out, cudaStream_t s) {
+    return enqueue_block_io(static_cast<FwdEngine*>(engine), layer, false, in, out, s);
+}
+
+int moe_block_hidden(void* engine) { return engine ? static_cast<FwdEngine*>(engine)->info.hidden : 0; }
+
+uint32_t* moe_block_status(void* engine) {
+    return engine ? static_cast<uint32_t*>(static_cast<FwdEngine*>(engine)->ws) : nullptr;
+}
+
+}  // namespace kq
 
 extern "C" void bakan_forward_destroy(void* engine) {
     FwdEngine* e = static_cast<FwdEngine*>(engine);

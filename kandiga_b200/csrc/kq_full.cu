@@ -18,8 +18,13 @@
 //                        projection)
 //   attn_merge_kernel    chunk merge per (q head, 32 dims), sigmoid output gate
 //   kq_dense_gemv        o_proj with the residual added in its epilogue
-// Dense MLP: RMSNorm + gate/up pair with SwiGLU in one pass, then down with the
-// residual.  Rounding points follow the reference's kernels: every buffer
+// Per GatedDeltaNet layer (full_forward_lg.m:1361-1508): kq_dense_gemv (input
+// RMSNorm + q|k|v|z|b|a), gdn_conv_kernel (ring buffer + conv1d + SiLU),
+// gdn_state_kernel (q/k norm and scale, gated delta rule on the fp32 state),
+// gdn_norm_kernel (RMSNormGated), kq_dense_gemv (out_proj + residual).
+// MLP: the MoE block engine of kq_forward.cu (routed experts from the BKEX
+// files, shared expert, gate, blend) or a dense MLP: RMSNorm + gate/up pair
+// with SwiGLU in one pass, then down with the residual.  Rounding points follow the reference's kernels: every buffer
 // between kernels is fp16 (attention.metal writes half after each step).
 #include "kq_internal.h"
 #include "kq_common.cuh"
@@ -45,6 +50,11 @@ struct Cfg {
     float eps = 1e-6f, theta = 10000.f;
     int group = 64;
     int act = KQ_ACT_SILU;
+    std::vector<char> linear;  // per layer: 1 = GatedDeltaNet, 0 = full attention
+    int lnk = 0, lnv = 0, lkd = 0, lvd = 0, conv_k = 4;  // GatedDeltaNet heads and dims
+    int num_experts = 0;       // > 0: MoE MLP, experts from the BKEX layer files
+    int conv_dim() const { return 2 * lnk * lkd + lnv * lvd; }
+    int lin_proj_rows() const { return conv_dim() + lnv * lvd + 2 * lnv; }
 };
 
 // ---- kernels ------------------------------------------------------------------------
@@ -446,6 +456,133 @@ __global__ void __launch_bounds__(MERGE_WARPS * 32) attn_merge_kernel(const Attn
     a.out[(size_t)h * hd + d] = __float2half(o);
 }
 
+// ---- GatedDeltaNet (linear attention) layer ------------------------------------------
+// Restates kandiga/metal/attention.metal:1055-1370 as dispatched by
+// kandiga/metal/full_forward_lg.m:1361-1508 (conv buffer update, conv1d + SiLU,
+// split q|k|v, per-head RMSNorm of q and k without weight, q * 1/kd and
+// k * 1/sqrt(kd), gated delta state update, RMSNormGated, out_proj).
+
+// Conv ring buffer [channel][ks]: shift left, append this token's projection
+// (conv1d_buffer_update), then silu(sum_k buf * w) -> fp16 (depthwise_conv1d_silu).
+__global__ void gdn_conv_kernel(const __half* __restrict__ proj, __half* __restrict__ state,
+                                const float* __restrict__ w, int conv_dim, int ks, __half* __restrict__ out) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+    if (ch >= conv_dim) return;
+    __half* st = state + (size_t)ch * ks;
+    float acc = 0.f;
+    for (int k = 0; k < ks; ++k) {
+        const __half v = k + 1 < ks ? st[k + 1] : proj[ch];
+        st[k] = v;
+        acc = fmaf(__half2float(v), w[(size_t)ch * ks + k], acc);
+    }
+    out[ch] = __float2half(acc / (1.f + expf(-acc)));
+}
+
+// One CTA per (value head hv, 32 value rows): q and k of key head hv / (nv / nk)
+// normalised and scaled in shared memory, the decay g = exp(-exp(A_log) *
+// softplus(a + dt_bias)) and beta = sigmoid(b); then per value row dv (a warp,
+// lane l owning key dims [l*KPL, l*KPL + KPL)): S *= g; delta = (v - S.k) * beta;
+// S += delta k; o = S.q (attention.metal:1108-1178, state fp32 [nv][vd][kd]).
+template <int KPL>
+__global__ void __launch_bounds__(256) gdn_state_kernel(const __half* __restrict__ conv, const __half* __restrict__ proj,
+                                                        const float* __restrict__ a_log,
+                                                        const float* __restrict__ dt_bias, float* __restrict__ state,
+                                                        int nk, int nv, int vd, int conv_dim, int vtot, float eps,
+                                                        __half* __restrict__ o) {
+    constexpr int KD = 32 * KPL;
+    __shared__ float sq[KD], sk[KD];
+    __shared__ float s_g, s_beta;
+    pdl_wait();
+    pdl_launch_dependents();
+    const int hv = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hk = hv / (nv / nk);
+    if (warp < 2) {  // warp 0: q, warp 1: k -- rmsnorm_per_head_no_weight, then the scale, each to fp16
+        const __half* src = conv + (size_t)warp * nk * KD + (size_t)hk * KD;
+        float v[KPL], ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) {
+            v[j] = __half2float(src[lane * KPL + j]);
+            ss += v[j] * v[j];
+        }
+        const float sc = 1.f / sqrtf(warp_sum(ss) / (float)KD + eps);
+        const float inv = 1.f / sqrtf((float)KD);
+        const float mul = warp == 0 ? inv * inv : inv;
+        float* dst = warp == 0 ? sq : sk;
+#pragma unroll
+        for (int j = 0; j < KPL; ++j)
+            dst[lane * KPL + j] = __half2float(__float2half(__half2float(__float2half(v[j] * sc)) * mul));
+    } else if (threadIdx.x == 64) {
+        const float av = __half2float(proj[conv_dim + vtot + nv + hv]);  // a follows b in the projection
+        const float bv = __half2float(proj[conv_dim + vtot + hv]);
+        const float sp = logf(1.f + expf(av + dt_bias[hv]));
+        s_g = expf(-expf(a_log[hv]) * sp);
+        s_beta = 1.f / (1.f + expf(-bv));
+    }
+    __syncthreads();
+    const float g = s_g, beta = s_beta;
+    float kf[KPL], qf[KPL];
+#pragma unroll
+    for (int j = 0; j < KPL; ++j) {
+        kf[j] = sk[lane * KPL + j];
+        qf[j] = sq[lane * KPL + j];
+    }
+    const __half* vsrc = conv + (size_t)2 * nk * KD + (size_t)hv * vd;
+    for (int r = warp; r < 32; r += 8) {
+        const int dv = blockIdx.y * 32 + r;
+        if (dv >= vd) break;
+        float* srow = state + ((size_t)hv * vd + dv) * KD + lane * KPL;
+        float sv[KPL];
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) sv[j] = srow[j];
+        float kv = 0.f;
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) {
+            sv[j] *= g;
+            kv = fmaf(sv[j], kf[j], kv);
+        }
+        kv = warp_sum(kv);
+        const float delta = (__half2float(vsrc[dv]) - kv) * beta;
+        float ov = 0.f;
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) {
+            sv[j] = fmaf(delta, kf[j], sv[j]);
+            ov = fmaf(sv[j], qf[j], ov);
+            srow[j] = sv[j];
+        }
+        ov = warp_sum(ov);
+        if (lane == 0) o[(size_t)hv * vd + dv] = __float2half(ov);
+    }
+}
+
+// RMSNormGated per value head: half(silu(z) * (o * rsqrt(mean(o^2) + eps) * w))
+// (rmsnorm_gated_kernel, attention.metal:1197-1260).
+__global__ void gdn_norm_kernel(const __half* __restrict__ o, const __half* __restrict__ proj,
+                                const float* __restrict__ w, int vd, int conv_dim, float eps, __half* __restrict__ out) {
+    __shared__ float red[32];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int hv = blockIdx.x;
+    float ss = 0.f;
+    for (int d = threadIdx.x; d < vd; d += blockDim.x) {
+        const float v = __half2float(o[(size_t)hv * vd + d]);
+        ss += v * v;
+    }
+    const float sc = 1.f / sqrtf(block_sum(ss, red) / (float)vd + eps);
+    for (int d = threadIdx.x; d < vd; d += blockDim.x) {
+        const float normed = __half2float(o[(size_t)hv * vd + d]) * sc * w[d];
+        const float z = __half2float(proj[conv_dim + (size_t)hv * vd + d]);
+        out[(size_t)hv * vd + d] = __float2half((z / (1.f + expf(-z))) * normed);
+    }
+}
+
+// float tensors of any 16/32-bit float type -> fp32 (conv weights, A_log, dt_bias, norm)
+__global__ void to_f32_kernel(const void* __restrict__ src, int dtype, size_t n, float* __restrict__ dst) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = load_as_float(src, dtype, i);
+}
+
 // norm weights of any 16/32-bit float type -> fp16 (the GEMV prologue's dtype)
 __global__ void to_f16_kernel(const void* __restrict__ src, int dtype, size_t n, __half* __restrict__ dst) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
@@ -462,8 +599,15 @@ struct Weight {
 };
 
 struct Layer {
-    kq_qmat* qkv = nullptr;
-    kq_qmat* o = nullptr;
+    bool linear = false;  // GatedDeltaNet
+    kq_qmat* qkv = nullptr;   // attention: q|k|v; GatedDeltaNet: q|k|v|z|b|a
+    kq_qmat* o = nullptr;     // o_proj / out_proj
+    float* conv_w = nullptr;  // [conv_dim][conv_k]
+    float* a_log = nullptr;   // [nv]
+    float* dt_bias = nullptr; // [nv]
+    float* gnorm = nullptr;   // [vd]
+    __half* conv_state = nullptr;  // [conv_dim][conv_k]
+    float* state = nullptr;        // [nv][vd][kd]
     kq_qmat* gate_up = nullptr;
     kq_qmat* down = nullptr;
     __half* in_norm = nullptr;
@@ -504,6 +648,13 @@ struct Engine {
     uint32_t* host_status = nullptr;
     int nchunk = 0;
     int position = 0;
+    // GatedDeltaNet activations
+    __half *lproj = nullptr, *lconv = nullptr, *lo = nullptr, *lnorm = nullptr;
+    // MoE MLP: the MoE block engine over the BKEX files, hidden state ping-pong
+    void* moe = nullptr;
+    __half* h2 = nullptr;
+    __half* hfinal = nullptr;  // buffer holding the last layer's output
+    uint32_t* host_moe_status = nullptr;
 };
 
 static void err(const char* what) { fprintf(stderr, "[kandiga] ERROR: bakan_full: %s\n", what); }
@@ -546,11 +697,41 @@ static int jint(const std::string& js, const char* key, int dflt) {
     return json_num(js, key, &v) ? (int)v : dflt;
 }
 
+// "layer_types": [...] strings -> 1 for "linear_attention"; false if absent
+static bool json_layer_types(const std::string& js, int n, std::vector<char>* out) {
+    size_t p = js.find("\"layer_types\"");
+    if (p == std::string::npos) return false;
+    p = js.find('[', p);
+    const size_t q = js.find(']', p);
+    if (p == std::string::npos || q == std::string::npos) return false;
+    out->clear();
+    size_t i = p;
+    while ((i = js.find('"', i + 1)) != std::string::npos && i < q) {
+        const size_t j = js.find('"', i + 1);
+        if (j == std::string::npos || j > q) break;
+        out->push_back(js.compare(i + 1, j - i - 1, "linear_attention") == 0 ? 1 : 0);
+        i = j;
+    }
+    out->resize(n, 0);
+    return true;
+}
+
 static bool parse_cfg(const std::string& js, int num_layers, Cfg* c) {
     c->hidden = jint(js, "hidden_size", 0);
     c->inter = jint(js, "intermediate_size", 0);
     c->layers = jint(js, "num_hidden_layers", num_layers);
     if (num_layers > 0 && num_layers < c->layers) c->layers = num_layers;
+    c->lnk = jint(js, "linear_num_key_heads", 0);
+    c->lnv = jint(js, "linear_num_value_heads", 0);
+    c->lkd = jint(js, "linear_key_head_dim", 0);
+    c->lvd = jint(js, "linear_value_head_dim", 0);
+    c->conv_k = jint(js, "linear_conv_kernel_dim", 4);
+    c->num_experts = jint(js, "num_experts", 0);
+    if (c->layers > 0 && !json_layer_types(js, c->layers, &c->linear)) {
+        const int every = c->lnv > 0 ? jint(js, "full_attention_interval", 4) : 1;
+        c->linear.assign(c->layers, 0);
+        for (int l = 0; l < c->layers; ++l) c->linear[l] = every > 1 && (l + 1) % every != 0;
+    }
     c->nq = jint(js, "num_attention_heads", 0);
     c->nkv = jint(js, "num_key_value_heads", c->nq);
     c->hd = jint(js, "head_dim", c->nq ? c->hidden / c->nq : 0);
@@ -565,8 +746,12 @@ static bool parse_cfg(const std::string& js, int num_layers, Cfg* c) {
     c->rope_dim = (int)(c->hd * prf);
     c->rope_dim -= c->rope_dim % 2;
     if (js.find("\"gelu") != std::string::npos) c->act = KQ_ACT_GELU_TANH;
-    return c->hidden > 0 && c->inter > 0 && c->layers > 0 && c->nq > 0 && c->nkv > 0 && c->nq % c->nkv == 0 &&
-           c->hd > 0 && c->vocab > 0 && c->max_seq > 0;
+    bool any_lin = false;
+    for (char x : c->linear) any_lin = any_lin || x;
+    const bool lin_ok = !any_lin || (c->lnk > 0 && c->lnv > 0 && c->lnv % c->lnk == 0 && c->lkd > 0 && c->lvd > 0 &&
+                                     c->conv_k > 0 && c->conv_k <= 8);
+    return c->hidden > 0 && (c->inter > 0 || c->num_experts > 0) && c->layers > 0 && c->nq > 0 && c->nkv > 0 &&
+           c->nq % c->nkv == 0 && c->hd > 0 && c->vocab > 0 && c->max_seq > 0 && lin_ok;
 }
 
 static const Weight* find(Engine* e, const std::string& name) {
@@ -600,6 +785,24 @@ static __half* norm_f16(Engine* e, const std::string& name, int n, bool required
         return nullptr;
     }
     to_f16_kernel<<<(n + 255) / 256, 256, 0, e->s>>>(wt->p, dt, (size_t)n, d);
+    return d;
+}
+
+// fp32 copy of a float tensor of n values (conv weights, A_log, dt_bias, norms)
+static float* f32_of(Engine* e, const std::string& name, size_t n, bool* ok) {
+    const Weight* wt = find(e, name);
+    const int dt = !wt ? -1 : wt->dtype == 0 ? KQ_DT_F16 : wt->dtype == 1 ? KQ_DT_BF16 : wt->dtype == 2 ? KQ_DT_F32 : -1;
+    if (dt < 0 || wt->bytes != n * (dt == KQ_DT_F32 ? 4 : 2)) {
+        fprintf(stderr, "[kandiga] ERROR: bakan_full: %s not set as %zu float values\n", name.c_str(), n);
+        *ok = false;
+        return nullptr;
+    }
+    float* d = dalloc<float>(e, n);
+    if (!d) {
+        *ok = false;
+        return nullptr;
+    }
+    to_f32_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 1024), 256, 0, e->s>>>(wt->p, dt, n, d);
     return d;
 }
 
@@ -767,32 +970,74 @@ static bool gqa_supported(const Cfg& c) {
     return (c.hd == 64 || c.hd == 128 || c.hd == 256) && (G == 1 || G == 2 || G == 4 || G == 8);
 }
 
-// Layers then (optionally) the head, enqueued on e->s.
+template <int KPL>
+static cudaError_t launch_gdn_state(Engine* e, const Layer& ly) {
+    const Cfg& c = e->c;
+    return pdl_launch(gdn_state_kernel<KPL>, dim3(c.lnv, (c.lvd + 31) / 32), dim3(256), 0, e->s,
+                      (const __half*)e->lconv, (const __half*)e->lproj, (const float*)ly.a_log,
+                      (const float*)ly.dt_bias, ly.state, c.lnk, c.lnv, c.lvd, c.conv_dim(), c.lnv * c.lvd, c.eps,
+                      e->lo);
+}
+
+// GatedDeltaNet token mixer of one layer on the hidden state `x` (in place).
+static int enqueue_linear(Engine* e, const Layer& ly, __half* x) {
+    const Cfg& c = e->c;
+    int rc = dense_gemv_res(ly.qkv, x, KQ_DT_F16, 1, ly.in_norm, c.eps, KQ_ACT_SILU, e->lproj, KQ_DT_F16, nullptr, e->s);
+    if (rc) return rc;
+    const int cdim = c.conv_dim();
+    if (pdl_launch(gdn_conv_kernel, dim3((cdim + 255) / 256), dim3(256), 0, e->s, (const __half*)e->lproj,
+                   ly.conv_state, (const float*)ly.conv_w, cdim, c.conv_k, e->lconv) != cudaSuccess)
+        return KQ_ERR_CUDA;
+    cudaError_t ce = c.lkd == 64 ? launch_gdn_state<2>(e, ly)
+                     : c.lkd == 128 ? launch_gdn_state<4>(e, ly)
+                                    : launch_gdn_state<8>(e, ly);
+    if (ce != cudaSuccess) return KQ_ERR_CUDA;
+    if (pdl_launch(gdn_norm_kernel, dim3(c.lnv), dim3(128), 0, e->s, (const __half*)e->lo, (const __half*)e->lproj,
+                   (const float*)ly.gnorm, c.lvd, cdim, c.eps, e->lnorm) != cudaSuccess)
+        return KQ_ERR_CUDA;
+    return dense_gemv_res(ly.o, e->lnorm, KQ_DT_F16, 1, nullptr, c.eps, KQ_ACT_SILU, x, KQ_DT_F16, x, e->s);
+}
+
+// Attention token mixer of one layer on the hidden state `x` (in place).
+static int enqueue_attention(Engine* e, const Layer& ly, __half* x) {
+    const Cfg& c = e->c;
+    int rc = dense_gemv_res(ly.qkv, x, KQ_DT_F16, 1, ly.in_norm, c.eps, KQ_ACT_SILU, e->qkv, KQ_DT_F16, nullptr, e->s);
+    if (rc) return rc;
+    if (attention(e, &ly) != cudaSuccess) return KQ_ERR_CUDA;
+    return dense_gemv_res(ly.o, e->attn, KQ_DT_F16, 1, nullptr, c.eps, KQ_ACT_SILU, x, KQ_DT_F16, x, e->s);
+}
+
+// Layers, enqueued on e->s; the hidden state ping-pongs between h and h2 across
+// MoE blocks (whose output cannot alias their input).
 static int enqueue_body(Engine* e) {
     const Cfg& c = e->c;
     embed_kernel<<<(c.hidden + 255) / 256, 256, 0, e->s>>>(
         e->dev_i, c.vocab, static_cast<const uint8_t*>(e->emb_w), static_cast<const uint16_t*>(e->emb_s),
         static_cast<const uint16_t*>(e->emb_b), e->emb_bits, e->emb_sb, e->emb_kind, c.hidden, c.group, e->h,
         c.rope_dim, c.theta, e->rope, e->status);
+    __half* cur = e->h;
+    __half* other = e->h2;
     for (int l = 0; l < c.layers; ++l) {
         const Layer& ly = e->L[l];
-        int rc = dense_gemv_res(ly.qkv, e->h, KQ_DT_F16, 1, ly.in_norm, c.eps, KQ_ACT_SILU, e->qkv, KQ_DT_F16, nullptr,
+        int rc = ly.linear ? enqueue_linear(e, ly, cur) : enqueue_attention(e, ly, cur);
+        if (rc) return rc;
+        if (e->moe) {
+            if (moe_block_enqueue(e->moe, l, cur, other, e->s) != KQ_OK) return KQ_ERR_CUDA;
+            std::swap(cur, other);
+        } else {
+            rc = dense_gemv_res(ly.gate_up, cur, KQ_DT_F16, 1, ly.post_norm, c.eps, c.act, e->act, KQ_DT_F16, nullptr,
                                 e->s);
-        if (rc) return rc;
-        if (attention(e, &ly) != cudaSuccess) return KQ_ERR_CUDA;
-        rc = dense_gemv_res(ly.o, e->attn, KQ_DT_F16, 1, nullptr, c.eps, KQ_ACT_SILU, e->h, KQ_DT_F16, e->h, e->s);
-        if (rc) return rc;
-        rc = dense_gemv_res(ly.gate_up, e->h, KQ_DT_F16, 1, ly.post_norm, c.eps, c.act, e->act, KQ_DT_F16, nullptr,
-                            e->s);
-        if (rc) return rc;
-        rc = dense_gemv_res(ly.down, e->act, KQ_DT_F16, 1, nullptr, c.eps, KQ_ACT_SILU, e->h, KQ_DT_F16, e->h, e->s);
-        if (rc) return rc;
+            if (rc) return rc;
+            rc = dense_gemv_res(ly.down, e->act, KQ_DT_F16, 1, nullptr, c.eps, KQ_ACT_SILU, cur, KQ_DT_F16, cur, e->s);
+            if (rc) return rc;
+        }
     }
+    e->hfinal = cur;
     return cudaGetLastError() == cudaSuccess ? KQ_OK : KQ_ERR_CUDA;
 }
 
 static int enqueue_head(Engine* e) {
-    return dense_gemv_res(e->lm, e->h, KQ_DT_F16, 1, e->final_norm, e->c.eps, KQ_ACT_SILU, e->logits, KQ_DT_F32,
+    return dense_gemv_res(e->lm, e->hfinal, KQ_DT_F16, 1, e->final_norm, e->c.eps, KQ_ACT_SILU, e->logits, KQ_DT_F32,
                           nullptr, e->s);
 }
 
@@ -859,43 +1104,81 @@ static int build(Engine* e) {
     if (!ok) return -1;
     e->L.assign(c.layers, Layer());
     const int qrows = c.nq * c.hd, kvrows = c.nkv * c.hd;
+    const int cdim = c.conv_dim(), vtot = c.lnv * c.lvd;
     for (int l = 0; l < c.layers; ++l) {
         Layer& ly = e->L[l];
+        ly.linear = c.linear[l] != 0;
         ly.in_norm = norm_f16(e, lname(l, "input_layernorm.weight"), c.hidden, true, &ok);
-        ly.post_norm = norm_f16(e, lname(l, "post_attention_layernorm.weight"), c.hidden, true, &ok);
-        ly.q_norm = norm_f16(e, lname(l, "self_attn.q_norm.weight"), c.hd, false, &ok);
-        ly.k_norm = norm_f16(e, lname(l, "self_attn.k_norm.weight"), c.hd, false, &ok);
+        if (!e->moe) ly.post_norm = norm_f16(e, lname(l, "post_attention_layernorm.weight"), c.hidden, true, &ok);
         int rows = 0;
-        if (find(e, lname(l, "self_attn.combined_proj.weight")))
-            ly.qkv = qlinear(e, {lname(l, "self_attn.combined_proj")}, c.hidden, &rows, &ok);
-        else
-            ly.qkv = qlinear(e, {lname(l, "self_attn.q_proj"), lname(l, "self_attn.k_proj"),
-                                 lname(l, "self_attn.v_proj")},
-                             c.hidden, &rows, &ok);
-        if (!ok) return -1;
-        if (rows == 2 * qrows + 2 * kvrows)
-            ly.gate = 1;  // q_proj carries the output gate, interleaved per head
-        else if (rows != qrows + 2 * kvrows) {
-            fprintf(stderr, "[kandiga] ERROR: bakan_full: layer %d q|k|v has %d rows\n", l, rows);
-            return -1;
+        if (ly.linear) {
+            if (find(e, lname(l, "linear_attn.combined_proj.weight")))
+                ly.qkv = qlinear(e, {lname(l, "linear_attn.combined_proj")}, c.hidden, &rows, &ok);
+            else
+                ly.qkv = qlinear(e, {lname(l, "linear_attn.in_proj_qkv"), lname(l, "linear_attn.in_proj_z"),
+                                     lname(l, "linear_attn.in_proj_b"), lname(l, "linear_attn.in_proj_a")},
+                                 c.hidden, &rows, &ok);
+            if (!ok) return -1;
+            if (rows != c.lin_proj_rows()) {
+                fprintf(stderr, "[kandiga] ERROR: bakan_full: layer %d q|k|v|z|b|a has %d rows, expected %d\n", l,
+                        rows, c.lin_proj_rows());
+                return -1;
+            }
+            ly.o = qlinear(e, {lname(l, "linear_attn.out_proj")}, vtot, nullptr, &ok);
+            ly.conv_w = f32_of(e, lname(l, "linear_attn.conv1d.weight"), (size_t)cdim * c.conv_k, &ok);
+            ly.a_log = f32_of(e, lname(l, "linear_attn.A_log"), c.lnv, &ok);
+            ly.dt_bias = f32_of(e, lname(l, "linear_attn.dt_bias"), c.lnv, &ok);
+            ly.gnorm = f32_of(e, lname(l, "linear_attn.norm.weight"), c.lvd, &ok);
+            if (!ok) return -1;
+            ly.conv_state = dalloc<__half>(e, (size_t)cdim * c.conv_k);
+            ly.state = dalloc<float>(e, (size_t)c.lnv * c.lvd * c.lkd);
+            if (!ly.conv_state || !ly.state) {
+                err("linear-attention state allocation failed");
+                return -1;
+            }
+        } else {
+            ly.q_norm = norm_f16(e, lname(l, "self_attn.q_norm.weight"), c.hd, false, &ok);
+            ly.k_norm = norm_f16(e, lname(l, "self_attn.k_norm.weight"), c.hd, false, &ok);
+            if (find(e, lname(l, "self_attn.combined_proj.weight")))
+                ly.qkv = qlinear(e, {lname(l, "self_attn.combined_proj")}, c.hidden, &rows, &ok);
+            else
+                ly.qkv = qlinear(e, {lname(l, "self_attn.q_proj"), lname(l, "self_attn.k_proj"),
+                                     lname(l, "self_attn.v_proj")},
+                                 c.hidden, &rows, &ok);
+            if (!ok) return -1;
+            if (rows == 2 * qrows + 2 * kvrows)
+                ly.gate = 1;  // q_proj carries the output gate, interleaved per head
+            else if (rows != qrows + 2 * kvrows) {
+                fprintf(stderr, "[kandiga] ERROR: bakan_full: layer %d q|k|v has %d rows\n", l, rows);
+                return -1;
+            }
+            ly.o = qlinear(e, {lname(l, "self_attn.o_proj")}, qrows, nullptr, &ok);
+            ly.kc = dalloc<__half>(e, (size_t)c.nkv * c.max_seq * c.hd);
+            ly.vc = dalloc<__half>(e, (size_t)c.nkv * c.max_seq * c.hd);
+            if (!ly.kc || !ly.vc) {
+                err("KV cache allocation failed");
+                return -1;
+            }
         }
-        ly.o = qlinear(e, {lname(l, "self_attn.o_proj")}, qrows, nullptr, &ok);
-        ly.gate_up = qlinear(e, {lname(l, "mlp.gate_proj")}, c.hidden, nullptr, &ok, lname(l, "mlp.up_proj"));
-        ly.down = qlinear(e, {lname(l, "mlp.down_proj")}, c.inter, nullptr, &ok);
-        if (!ok) return -1;
-        ly.kc = dalloc<__half>(e, (size_t)c.nkv * c.max_seq * c.hd);
-        ly.vc = dalloc<__half>(e, (size_t)c.nkv * c.max_seq * c.hd);
-        if (!ly.kc || !ly.vc) {
-            err("KV cache allocation failed");
-            return -1;
+        if (e->moe) {
+            if (moe_block_prepare(e->moe, l) != 0) return -1;
+        } else {
+            ly.gate_up = qlinear(e, {lname(l, "mlp.gate_proj")}, c.hidden, nullptr, &ok, lname(l, "mlp.up_proj"));
+            ly.down = qlinear(e, {lname(l, "mlp.down_proj")}, c.inter, nullptr, &ok);
         }
+        if (!ok) return -1;
     }
     e->nchunk = (ATTN_CTAS + c.nkv - 1) / c.nkv;  // context chunks per kv head
     e->h = dalloc<__half>(e, c.hidden);
     e->qkv = dalloc<__half>(e, (size_t)2 * qrows + 2 * kvrows);
     e->rope = dalloc<float2>(e, c.rope_dim / 2 + 1);
     e->attn = dalloc<__half>(e, qrows);
-    e->act = dalloc<__half>(e, c.inter);
+    e->act = dalloc<__half>(e, c.inter > 0 ? c.inter : 1);
+    e->h2 = dalloc<__half>(e, c.hidden);
+    e->lproj = dalloc<__half>(e, (size_t)c.lin_proj_rows() + 1);
+    e->lconv = dalloc<__half>(e, (size_t)cdim + 1);
+    e->lo = dalloc<__half>(e, (size_t)vtot + 1);
+    e->lnorm = dalloc<__half>(e, (size_t)vtot + 1);
     e->logits = dalloc<float>(e, c.vocab);
     e->pm = dalloc<float>(e, (size_t)c.nq * e->nchunk);
     e->pl = dalloc<float>(e, (size_t)c.nq * e->nchunk);
@@ -903,13 +1186,14 @@ static int build(Engine* e) {
     e->dev_i = dalloc<int>(e, 4);
     e->status = dalloc<uint32_t>(e, 1);
     if (!e->h || !e->qkv || !e->rope || !e->attn || !e->act || !e->logits || !e->pm || !e->pl || !e->pacc ||
-        !e->dev_i || !e->status) {
+        !e->dev_i || !e->status || !e->h2 || !e->lproj || !e->lconv || !e->lo || !e->lnorm) {
         err("buffer allocation failed");
         return -1;
     }
     if (cudaHostAlloc(reinterpret_cast<void**>(&e->host_i), 4 * sizeof(int), 0) != cudaSuccess ||
         cudaHostAlloc(reinterpret_cast<void**>(&e->host_logits), (size_t)c.vocab * sizeof(float), 0) != cudaSuccess ||
-        cudaHostAlloc(reinterpret_cast<void**>(&e->host_status), sizeof(uint32_t), 0) != cudaSuccess) {
+        cudaHostAlloc(reinterpret_cast<void**>(&e->host_status), sizeof(uint32_t), 0) != cudaSuccess ||
+        cudaHostAlloc(reinterpret_cast<void**>(&e->host_moe_status), sizeof(uint32_t), 0) != cudaSuccess) {
         cudaGetLastError();
         err("pinned host buffers");
         return -1;
@@ -949,19 +1233,34 @@ static int step(Engine* e, int token, int position, float* logits_out) {
     }
     if (ce == cudaSuccess)
         ce = cudaMemcpyAsync(e->host_status, e->status, sizeof(uint32_t), cudaMemcpyDeviceToHost, e->s);
+    *e->host_moe_status = 0;
+    if (ce == cudaSuccess && e->moe)
+        ce = cudaMemcpyAsync(e->host_moe_status, moe_block_status(e->moe), sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                             e->s);
     if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->s);
     if (ce != cudaSuccess) {
         fprintf(stderr, "[kandiga] ERROR: bakan_full: %s\n", cudaGetErrorString(ce));
         return -1;
     }
-    if (*e->host_status) {
-        fprintf(stderr, "[kandiga] ERROR: bakan_full: device status 0x%x\n", *e->host_status);
+    if (*e->host_status || *e->host_moe_status) {
+        fprintf(stderr, "[kandiga] ERROR: bakan_full: device status 0x%x / MoE 0x%x\n", *e->host_status,
+                *e->host_moe_status);
         cudaMemsetAsync(e->status, 0, sizeof(uint32_t), e->s);
+        if (e->moe) cudaMemsetAsync(moe_block_status(e->moe), 0, sizeof(uint32_t), e->s);
+        cudaStreamSynchronize(e->s);
         return -1;
     }
     if (logits_out) memcpy(logits_out, e->host_logits, (size_t)e->c.vocab * sizeof(float));
     e->position = position + 1;
     return 0;
+}
+
+// the idx-th layer of one kind (GatedDeltaNet or attention), nullptr if none
+static Layer* nth_layer(Engine* e, bool linear, int idx) {
+    if (idx < 0) return nullptr;
+    for (auto& ly : e->L)
+        if (ly.linear == linear && idx-- == 0) return &ly;
+    return nullptr;
 }
 
 static void destroy(Engine* e) {
@@ -976,6 +1275,8 @@ static void destroy(Engine* e) {
     if (e->host_i) cudaFreeHost(e->host_i);
     if (e->host_logits) cudaFreeHost(e->host_logits);
     if (e->host_status) cudaFreeHost(e->host_status);
+    if (e->host_moe_status) cudaFreeHost(e->host_moe_status);
+    if (e->moe) bakan_forward_destroy(e->moe);
     if (e->s) cudaStreamDestroy(e->s);
     delete e;
 }
@@ -995,11 +1296,32 @@ static Engine* create(const std::string& json, const char* dir, int num_layers) 
         delete e;
         return nullptr;
     }
+    bool any_lin = false;
+    for (char x : e->c.linear) any_lin = any_lin || x;
+    if (any_lin && e->c.lkd != 64 && e->c.lkd != 128 && e->c.lkd != 256) {
+        err("linear_key_head_dim must be 64, 128 or 256");
+        delete e;
+        return nullptr;
+    }
     e->dir = dir ? dir : "";
     if (cudaStreamCreateWithFlags(&e->s, cudaStreamNonBlocking) != cudaSuccess) {
         cudaGetLastError();
         delete e;
         return nullptr;
+    }
+    if (e->c.num_experts > 0) {  // routed experts from packed_dir/layer_XX.bin, as bakan_full_init's argument says
+        e->moe = bakan_forward_init(e->dir.c_str(), e->c.layers);
+        if (!e->moe || moe_block_hidden(e->moe) != e->c.hidden) {
+            err("MoE layers need the BKEX expert files of every layer in packed_expert_dir, hidden_size as the model's");
+            destroy(e);
+            return nullptr;
+        }
+        const int top_k = jint(json, "num_experts_per_tok", 8);
+        if (kq_forward_set_params(e->moe, top_k, e->c.eps) != KQ_OK) {
+            err("num_experts_per_tok outside [1, min(16, experts)]");
+            destroy(e);
+            return nullptr;
+        }
     }
     return e;
 }
@@ -1046,6 +1368,35 @@ extern "C" int bakan_full_set_weight(void* engine, const char* name, const void*
             key = key.substr(strlen(pre));
             break;
         }
+    if (e->moe) {  // the MoE block's tensors go to the MoE block engine (weight types of bakan_forward.h:35-53)
+        const int layer = key.rfind("layers.", 0) == 0 ? atoi(key.c_str() + 7) : -1;
+        const size_t dot = key.find('.', 7);
+        const std::string rest = dot == std::string::npos ? "" : key.substr(dot + 1);
+        static const struct {
+            const char* name;
+            int wt;
+        } kMoe[] = {{"post_attention_layernorm.weight", 0},    {"mlp.gate.weight", 1},
+                    {"mlp.gate.scales", 2},                    {"mlp.gate.biases", 3},
+                    {"mlp.shared_expert_gate.weight", 4},      {"mlp.shared_expert_gate.scales", 5},
+                    {"mlp.shared_expert_gate.biases", 6},      {"mlp.shared_expert.up_proj.weight", 7},
+                    {"mlp.shared_expert.up_proj.scales", 8},   {"mlp.shared_expert.up_proj.biases", 9},
+                    {"mlp.shared_expert.gate_proj.weight", 10}, {"mlp.shared_expert.gate_proj.scales", 11},
+                    {"mlp.shared_expert.gate_proj.biases", 12}, {"mlp.shared_expert.down_proj.weight", 13},
+                    {"mlp.shared_expert.down_proj.scales", 14}, {"mlp.shared_expert.down_proj.biases", 15}};
+        if (layer >= 0 && (rest.rfind("mlp.switch_mlp.", 0) == 0 || rest.rfind("mlp.experts.", 0) == 0))
+            return 1;  // routed experts come from the BKEX files
+        for (const auto& m : kMoe) {
+            if (layer < 0 || rest != m.name) continue;
+            const int fdt = dtype == 0 ? 0 : dtype == 1 ? 2 : dtype == 3 ? 1 : -1;  // bakan_forward dtype codes
+            if (fdt < 0) {
+                fprintf(stderr, "[kandiga] ERROR: bakan_full: %s must be fp16, bf16 or packed\n", name);
+                return -1;
+            }
+            const int rows = ndim == 2 ? (int)shape[0] : 1;
+            const int cols = ndim == 2 ? (int)shape[1] : ndim == 1 ? (int)shape[0] : 0;
+            return bakan_forward_set_weight(e->moe, layer, m.wt, data, size, rows, cols, fdt) == 0 ? 0 : -1;
+        }
+    }
     kq::full::Weight wt;
     wt.shape.assign(shape, shape + ndim);
     wt.dtype = dtype;
@@ -1107,9 +1458,16 @@ extern "C" void bakan_full_reset_cache(void* engine) {
     Engine* e = static_cast<Engine*>(engine);
     if (!e || !e->built) return;
     const size_t kv = (size_t)e->c.nkv * e->c.max_seq * e->c.hd * sizeof(__half);
+    const size_t conv = (size_t)e->c.conv_dim() * e->c.conv_k * sizeof(__half);
+    const size_t st = (size_t)e->c.lnv * e->c.lvd * e->c.lkd * sizeof(float);
     for (auto& ly : e->L) {
-        cudaMemsetAsync(ly.kc, 0, kv, e->s);
-        cudaMemsetAsync(ly.vc, 0, kv, e->s);
+        if (ly.linear) {
+            cudaMemsetAsync(ly.conv_state, 0, conv, e->s);
+            cudaMemsetAsync(ly.state, 0, st, e->s);
+        } else {
+            cudaMemsetAsync(ly.kc, 0, kv, e->s);
+            cudaMemsetAsync(ly.vc, 0, kv, e->s);
+        }
     }
     cudaStreamSynchronize(e->s);
     e->position = 0;
@@ -1139,12 +1497,13 @@ extern "C" int bakan_full_set_kv_cache(void* engine, int attn_layer_idx, const v
         kq::full::err("engine not built");
         return -1;
     }
-    if (attn_layer_idx < 0 || attn_layer_idx >= (int)e->L.size() || seq_len <= 0 || seq_len > e->c.max_seq ||
-        num_kv_heads != e->c.nkv || head_dim != e->c.hd || !keys_data || !values_data) {
+    kq::full::Layer* lp = kq::full::nth_layer(e, false, attn_layer_idx);
+    if (!lp || seq_len <= 0 || seq_len > e->c.max_seq || num_kv_heads != e->c.nkv || head_dim != e->c.hd ||
+        !keys_data || !values_data) {
         kq::full::err("set_kv_cache: layer, length or shape outside the model's");
         return -1;
     }
-    auto& ly = e->L[attn_layer_idx];
+    auto& ly = *lp;
     const size_t row = (size_t)head_dim * sizeof(__half);
     const size_t kvb = (size_t)e->c.nkv * e->c.max_seq * row;
     cudaError_t ce = cudaMemsetAsync(ly.kc, 0, kvb, e->s);
@@ -1158,6 +1517,48 @@ extern "C" int bakan_full_set_kv_cache(void* engine, int attn_layer_idx, const v
                                (size_t)seq_len * row, num_kv_heads, cudaMemcpyHostToDevice, e->s);
     if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->s);
     return ce == cudaSuccess ? 0 : -1;
+}
+
+// replaces kandiga/metal/full_forward.h:174 (state [hv][dv][dk] fp32)
+extern "C" int bakan_full_set_linear_state(void* engine, int lin_layer_idx, const void* state_data, int state_bytes) {
+    Engine* e = static_cast<Engine*>(engine);
+    if (!e || !e->built) {
+        kq::full::err("engine not built");
+        return -1;
+    }
+    kq::full::Layer* lp = kq::full::nth_layer(e, true, lin_layer_idx);
+    const size_t want = (size_t)e->c.lnv * e->c.lvd * e->c.lkd * sizeof(float);
+    if (!lp) {
+        fprintf(stderr, "[kandiga] ERROR: bakan_full: no linear-attention layer %d\n", lin_layer_idx);
+        return -1;
+    }
+    if (!state_data || state_bytes < 0 || (size_t)state_bytes != want) {
+        fprintf(stderr, "[kandiga] ERROR: bakan_full: linear state %d: %d bytes (expected %zu)\n", lin_layer_idx,
+                state_bytes, want);
+        return -1;
+    }
+    return cudaMemcpy(lp->state, state_data, want, cudaMemcpyHostToDevice) == cudaSuccess ? 0 : -1;
+}
+
+// replaces kandiga/metal/full_forward.h:193 (conv buffer [channel][kernel_pos] fp16)
+extern "C" int bakan_full_set_conv_state(void* engine, int lin_layer_idx, const void* conv_data, int conv_bytes) {
+    Engine* e = static_cast<Engine*>(engine);
+    if (!e || !e->built) {
+        kq::full::err("engine not built");
+        return -1;
+    }
+    kq::full::Layer* lp = kq::full::nth_layer(e, true, lin_layer_idx);
+    const size_t want = (size_t)e->c.conv_dim() * e->c.conv_k * sizeof(__half);
+    if (!lp) {
+        fprintf(stderr, "[kandiga] ERROR: bakan_full: no linear-attention layer %d\n", lin_layer_idx);
+        return -1;
+    }
+    if (!conv_data || conv_bytes < 0 || (size_t)conv_bytes != want) {
+        fprintf(stderr, "[kandiga] ERROR: bakan_full: conv state %d: %d bytes (expected %zu)\n", lin_layer_idx,
+                conv_bytes, want);
+        return -1;
+    }
+    return cudaMemcpy(lp->conv_state, conv_data, want, cudaMemcpyHostToDevice) == cudaSuccess ? 0 : -1;
 }
 
 extern "C" int bakan_full_set_position(void* engine, int position) {

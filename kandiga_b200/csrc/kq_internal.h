@@ -46,6 +46,16 @@ int bkex_parse(const uint8_t* hdr, size_t n, BkexInfo* info);
 int dense_gemv_res(const kq_qmat* m, const void* x, int x_dtype, int T, const void* norm_w, float eps,
                    int activation, void* y, int y_dtype, const void* residual, void* stream);
 
+// The MoE block engine (bakan_forward_*, kq_forward.cu) as one layer kind of
+// the whole-model decode step.  moe_block_prepare: all weights of `layer` set,
+// workspace allocated (call before capturing); moe_block_enqueue: out = in +
+// MoE(rmsnorm(in)) on stream s (fp16 [hidden]; out != in); moe_block_status:
+// the device status word its kernels latch into.
+int moe_block_prepare(void* engine, int layer);
+int moe_block_enqueue(void* engine, int layer, const __half* in, __half* out, cudaStream_t s);
+int moe_block_hidden(void* engine);
+uint32_t* moe_block_status(void* engine);
+
 int load_bkex_dir(const char* packed_dir, int num_layers, cudaStream_t s, kq_table** out, BkexInfo* info);
 
 // Workspace carve-up for kq_moe_* (offsets in bytes, 256-aligned).

@@ -106,6 +106,18 @@ class FullForwardEngine:
                                                      v.ctypes.data_as(ctypes.c_void_p), k.shape[1], k.shape[0],
                                                      k.shape[2]))
 
+    def set_linear_state(self, lin_layer_idx: int, state: np.ndarray) -> int:
+        """GatedDeltaNet state of the lin_layer_idx-th linear layer, fp32 [v heads, v dim, k dim]."""
+        a = np.ascontiguousarray(state, dtype=np.float32)
+        return int(self._lib.bakan_full_set_linear_state(self._engine, lin_layer_idx,
+                                                         a.ctypes.data_as(ctypes.c_void_p), a.nbytes))
+
+    def set_conv_state(self, lin_layer_idx: int, conv: np.ndarray) -> int:
+        """conv1d window of the lin_layer_idx-th linear layer, fp16 [channels, kernel]."""
+        a = np.ascontiguousarray(conv, dtype=np.float16)
+        return int(self._lib.bakan_full_set_conv_state(self._engine, lin_layer_idx,
+                                                       a.ctypes.data_as(ctypes.c_void_p), a.nbytes))
+
     def set_position(self, position: int) -> int:
         return int(self._lib.bakan_full_set_position(self._engine, position))
 

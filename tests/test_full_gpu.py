@@ -132,3 +132,78 @@ def test_errors_are_reported(gpu):
     # unsupported shapes are refused at init
     with pytest.raises(RuntimeError):
         FullForwardEngine("", 2, config=dict(cfg, head_dim=96))
+
+
+HYBRID = dict(hidden_size=256, num_hidden_layers=4, num_attention_heads=4, num_key_value_heads=2, head_dim=64,
+              vocab_size=512, rms_norm_eps=1e-6, rope_theta=10000.0, partial_rotary_factor=0.25, max_cache_len=64,
+              linear_num_key_heads=2, linear_num_value_heads=8, linear_key_head_dim=64, linear_value_head_dim=64,
+              linear_conv_kernel_dim=4, full_attention_interval=4, num_experts=16, num_experts_per_tok=4,
+              moe_intermediate_size=256, shared_expert_intermediate_size=256)
+
+
+@pytest.fixture(scope="module")
+def hybrid(tmp_path_factory, gpu):
+    """the hybrid shape in miniature: 3 GatedDeltaNet layers and 1 attention
+    layer (with output gate), MoE blocks with a shared expert; BKEX expert
+    files and config.json in a directory, as bakan_full_init reads them"""
+    import json
+    from oracle.full_step import random_moe
+    from tests.test_bakan_gpu import write_bkex
+    d = tmp_path_factory.mktemp("hybrid")
+    W = random_model(HYBRID, bits=4, seed=21, gate=True)
+    moe, WM = random_moe(HYBRID, seed=21)
+    write_bkex(str(d), [m["experts"] for m in moe])
+    (d / "config.json").write_text(json.dumps(HYBRID))
+    return str(d), W, moe, WM
+
+
+def hybrid_engine(d, W, WM):
+    from kandiga_b200 import _native as N
+    from kandiga_b200.full import FullForwardEngine
+    e = FullForwardEngine(d, HYBRID["num_hidden_layers"])   # config.json from the directory
+    load(e, W, "bf16")
+    load(e, WM, "bf16")
+    assert N.load().bakan_full_build(e._engine) == 0
+    return e
+
+
+def test_hybrid_gated_delta_net_and_moe_match_oracle(hybrid):
+    d, W, moe, WM = hybrid
+    ref = FullStepRef(HYBRID, W, 4, "bf16", moe=moe)
+    e = hybrid_engine(d, W, WM)
+    rng = np.random.RandomState(8)
+    worst = 0.0
+    for pos, t in enumerate(rng.randint(0, HYBRID["vocab_size"], 24)):
+        got = e.forward(int(t), pos)
+        want = ref.step(int(t), pos)
+        err = rel_l2(got, want)
+        worst = max(worst, err)
+        assert err < TOL, (pos, err)
+    print("hybrid worst rel L2", worst)
+
+
+def test_hybrid_state_handover(hybrid):
+    """bakan_full_set_linear_state / set_conv_state / set_kv_cache / set_position:
+    a state handed over from elsewhere, then decode continues from it"""
+    d, W, moe, WM = hybrid
+    ref = FullStepRef(HYBRID, W, 4, "bf16", moe=moe)
+    e = hybrid_engine(d, W, WM)
+    rng = np.random.RandomState(3)
+    S = 20
+    lin = [l for l in range(HYBRID["num_hidden_layers"]) if ref.kinds[l]]
+    att = [l for l in range(HYBRID["num_hidden_layers"]) if not ref.kinds[l]]
+    for i, l in enumerate(lin):
+        st = (rng.randn(*ref.state[l].shape) * 0.1).astype(np.float32)
+        cv = (rng.randn(*ref.conv[l].shape) * 0.5).astype(np.float16)
+        assert e.set_linear_state(i, st) == 0 and e.set_conv_state(i, cv) == 0
+        ref.state[l], ref.conv[l] = st, cv
+    for i, l in enumerate(att):
+        k = rng.randn(HYBRID["num_key_value_heads"], S, HYBRID["head_dim"]).astype(np.float16)
+        v = rng.randn(HYBRID["num_key_value_heads"], S, HYBRID["head_dim"]).astype(np.float16)
+        assert e.set_kv_cache(i, k, v) == 0
+        ref.kc[l, :, :S], ref.vc[l, :, :S] = k, v
+    assert e.set_position(S) == 0
+    for i in range(3):
+        assert rel_l2(e.forward(7 + i, S + i), ref.step(7 + i, S + i)) < TOL
+    assert e.set_linear_state(len(lin), np.zeros_like(ref.state[0])) == -1   # no such linear layer
+    assert e.set_conv_state(0, np.zeros((3, 3), np.float16)) == -1           # wrong size
