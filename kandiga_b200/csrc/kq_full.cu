@@ -911,8 +911,7 @@ static cudaError_t pdl_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
 }
 
 static cudaError_t smem_opt_in(const void* fn, size_t bytes) {
-    return bytes > 48 * 1024 ? cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes)
-                             : cudaSuccess;
+    return bytes > 48 * 1024 ? raise_smem_limit(fn, bytes) : cudaSuccess;
 }
 
 // launch = false: only raise the kernel's shared-memory limit (done once,
@@ -1020,9 +1019,18 @@ static int enqueue_body(Engine* e) {
     for (int l = 0; l < c.layers; ++l) {
         const Layer& ly = e->L[l];
         int rc = ly.linear ? enqueue_linear(e, ly, cur) : enqueue_attention(e, ly, cur);
-        if (rc) return rc;
+        if (rc) {
+            fprintf(stderr, "[kandiga] ERROR: bakan_full: layer %d token mixer: code %d (%s)\n", l, rc,
+                    cudaGetErrorString(cudaGetLastError()));
+            return rc;
+        }
         if (e->moe) {
-            if (moe_block_enqueue(e->moe, l, cur, other, e->s) != KQ_OK) return KQ_ERR_CUDA;
+            rc = moe_block_enqueue(e->moe, l, cur, other, e->s);
+            if (rc != KQ_OK) {
+                fprintf(stderr, "[kandiga] ERROR: bakan_full: layer %d MoE block: code %d (%s)\n", l, rc,
+                        cudaGetErrorString(cudaGetLastError()));
+                return KQ_ERR_CUDA;
+            }
             std::swap(cur, other);
         } else {
             rc = dense_gemv_res(ly.gate_up, cur, KQ_DT_F16, 1, ly.post_norm, c.eps, c.act, e->act, KQ_DT_F16, nullptr,
@@ -1047,6 +1055,8 @@ static int capture(Engine* e, int (*fn)(Engine*), cudaGraphExec_t* out) {
     const int rc = fn(e);
     const cudaError_t ce = cudaStreamEndCapture(e->s, &g);
     if (rc || ce != cudaSuccess) {
+        fprintf(stderr, "[kandiga] ERROR: bakan_full: capture: enqueue code %d, end capture: %s\n", rc,
+                cudaGetErrorString(ce));
         if (g) cudaGraphDestroy(g);
         cudaGetLastError();
         return rc ? rc : KQ_ERR_CUDA;

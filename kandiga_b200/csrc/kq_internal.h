@@ -56,6 +56,12 @@ int moe_block_enqueue(void* engine, int layer, const __half* in, __half* out, cu
 int moe_block_hidden(void* engine);
 uint32_t* moe_block_status(void* engine);
 
+// Raise a kernel's dynamic shared-memory limit to at least `bytes` on the
+// current device.  One record per (kernel, device) for the whole library, and
+// the limit only ever rises, so launch paths that share a kernel cannot lower
+// it under one another.
+cudaError_t raise_smem_limit(const void* kernel, size_t bytes);
+
 int load_bkex_dir(const char* packed_dir, int num_layers, cudaStream_t s, kq_table** out, BkexInfo* info);
 
 // Workspace carve-up for kq_moe_* (offsets in bytes, 256-aligned).

@@ -512,16 +512,8 @@ __global__ void __launch_bounds__(DOWN_NW * 32, 1) moe_down_kernel(const GemvPar
 
 // Raise a kernel's dynamic shared-memory limit once per device.
 template <typename Kern>
-static cudaError_t smem_attr(Kern kern, size_t bytes, int* configured) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if ((size_t)configured[dev] < bytes) {
-        cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-        if (err != cudaSuccess) return err;
-        configured[dev] = (int)bytes;
-    }
-    return cudaSuccess;
+static cudaError_t smem_attr(Kern kern, size_t bytes, int* /*unused*/) {
+    return raise_smem_limit(reinterpret_cast<const void*>(kern), bytes);
 }
 
 template <typename Kern>
@@ -564,7 +556,32 @@ static cudaError_t launch_down_t(const GemvParams& p, cudaStream_t s) {
     return launch_pdl(kern, dim3((unsigned)(p.T * p.nrt)), dim3(DOWN_NW * 32), smem, s, p);
 }
 
+// Dense matrices (MODE_DENSE / MODE_DENSE_PAIR): warps per CTA and tile
+// buffers per warp of the same kernel, tuned apart from the routed path.
+#ifndef KQ_DENSE_NW
+#define KQ_DENSE_NW 4
+#endif
+#ifndef KQ_DENSE_NBUF
+#define KQ_DENSE_NBUF 2
+#endif
+
+template <int BITS, int SB_DT>
+static cudaError_t launch_dense_t(const GemvParams& p, cudaStream_t s) {
+    static int configured[64] = {0};
+    auto kern = qunit_kernel<BITS, SB_DT, KQ_DENSE_NW, KQ_DENSE_NBUF>;
+    const size_t smem = qunit_smem<BITS, KQ_DENSE_NW, KQ_DENSE_NBUF>(p.nst);
+    cudaError_t err = smem_attr(kern, smem, configured);
+    if (err != cudaSuccess) return err;
+    const long units = (long)p.T * p.K * p.nrt;
+    return launch_pdl(kern, dim3((unsigned)units), dim3(KQ_DENSE_NW * 32), smem, s, p);
+}
+
 static cudaError_t launch_qunit(int bits, int sb_dt, const GemvParams& p, cudaStream_t s) {
+    if (p.mode == MODE_DENSE || p.mode == MODE_DENSE_PAIR) {
+        if (bits == 3)
+            return sb_dt == KQ_DT_F16 ? launch_dense_t<3, KQ_DT_F16>(p, s) : launch_dense_t<3, KQ_DT_BF16>(p, s);
+        return sb_dt == KQ_DT_F16 ? launch_dense_t<4, KQ_DT_F16>(p, s) : launch_dense_t<4, KQ_DT_BF16>(p, s);
+    }
     if (bits == 3) return sb_dt == KQ_DT_F16 ? launch_qunit_t<3, KQ_DT_F16>(p, s) : launch_qunit_t<3, KQ_DT_BF16>(p, s);
     return sb_dt == KQ_DT_F16 ? launch_qunit_t<4, KQ_DT_F16>(p, s) : launch_qunit_t<4, KQ_DT_BF16>(p, s);
 }

@@ -496,3 +496,20 @@ extern "C" int kq_table_load_bkex(kq_table* t, int layer, const void* file_bytes
     cudaFree(staging);
     return rc;
 }
+
+#include <map>
+#include <mutex>
+#include <utility>
+
+cudaError_t kq::raise_smem_limit(const void* kernel, size_t bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, size_t> limits;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    size_t& cur = limits[{kernel, dev}];
+    if (cur >= bytes) return cudaSuccess;
+    const cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (err == cudaSuccess) cur = bytes;
+    return err;
+}
