@@ -565,15 +565,27 @@ static cudaError_t launch_down_t(const GemvParams& p, cudaStream_t s) {
 #define KQ_DENSE_NBUF 2
 #endif
 
-template <int BITS, int SB_DT>
-static cudaError_t launch_dense_t(const GemvParams& p, cudaStream_t s) {
-    static int configured[64] = {0};
-    auto kern = qunit_kernel<BITS, SB_DT, KQ_DENSE_NW, KQ_DENSE_NBUF>;
-    const size_t smem = qunit_smem<BITS, KQ_DENSE_NW, KQ_DENSE_NBUF>(p.nst);
-    cudaError_t err = smem_attr(kern, smem, configured);
+#ifndef KQ_WIDE_MIN_NST
+#define KQ_WIDE_MIN_NST 8  // column tiles from which a matrix gets wide CTAs
+#endif
+
+template <int BITS, int SB_DT, int NW, int NBUF>
+static cudaError_t launch_dense_nw(const GemvParams& p, cudaStream_t s) {
+    auto kern = qunit_kernel<BITS, SB_DT, NW, NBUF>;
+    const size_t smem = qunit_smem<BITS, NW, NBUF>(p.nst);
+    cudaError_t err = smem_attr(kern, smem, nullptr);
     if (err != cudaSuccess) return err;
     const long units = (long)p.T * p.K * p.nrt;
-    return launch_pdl(kern, dim3((unsigned)units), dim3(KQ_DENSE_NW * 32), smem, s, p);
+    return launch_pdl(kern, dim3((unsigned)units), dim3(NW * 32), smem, s, p);
+}
+
+// Long rows (K >= 4096) with few row tiles (one wave at two CTAs per SM) get
+// 16 warps per CTA: each thread stages and multiplies a quarter as much.
+template <int BITS, int SB_DT>
+static cudaError_t launch_dense_t(const GemvParams& p, cudaStream_t s) {
+    const long units = (long)p.T * p.K * p.nrt;
+    if (p.nst >= KQ_WIDE_MIN_NST && units <= 2L * 148) return launch_dense_nw<BITS, SB_DT, 16, 1>(p, s);
+    return launch_dense_nw<BITS, SB_DT, KQ_DENSE_NW, KQ_DENSE_NBUF>(p, s);
 }
 
 static cudaError_t launch_qunit(int bits, int sb_dt, const GemvParams& p, cudaStream_t s) {
