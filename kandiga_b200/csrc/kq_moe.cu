@@ -251,8 +251,11 @@ __host__ __device__ constexpr size_t qunit_smem(int nst) {
            256;                                                           // scratch
 }
 
-template <int BITS, int SB_DT, int NW, int NBUF>
+// RT > 1 (dense matrices only): RT row tiles per CTA, NW / RT warps each,
+// sharing one staged input.
+template <int BITS, int SB_DT, int NW, int NBUF, int RT = 1>
 __global__ void __launch_bounds__(NW * 32) qunit_kernel(const GemvParams p) {
+    constexpr int WPG = NW / RT;  // warps per row tile
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int TB = TileT<BITS>::BYTES;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -275,7 +278,11 @@ __global__ void __launch_bounds__(NW * 32) qunit_kernel(const GemvParams p) {
 
     const int mode = p.mode;
     const int u = blockIdx.x;
-    const int tk = u / p.nrt, rt = u % p.nrt;
+    const int nrtc = (p.nrt + RT - 1) / RT;  // CTAs per token
+    const int tk = u / nrtc;
+    const int grp = warp / WPG, wg = warp % WPG;
+    const int rt = (u % nrtc) * RT + grp;    // this warp's row tile
+    const bool rt_ok = rt < p.nrt;
     const int t = tk / p.K, k = tk % p.K;
     uint8_t* my_tiles = tiles + (size_t)warp * NBUF * TB;
     uint64_t* my_bars = bars + warp * NBUF;
@@ -284,14 +291,20 @@ __global__ void __launch_bounds__(NW * 32) qunit_kernel(const GemvParams p) {
         fence_mbar_init();
     }
     __syncthreads();
-    auto ntiles_of = [&](int w) { return w < p.nst ? (p.nst - 1 - w) / NW + 1 : 0; };
-    const int ntl = ntiles_of(warp);  // this warp's tiles: st = warp, warp + NW, ...
+    // warp w's tiles: column tiles st = w % WPG, + WPG, ... of row tile (u % nrtc) * RT + w / WPG
+    auto ntiles_of = [&](int w) {
+        const int wl = w % WPG;
+        if ((u % nrtc) * RT + w / WPG >= p.nrt) return 0;
+        return wl < p.nst ? (p.nst - 1 - wl) / WPG + 1 : 0;
+    };
+    const int ntl = ntiles_of(warp);
     const uint64_t pol = policy_evict_first();
     auto issue_for = [&](int w, int i, const uint8_t* mb) {
-        const int st = w + i * NW, slot = i % NBUF;
+        const int st = w % WPG + i * WPG, slot = i % NBUF;
+        const int rtw = (u % nrtc) * RT + w / WPG;
         uint64_t* bar = bars + w * NBUF + slot;
         mbar_expect_tx(bar, TB);
-        bulk_g2s(tiles + ((size_t)w * NBUF + slot) * TB, mb + ((size_t)rt * p.nst + st) * TB, TB, bar, pol);
+        bulk_g2s(tiles + ((size_t)w * NBUF + slot) * TB, mb + ((size_t)rtw * p.nst + st) * TB, TB, bar, pol);
     };
 
     bool valid = true;
@@ -354,16 +367,16 @@ __global__ void __launch_bounds__(NW * 32) qunit_kernel(const GemvParams p) {
             fence_proxy_async_smem();
             issue_for(warp, i + NBUF, mbase);
         }
-        tile_compute<BITS, SB_DT>(R, warp + i * NW, xs, cx, y0, y1);
+        tile_compute<BITS, SB_DT>(R, wg + i * WPG, xs, cx, y0, y1);
     }
     red[warp * 32 + lane] = make_float2(y0, y1);
     __syncthreads();
-    if (warp != 0) return;
+    if (wg != 0 || !rt_ok) return;  // the first warp of each row tile finishes it
     y0 = 0.f;
     y1 = 0.f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) {
-        const float2 v = red[w * 32 + lane];
+    for (int w = 0; w < WPG; ++w) {
+        const float2 v = red[(grp * WPG + w) * 32 + lane];
         y0 += v.x;
         y1 += v.y;
     }
@@ -569,15 +582,22 @@ static cudaError_t launch_down_t(const GemvParams& p, cudaStream_t s) {
 #define KQ_WIDE_MIN_NST 8  // column tiles from which a matrix gets wide CTAs
 #endif
 
-template <int BITS, int SB_DT, int NW, int NBUF>
+template <int BITS, int SB_DT, int NW, int NBUF, int RT = 1>
 static cudaError_t launch_dense_nw(const GemvParams& p, cudaStream_t s) {
-    auto kern = qunit_kernel<BITS, SB_DT, NW, NBUF>;
+    auto kern = qunit_kernel<BITS, SB_DT, NW, NBUF, RT>;
     const size_t smem = qunit_smem<BITS, NW, NBUF>(p.nst);
     cudaError_t err = smem_attr(kern, smem, nullptr);
     if (err != cudaSuccess) return err;
-    const long units = (long)p.T * p.K * p.nrt;
+    const long units = (long)p.T * p.K * ((p.nrt + RT - 1) / RT);
     return launch_pdl(kern, dim3((unsigned)units), dim3(NW * 32), smem, s, p);
 }
+
+#ifndef KQ_SHORT_RT
+#define KQ_SHORT_RT 4  // row tiles per CTA for short rows with many row tiles
+#endif
+#ifndef KQ_SHORT_NBUF
+#define KQ_SHORT_NBUF 1
+#endif
 
 // Long rows (K >= 4096) with few row tiles (one wave at two CTAs per SM) get
 // 16 warps per CTA: each thread stages and multiplies a quarter as much.
@@ -585,6 +605,8 @@ template <int BITS, int SB_DT>
 static cudaError_t launch_dense_t(const GemvParams& p, cudaStream_t s) {
     const long units = (long)p.T * p.K * p.nrt;
     if (p.nst >= KQ_WIDE_MIN_NST && units <= 2L * 148) return launch_dense_nw<BITS, SB_DT, 16, 1>(p, s);
+    if (KQ_SHORT_RT > 1 && p.nst < KQ_WIDE_MIN_NST && units > 2L * 148)
+        return launch_dense_nw<BITS, SB_DT, 4 * KQ_SHORT_RT, KQ_SHORT_NBUF, KQ_SHORT_RT>(p, s);
     return launch_dense_nw<BITS, SB_DT, KQ_DENSE_NW, KQ_DENSE_NBUF>(p, s);
 }
 
