@@ -248,7 +248,8 @@ int kq_table_load_mlx(kq_table* t, int layer, int expert_begin, int num_experts,
                       const kq_mlx_matrix* down, void* stream);
 
 /* Load one BKEX layer file image (header + payload) that the caller has in
- * host memory.  The header must match the table's desc. */
+ * host memory into experts [0, file's count) of `layer`.  The header must
+ * match the table's desc, which may hold more experts than the file. */
 int kq_table_load_bkex(kq_table* t, int layer, const void* file_bytes, size_t nbytes, void* stream);
 
 /* Unpack one matrix (0 gate, 1 up, 2 down) of one expert back to MLX layout

@@ -18,7 +18,8 @@
 
 namespace kq {
 
-int load_bkex_dir(const char* packed_dir, int num_layers, cudaStream_t s, kq_table** out, BkexInfo* info) {
+int load_bkex_dir(const char* packed_dir, int num_layers, cudaStream_t s, kq_table** out, BkexInfo* info,
+                  int extra_experts) {
     *out = nullptr;
     kq_table* table = nullptr;
     auto fail = [&]() {
@@ -51,7 +52,7 @@ int load_bkex_dir(const char* packed_dir, int num_layers, cudaStream_t s, kq_tab
             }
             kq_table_desc d{};
             d.num_layers = num_layers;
-            d.num_experts = info->num_experts;
+            d.num_experts = info->num_experts + extra_experts;
             d.hidden = info->hidden;
             d.inter = info->inter;
             d.bits = info->bits;

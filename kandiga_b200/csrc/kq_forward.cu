@@ -96,6 +96,12 @@ struct FwdLayer {
     DevTensor wt[WT_COUNT];
     kq_qmat* router = nullptr;
     bool shared_loaded = false;
+    // fast path (finalize_layer): the shared expert as expert E of the routed
+    // table, the router with the shared-gate row as row E, the norm in fp16
+    bool dirty = true;
+    bool merged = false;
+    kq_qmat* router_ext = nullptr;  // rows: E routed, 1 gate, zero rows to a multiple of 16
+    __half* norm16 = nullptr;
 };
 
 struct FwdEngine {
@@ -225,7 +231,7 @@ bool alloc_all(FwdEngine* e) {
     const int H = e->info.hidden, E = e->info.num_experts;
     auto dev = [](void** p, size_t n) { return cudaMalloc(p, n) == cudaSuccess; };
     bool ok = dev((void**)&e->dh, H * 2) && dev((void**)&e->dnorm, H * 2) && dev((void**)&e->dshared, H * 2) &&
-              dev((void**)&e->dout, H * 2) && dev((void**)&e->dlogits, (size_t)E * 4) && dev((void**)&e->droute, H * 4) &&
+              dev((void**)&e->dout, H * 2) && dev((void**)&e->dlogits, (size_t)(E + 16) * 4) && dev((void**)&e->droute, H * 4) &&
               dev((void**)&e->dgate, 4) && dev((void**)&e->dones, 4) && dev((void**)&e->dw, 32 * 4) &&
               dev((void**)&e->dgw, 4) && dev((void**)&e->didx, 32 * 4) && dev((void**)&e->dzero, 4) &&
               dev((void**)&e->dgidx, 4);
@@ -242,7 +248,7 @@ bool alloc_all(FwdEngine* e) {
 }
 
 bool ensure_ws(FwdEngine* e) {
-    size_t need = kq_moe_workspace_size(e->routed, 1, e->top_k);
+    size_t need = kq_moe_workspace_size(e->routed, 1, e->top_k + 1);
     if (e->shared) need = std::max(need, kq_moe_workspace_size(e->shared, 1, 1));
     if (need <= e->ws_bytes) return true;
     drop_graphs(e);
@@ -257,10 +263,98 @@ bool ensure_ws(FwdEngine* e) {
     return kq_workspace_init(e->ws, need, e->stream) == KQ_OK;
 }
 
+__global__ void fwd_to_f16_kernel(const void* __restrict__ src, int dtype, int n, __half* __restrict__ dst) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) dst[i] = __float2half(load_as_float(src, dtype, i));
+}
+
+// Build the fast path of a layer once its tensors are all set: the shared
+// expert into slot E of the routed table (same inter, bits and scale dtype as
+// the routed experts), the router with the gate row appended (same bits and
+// scale dtype), the norm weight in fp16.  Layers that do not match keep the
+// separate path.  Called before a graph of the layer is captured.
+int finalize_layer(FwdEngine* e, int layer) {
+    FwdLayer& L = e->layers[layer];
+    if (!L.dirty) return 0;
+    const int H = e->info.hidden, E = e->info.num_experts;
+    cudaStream_t s = e->stream;
+    L.merged = false;
+    if (L.router_ext) kq_qmat_destroy(L.router_ext);
+    L.router_ext = nullptr;
+    if (L.shared_loaded) {
+        int I, b, sb;
+        if (matrix_ok(L, WT_SHARED_UP_W, H, &I, &b, &sb) && I == e->info.inter && b == e->info.bits &&
+            sb == e->info.sb_dtype) {
+            const kq_mlx_matrix g = mlx_of(L, WT_SHARED_GATE_PROJ_W), u = mlx_of(L, WT_SHARED_UP_W),
+                                dn = mlx_of(L, WT_SHARED_DOWN_W);
+            if (kq_table_load_mlx(e->routed, layer, E, 1, &g, &u, &dn, s) != KQ_OK) return -1;
+            L.merged = true;
+        }
+    }
+    int rr, rb, rs, gr, gb, gs;
+    if (L.router && have(L, WT_SHARED_GATE_W, WT_SHARED_GATE_B) && matrix_ok(L, WT_ROUTER_WEIGHT, H, &rr, &rb, &rs) &&
+        matrix_ok(L, WT_SHARED_GATE_W, H, &gr, &gb, &gs) && gr >= 1 && gb == rb && gs == rs) {
+        const int rows = (E + 1 + 15) / 16 * 16;
+        const size_t wrow = (size_t)H * rb / 8, srow = (size_t)H / 64 * 2;
+        uint8_t* buf = nullptr;
+        const size_t wbytes = rows * wrow, sbytes = rows * srow;
+        if (cudaMalloc(&buf, wbytes + 2 * sbytes) != cudaSuccess) {
+            cudaGetLastError();
+            return -1;
+        }
+        bool ok = cudaMemsetAsync(buf, 0, wbytes + 2 * sbytes, s) == cudaSuccess;
+        uint8_t* parts[3] = {buf, buf + wbytes, buf + wbytes + sbytes};
+        const size_t per[3] = {wrow, srow, srow};
+        for (int k = 0; k < 3 && ok; ++k) {
+            ok = cudaMemcpyAsync(parts[k], L.wt[WT_ROUTER_WEIGHT + k].p, (size_t)E * per[k], cudaMemcpyDeviceToDevice,
+                                 s) == cudaSuccess &&
+                 cudaMemcpyAsync(parts[k] + (size_t)E * per[k], L.wt[WT_SHARED_GATE_W + k].p, per[k],
+                                 cudaMemcpyDeviceToDevice, s) == cudaSuccess;
+        }
+        kq_mlx_matrix m{};
+        m.weight = parts[0];
+        m.scales = parts[1];
+        m.biases = parts[2];
+        ok = ok && kq_qmat_create(rows, H, rb, rs, 0, &L.router_ext) == KQ_OK &&
+             kq_qmat_load_mlx(L.router_ext, &m, nullptr, s) == KQ_OK && cudaStreamSynchronize(s) == cudaSuccess;
+        cudaFree(buf);
+        if (!ok) {
+            if (L.router_ext) kq_qmat_destroy(L.router_ext);
+            L.router_ext = nullptr;
+            return -1;
+        }
+    }
+    const DevTensor& nt = L.wt[WT_POST_ATTN_NORM];
+    if (nt.p) {
+        if (!L.norm16 && cudaMalloc(&L.norm16, (size_t)H * 2) != cudaSuccess) {
+            cudaGetLastError();
+            return -1;
+        }
+        fwd_to_f16_kernel<<<(H + 255) / 256, 256, 0, s>>>(nt.p, nt.dtype == FWD_BF16 ? KQ_DT_BF16 : KQ_DT_F16, H,
+                                                          L.norm16);
+        if (cudaStreamSynchronize(s) != cudaSuccess) return -1;
+    }
+    L.dirty = false;
+    return 0;
+}
+
 // Enqueue one block on stream s: out = [in] + MoE(x), x = in or rmsnorm(in).
 int enqueue_block_io(FwdEngine* e, int layer, bool normed, const __half* in, __half* out, cudaStream_t s) {
     const FwdLayer& L = e->layers[layer];
     const int H = e->info.hidden;
+    if (L.merged && L.router_ext && (normed || L.norm16)) {
+        // router + shared gate in one GEMV (RMSNorm prologue), top-K + (shared, sigmoid(gate)),
+        // then K + 1 experts whose down pass blends them into the residual
+        const int E = e->info.num_experts;
+        const __half* nw = normed ? nullptr : L.norm16;
+        int rc = dense_gemv_res(L.router_ext, in, KQ_DT_F16, 1, nw, e->eps, KQ_ACT_SILU, e->dlogits, KQ_DT_F32,
+                                nullptr, s);
+        if (rc == KQ_OK) rc = route_with_shared(e->dlogits, E, e->top_k, E, e->didx, e->dw, s);
+        if (rc == KQ_OK)
+            rc = moe_decode_ex(e->routed, layer, in, KQ_DT_F16, 1, nullptr, e->didx, e->dw, e->top_k + 1, nullptr, out,
+                               KQ_DT_F16, normed ? nullptr : in, nw, e->eps, e->ws, e->ws_bytes, s);
+        return rc;
+    }
     const __half* x = in;
     if (!normed) {
         fwd_rmsnorm_kernel<<<1, FWD_NORM_THREADS, 0, s>>>(in, L.wt[WT_POST_ATTN_NORM].p,
@@ -270,9 +364,11 @@ int enqueue_block_io(FwdEngine* e, int layer, bool normed, const __half* in, __h
         if (cudaGetLastError() != cudaSuccess) return KQ_ERR_CUDA;
         x = e->dnorm;
     }
+    // the routed table has one slot past the E routed experts: route over E explicitly
     int rc = kq_dense_gemv(L.router, x, KQ_DT_F16, 1, nullptr, 0.f, KQ_ACT_SILU, e->dlogits, KQ_DT_F32, s);
+    if (rc == KQ_OK) rc = kq_router_topk(e->dlogits, 1, e->info.num_experts, e->top_k, e->didx, e->dw, s);
     if (rc == KQ_OK)
-        rc = kq_moe_decode(e->routed, layer, x, KQ_DT_F16, 1, e->dlogits, e->didx, e->dw, e->top_k, nullptr, e->droute,
+        rc = kq_moe_decode(e->routed, layer, x, KQ_DT_F16, 1, nullptr, e->didx, e->dw, e->top_k, nullptr, e->droute,
                            KQ_DT_F32, nullptr, e->ws, e->ws_bytes, s);
     const DevTensor& gw = L.wt[WT_SHARED_GATE_W];
     if (rc == KQ_OK)
@@ -312,8 +408,8 @@ int run_block(FwdEngine* e, int layer, const void* in, void* out, bool normed) {
         fprintf(stderr, "[kandiga] ERROR: layer %d has no %s weights\n", layer, miss);
         return -1;
     }
-    if (!ensure_ws(e)) {
-        fprintf(stderr, "[kandiga] ERROR: device allocation failed\n");
+    if (!ensure_ws(e) || finalize_layer(e, layer) != 0) {
+        fprintf(stderr, "[kandiga] ERROR: device allocation or setup failed (layer %d)\n", layer);
         return -1;
     }
     const int H = e->info.hidden;
@@ -375,7 +471,8 @@ extern "C" void* bakan_forward_init(const char* packed_expert_dir, int num_layer
         delete e;
         return nullptr;
     }
-    if (load_bkex_dir(packed_expert_dir, num_layers, e->stream, &e->routed, &e->info) || !alloc_all(e)) {
+    // one slot per layer past the routed experts: the shared expert, when its shape matches theirs
+    if (load_bkex_dir(packed_expert_dir, num_layers, e->stream, &e->routed, &e->info, 1) || !alloc_all(e)) {
         if (e->routed) fprintf(stderr, "[kandiga] ERROR: device allocation failed\n");
         bakan_forward_destroy(e);
         return nullptr;
@@ -425,6 +522,7 @@ extern "C" int bakan_forward_set_weight(void* engine, int layer_idx, int weight_
     t.rows = rows;
     t.cols = cols;
     t.dtype = dtype;
+    e->layers[layer_idx].dirty = true;
     if (weight_type >= WT_ROUTER_WEIGHT && weight_type <= WT_ROUTER_BIASES) return build_router(e, layer_idx);
     if (weight_type >= WT_SHARED_UP_W) return build_shared(e, layer_idx);
     return 0;
@@ -462,7 +560,7 @@ int moe_block_prepare(void* engine, int layer) {
         fprintf(stderr, "[kandiga] ERROR: layer %d has no %s weights\n", layer, miss);
         return -1;
     }
-    return ensure_ws(e) ? 0 : -1;
+    return ensure_ws(e) && finalize_layer(e, layer) == 0 ? 0 : -1;
 }
 
 int moe_block_enqueue(void* engine, int layer, const __half* in, __half* out, cudaStream_t s) {
@@ -486,6 +584,8 @@ extern "C" void bakan_forward_destroy(void* engine) {
         for (DevTensor& t : L.wt)
             if (t.p) cudaFree(t.p);
         if (L.router) kq_qmat_destroy(L.router);
+        if (L.router_ext) kq_qmat_destroy(L.router_ext);
+        if (L.norm16) cudaFree(L.norm16);
     }
     kq_table_destroy(e->routed);
     kq_table_destroy(e->shared);

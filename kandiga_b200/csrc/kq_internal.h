@@ -38,9 +38,16 @@ struct BkexInfo {
 };
 int bkex_parse(const uint8_t* hdr, size_t n, BkexInfo* info);
 
-// Read packed_dir/layer_XX.bin for XX < num_layers into a new HBM table on
-// stream s.  0 on success; -1 after a "[kandiga] ERROR: ..." line on stderr,
-// with nothing left allocated.
+// kq_moe_decode with an optional RMSNorm of x (norm_w fp16 [hidden], x fp16)
+// applied in the gate/up input staging.
+int moe_decode_ex(const kq_table* t, int layer, const void* x, int x_dtype, int T, const float* logits,
+                  int32_t* idx, float* weights, int K, void* out_per_k, void* out, int out_dtype,
+                  const void* residual, const void* norm_w, float eps, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+// One token: idx/w [K + 1] = top-K of logits[0, E), then (shared_id, sigmoid(logits[E])).
+int route_with_shared(const float* logits, int E, int K, int shared_id, int32_t* idx, float* w, cudaStream_t s);
+
 // kq_dense_gemv with a residual added in the epilogue: y = residual + W x
 // (residual in y_dtype, may alias y; not for gate/up pairs).
 int dense_gemv_res(const kq_qmat* m, const void* x, int x_dtype, int T, const void* norm_w, float eps,
@@ -62,7 +69,12 @@ uint32_t* moe_block_status(void* engine);
 // it under one another.
 cudaError_t raise_smem_limit(const void* kernel, size_t bytes);
 
-int load_bkex_dir(const char* packed_dir, int num_layers, cudaStream_t s, kq_table** out, BkexInfo* info);
+// Read packed_dir/layer_XX.bin for XX < num_layers into a new HBM table on
+// stream s, with extra_experts more (empty) expert slots per layer after the
+// file's.  0 on success; -1 after a "[kandiga] ERROR: ..." line on stderr,
+// with nothing left allocated.
+int load_bkex_dir(const char* packed_dir, int num_layers, cudaStream_t s, kq_table** out, BkexInfo* info,
+                  int extra_experts = 0);
 
 // Workspace carve-up for kq_moe_* (offsets in bytes, 256-aligned).
 struct MoeWs {

@@ -640,6 +640,44 @@ static cudaError_t launch_router(const float* logits, int T, int E, int K, int32
     return cudaLaunchKernelEx(&cfg, router_topk_kernel, logits, T, E, K, idx, w);
 }
 
+// One token's routing plus a fixed shared expert: top-K of logits[0, E)
+// (softmax, strict '>', lowest index on ties, renormalised), then assignment K
+// = (shared_id, sigmoid(logits[E])) -- the shared expert's gate logit computed
+// by the same GEMV as the router (moe_block.metal:335-404, 515-584).
+__global__ void route_shared_kernel(const float* __restrict__ logits, int E, int K, int shared_id,
+                                    int32_t* __restrict__ idx, float* __restrict__ wout) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    int i;
+    float w;
+    warp_topk_any(logits, E, K, i, w);
+    if (lane < K) {
+        idx[lane] = i;
+        wout[lane] = w;
+    }
+    if (lane == 0) {
+        idx[K] = shared_id;
+        wout[K] = 1.f / (1.f + expf(-__ldcg(logits + E)));
+    }
+}
+
+int route_with_shared(const float* logits, int E, int K, int shared_id, int32_t* idx, float* w,
+                      cudaStream_t s) {
+    if (E > 1024 || K + 1 > MAX_K || K > 32) return KQ_ERR_UNSUPPORTED;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, route_shared_kernel, logits, E, K, shared_id, idx, w) == cudaSuccess ? KQ_OK
+                                                                                                       : KQ_ERR_CUDA;
+}
+
 int launch_router_ext(const float* logits, int T, int E, int K, int32_t* idx, float* w, cudaStream_t s) {
     if (E > 1024 || K > MAX_K) return KQ_ERR_UNSUPPORTED;
     return launch_router(logits, T, E, K, idx, w, s) == cudaSuccess ? KQ_OK : KQ_ERR_CUDA;
@@ -702,7 +740,16 @@ extern "C" int kq_moe_decode(const kq_table* t, int layer, const void* x, int x_
                              const float* logits, int32_t* idx, float* weights, int K,
                              void* out_per_k, void* out, int out_dtype, const void* residual,
                              void* workspace, size_t workspace_bytes, void* stream) {
+    return kq::moe_decode_ex(t, layer, x, x_dtype, T, logits, idx, weights, K, out_per_k, out, out_dtype, residual,
+                             nullptr, 0.f, workspace, workspace_bytes, stream);
+}
+
+int kq::moe_decode_ex(const kq_table* t, int layer, const void* x, int x_dtype, int T, const float* logits,
+                      int32_t* idx, float* weights, int K, void* out_per_k, void* out, int out_dtype,
+                      const void* residual, const void* norm_w, float eps, void* workspace, size_t workspace_bytes,
+                      void* stream) {
     if (!t) return KQ_ERR_ARG;
+    if (norm_w && x_dtype != KQ_DT_F16) return KQ_ERR_ARG;
     if (layer < 0 || layer >= t->d.num_layers) return KQ_ERR_ARG;
     if (T < 0 || K <= 0 || K > MAX_K || K > t->d.num_experts) return KQ_ERR_ARG;
     if (T == 0) return KQ_OK;
@@ -740,6 +787,8 @@ extern "C" int kq_moe_decode(const kq_table* t, int layer, const void* x, int x_
     p.act_kind = t->d.activation;
     p.x = x;
     p.x_dtype = x_dtype;
+    p.norm_w = norm_w;  // RMSNorm of x in the gate/up staging (the down pass reads the activations)
+    p.eps = eps;
     // gate/up + SwiGLU
     p.mode = MODE_GATEUP;
     p.mat_off = 0;

@@ -463,7 +463,7 @@ extern "C" int kq_table_load_bkex(kq_table* t, int layer, const void* file_bytes
     int rc = bkex_parse(static_cast<const uint8_t*>(file_bytes), nbytes, &info);
     if (rc) return rc;
     if (info.hidden != t->d.hidden || info.inter != t->d.inter || info.bits != t->d.bits ||
-        info.num_experts != t->d.num_experts || info.sb_dtype != t->d.sb_dtype)
+        info.num_experts > t->d.num_experts || info.sb_dtype != t->d.sb_dtype)  // experts [0, file's) are filled
         return KQ_ERR_FORMAT;
     if (nbytes < 4096 + (size_t)info.num_experts * info.expert_size) return KQ_ERR_FORMAT;
     cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -16,8 +16,13 @@ H, I, E, IS = 1024, 512, 32, 512
 RTOL_L2 = 2e-3
 
 
-@pytest.fixture(scope="module")
-def block(tmp_path_factory, gpu):
+@pytest.fixture(scope="module", params=["separate", "merged"])
+def block(tmp_path_factory, gpu, request):
+    """'separate': a 4-bit shared expert next to 3-bit routed experts (its own
+    table, the separate gate kernel and combine); 'merged': a shared expert of
+    the routed experts' shape, served as expert E of the routed table with the
+    gate row inside the router GEMV (4 launches per block)."""
+    shared_bits = 4 if request.param == "separate" else 3
     d = tmp_path_factory.mktemp("fwd")
     layers = [O.ExpertLayer.random(3, H, I, E, seed=60 + l, sb_dtype="bf16") for l in range(2)]
     write_bkex(str(d), layers)
@@ -28,7 +33,7 @@ def block(tmp_path_factory, gpu):
             norm=O.f32_to_bf16_bits((1.0 + 0.1 * rng.randn(H)).astype(np.float32)),
             router=O.quantize_affine((rng.randn(E, H) * 0.02).astype(np.float32), 4, 64, "bf16"),
             sgate=O.quantize_affine((rng.randn(1, H) * 0.02).astype(np.float32), 4, 64, "bf16"),
-            shared=O.ExpertLayer.random(4, H, IS, 1, seed=80 + l, sb_dtype="bf16")))
+            shared=O.ExpertLayer.random(shared_bits, H, IS, 1, seed=80 + l, sb_dtype="bf16")))
     return str(d), layers, per
 
 
@@ -60,7 +65,7 @@ def oracle_block(layer, p, h, normed_input, K=8, eps=1e-6):
     idx, w = O.router_topk(logits[None], K)
     y = layer.moe(xf[None], idx)
     gpk, gs, gb = p["sgate"]
-    gate = O.shared_gate(xf[None], gpk, gs, gb, 4, "bf16")
+    gate = O.shared_gate(xf[None], gpk, gs, gb, 4, "bf16")  # router and gate rows: 4-bit
     shared = p["shared"].moe(xf[None], np.zeros((1, 1), np.int32))[0, 0].astype(np.float16).astype(np.float32)
     res = None if normed_input else h.astype(np.float32)[None]
     return logits, O.combine(y, w, res, shared[None], gate)[0]

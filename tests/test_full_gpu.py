@@ -141,17 +141,19 @@ HYBRID = dict(hidden_size=256, num_hidden_layers=4, num_attention_heads=4, num_k
               moe_intermediate_size=256, shared_expert_intermediate_size=256)
 
 
-@pytest.fixture(scope="module")
-def hybrid(tmp_path_factory, gpu):
+@pytest.fixture(scope="module", params=[3, 4])
+def hybrid(tmp_path_factory, gpu, request):
     """the hybrid shape in miniature: 3 GatedDeltaNet layers and 1 attention
     layer (with output gate), MoE blocks with a shared expert; BKEX expert
-    files and config.json in a directory, as bakan_full_init reads them"""
+    files and config.json in a directory, as bakan_full_init reads them.
+    Routed experts 3-bit: the 4-bit shared expert keeps its own table; 4-bit:
+    it joins the routed table (the merged MoE block)."""
     import json
     from oracle.full_step import random_moe
     from tests.test_bakan_gpu import write_bkex
     d = tmp_path_factory.mktemp("hybrid")
     W = random_model(HYBRID, bits=4, seed=21, gate=True)
-    moe, WM = random_moe(HYBRID, seed=21)
+    moe, WM = random_moe(HYBRID, seed=21, expert_bits=request.param)
     write_bkex(str(d), [m["experts"] for m in moe])
     (d / "config.json").write_text(json.dumps(HYBRID))
     return str(d), W, moe, WM
