@@ -20,8 +20,8 @@
 //   kq_dense_gemv        o_proj with the residual added in its epilogue
 // Per GatedDeltaNet layer (full_forward_lg.m:1361-1508): kq_dense_gemv (input
 // RMSNorm + q|k|v|z|b|a), gdn_conv_kernel (ring buffer + conv1d + SiLU),
-// gdn_state_kernel (q/k norm and scale, gated delta rule on the fp32 state),
-// gdn_norm_kernel (RMSNormGated), kq_dense_gemv (out_proj + residual).
+// gdn_state_kernel (q/k norm and scale, gated delta rule on the fp32 state,
+// RMSNormGated of the head), kq_dense_gemv (out_proj + residual).
 // MLP: the MoE block engine of kq_forward.cu (routed experts from the BKEX
 // files, shared expert, gate, blend) or a dense MLP: RMSNorm + gate/up pair
 // with SwiGLU in one pass, then down with the residual.  Rounding points follow the reference's kernels: every buffer
@@ -480,20 +480,27 @@ __global__ void gdn_conv_kernel(const __half* __restrict__ proj, __half* __restr
     out[ch] = __float2half(acc / (1.f + expf(-acc)));
 }
 
-// One CTA per (value head hv, 32 value rows): q and k of key head hv / (nv / nk)
+// One CTA per value head hv (8 warps): q and k of key head hv / (nv / nk)
 // normalised and scaled in shared memory, the decay g = exp(-exp(A_log) *
-// softplus(a + dt_bias)) and beta = sigmoid(b); then per value row dv (a warp,
-// lane l owning key dims [l*KPL, l*KPL + KPL)): S *= g; delta = (v - S.k) * beta;
-// S += delta k; o = S.q (attention.metal:1108-1178, state fp32 [nv][vd][kd]).
+// softplus(a + dt_bias)) and beta = sigmoid(b); then per value row dv (lane l
+// owning key dims [l*KPL, l*KPL + KPL), 64 / KPL rows in flight per warp): S *= g;
+// delta = (v - S.k) * beta; S += delta k; o = S.q (attention.metal:1108-1178,
+// state fp32 [nv][vd][kd]).  The head's o rows, rounded to fp16, then go
+// through RMSNormGated in the same CTA: half(silu(z) * (o * rsqrt(mean(o^2) +
+// eps) * w)) (rmsnorm_gated_kernel, attention.metal:1197-1260).
 template <int KPL>
 __global__ void __launch_bounds__(256) gdn_state_kernel(const __half* __restrict__ conv, const __half* __restrict__ proj,
                                                         const float* __restrict__ a_log,
-                                                        const float* __restrict__ dt_bias, float* __restrict__ state,
+                                                        const float* __restrict__ dt_bias,
+                                                        const float* __restrict__ gnorm, float* __restrict__ state,
                                                         int nk, int nv, int vd, int conv_dim, int vtot, float eps,
-                                                        __half* __restrict__ o) {
+                                                        __half* __restrict__ out) {
     constexpr int KD = 32 * KPL;
+    constexpr int RB = 64 / KPL;  // rows in flight per warp (16 at kd 128: a warp's rows in one batch)
+    extern __shared__ float so[];  // [vd] o rows of this head
     __shared__ float sq[KD], sk[KD];
     __shared__ float s_g, s_beta;
+    __shared__ float red[32];
     pdl_wait();
     pdl_launch_dependents();
     const int hv = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -529,49 +536,61 @@ __global__ void __launch_bounds__(256) gdn_state_kernel(const __half* __restrict
         qf[j] = sq[lane * KPL + j];
     }
     const __half* vsrc = conv + (size_t)2 * nk * KD + (size_t)hv * vd;
-    for (int r = warp; r < 32; r += 8) {
-        const int dv = blockIdx.y * 32 + r;
-        if (dv >= vd) break;
-        float* srow = state + ((size_t)hv * vd + dv) * KD + lane * KPL;
-        float sv[KPL];
+    for (int r0 = warp * RB; r0 < vd; r0 += 8 * RB) {
+        float sv[RB][KPL], kv[RB];
 #pragma unroll
-        for (int j = 0; j < KPL; ++j) sv[j] = srow[j];
-        float kv = 0.f;
+        for (int b = 0; b < RB; ++b) {
+            const int dv = r0 + b;
+            const float* srow = state + ((size_t)hv * vd + (dv < vd ? dv : 0)) * KD + lane * KPL;
 #pragma unroll
-        for (int j = 0; j < KPL; ++j) {
-            sv[j] *= g;
-            kv = fmaf(sv[j], kf[j], kv);
+            for (int j = 0; j < KPL; ++j) sv[b][j] = dv < vd ? srow[j] : 0.f;
         }
-        kv = warp_sum(kv);
-        const float delta = (__half2float(vsrc[dv]) - kv) * beta;
-        float ov = 0.f;
 #pragma unroll
-        for (int j = 0; j < KPL; ++j) {
-            sv[j] = fmaf(delta, kf[j], sv[j]);
-            ov = fmaf(sv[j], qf[j], ov);
-            srow[j] = sv[j];
+        for (int b = 0; b < RB; ++b) {
+            kv[b] = 0.f;
+#pragma unroll
+            for (int j = 0; j < KPL; ++j) {
+                sv[b][j] *= g;
+                kv[b] = fmaf(sv[b][j], kf[j], kv[b]);
+            }
         }
-        ov = warp_sum(ov);
-        if (lane == 0) o[(size_t)hv * vd + dv] = __float2half(ov);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int b = 0; b < RB; ++b) kv[b] += __shfl_xor_sync(0xffffffffu, kv[b], o);
+        float ov[RB];
+#pragma unroll
+        for (int b = 0; b < RB; ++b) {
+            const int dv = r0 + b;
+            const float delta = ((dv < vd ? __half2float(vsrc[dv]) : 0.f) - kv[b]) * beta;
+            ov[b] = 0.f;
+#pragma unroll
+            for (int j = 0; j < KPL; ++j) {
+                sv[b][j] = fmaf(delta, kf[j], sv[b][j]);
+                ov[b] = fmaf(sv[b][j], qf[j], ov[b]);
+            }
+            if (dv < vd) {
+                float* srow = state + ((size_t)hv * vd + dv) * KD + lane * KPL;
+#pragma unroll
+                for (int j = 0; j < KPL; ++j) srow[j] = sv[b][j];
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int b = 0; b < RB; ++b) ov[b] += __shfl_xor_sync(0xffffffffu, ov[b], o);
+        if (lane == 0)
+#pragma unroll
+            for (int b = 0; b < RB; ++b)
+                if (r0 + b < vd) so[r0 + b] = __half2float(__float2half(ov[b]));
     }
-}
-
-// RMSNormGated per value head: half(silu(z) * (o * rsqrt(mean(o^2) + eps) * w))
-// (rmsnorm_gated_kernel, attention.metal:1197-1260).
-__global__ void gdn_norm_kernel(const __half* __restrict__ o, const __half* __restrict__ proj,
-                                const float* __restrict__ w, int vd, int conv_dim, float eps, __half* __restrict__ out) {
-    __shared__ float red[32];
-    pdl_wait();
-    pdl_launch_dependents();
-    const int hv = blockIdx.x;
+    __syncthreads();
+    // RMSNormGated over the head's vd outputs
     float ss = 0.f;
-    for (int d = threadIdx.x; d < vd; d += blockDim.x) {
-        const float v = __half2float(o[(size_t)hv * vd + d]);
-        ss += v * v;
-    }
+    for (int d = threadIdx.x; d < vd; d += blockDim.x) ss += so[d] * so[d];
     const float sc = 1.f / sqrtf(block_sum(ss, red) / (float)vd + eps);
     for (int d = threadIdx.x; d < vd; d += blockDim.x) {
-        const float normed = __half2float(o[(size_t)hv * vd + d]) * sc * w[d];
+        const float normed = so[d] * sc * gnorm[d];
         const float z = __half2float(proj[conv_dim + (size_t)hv * vd + d]);
         out[(size_t)hv * vd + d] = __float2half((z / (1.f + expf(-z))) * normed);
     }
@@ -649,7 +668,7 @@ struct Engine {
     int nchunk = 0;
     int position = 0;
     // GatedDeltaNet activations
-    __half *lproj = nullptr, *lconv = nullptr, *lo = nullptr, *lnorm = nullptr;
+    __half *lproj = nullptr, *lconv = nullptr, *lnorm = nullptr;
     // MoE MLP: the MoE block engine over the BKEX files, hidden state ping-pong
     void* moe = nullptr;
     __half* h2 = nullptr;
@@ -972,10 +991,10 @@ static bool gqa_supported(const Cfg& c) {
 template <int KPL>
 static cudaError_t launch_gdn_state(Engine* e, const Layer& ly) {
     const Cfg& c = e->c;
-    return pdl_launch(gdn_state_kernel<KPL>, dim3(c.lnv, (c.lvd + 31) / 32), dim3(256), 0, e->s,
+    return pdl_launch(gdn_state_kernel<KPL>, dim3(c.lnv), dim3(256), (size_t)c.lvd * sizeof(float), e->s,
                       (const __half*)e->lconv, (const __half*)e->lproj, (const float*)ly.a_log,
-                      (const float*)ly.dt_bias, ly.state, c.lnk, c.lnv, c.lvd, c.conv_dim(), c.lnv * c.lvd, c.eps,
-                      e->lo);
+                      (const float*)ly.dt_bias, (const float*)ly.gnorm, ly.state, c.lnk, c.lnv, c.lvd, c.conv_dim(),
+                      c.lnv * c.lvd, c.eps, e->lnorm);
 }
 
 // GatedDeltaNet token mixer of one layer on the hidden state `x` (in place).
@@ -991,9 +1010,6 @@ static int enqueue_linear(Engine* e, const Layer& ly, __half* x) {
                      : c.lkd == 128 ? launch_gdn_state<4>(e, ly)
                                     : launch_gdn_state<8>(e, ly);
     if (ce != cudaSuccess) return KQ_ERR_CUDA;
-    if (pdl_launch(gdn_norm_kernel, dim3(c.lnv), dim3(128), 0, e->s, (const __half*)e->lo, (const __half*)e->lproj,
-                   (const float*)ly.gnorm, c.lvd, cdim, c.eps, e->lnorm) != cudaSuccess)
-        return KQ_ERR_CUDA;
     return dense_gemv_res(ly.o, e->lnorm, KQ_DT_F16, 1, nullptr, c.eps, KQ_ACT_SILU, x, KQ_DT_F16, x, e->s);
 }
 
@@ -1187,7 +1203,6 @@ static int build(Engine* e) {
     e->h2 = dalloc<__half>(e, c.hidden);
     e->lproj = dalloc<__half>(e, (size_t)c.lin_proj_rows() + 1);
     e->lconv = dalloc<__half>(e, (size_t)cdim + 1);
-    e->lo = dalloc<__half>(e, (size_t)vtot + 1);
     e->lnorm = dalloc<__half>(e, (size_t)vtot + 1);
     e->logits = dalloc<float>(e, c.vocab);
     e->pm = dalloc<float>(e, (size_t)c.nq * e->nchunk);
@@ -1196,7 +1211,7 @@ static int build(Engine* e) {
     e->dev_i = dalloc<int>(e, 4);
     e->status = dalloc<uint32_t>(e, 1);
     if (!e->h || !e->qkv || !e->rope || !e->attn || !e->act || !e->logits || !e->pm || !e->pl || !e->pacc ||
-        !e->dev_i || !e->status || !e->h2 || !e->lproj || !e->lconv || !e->lo || !e->lnorm) {
+        !e->dev_i || !e->status || !e->h2 || !e->lproj || !e->lconv || !e->lnorm) {
         err("buffer allocation failed");
         return -1;
     }
