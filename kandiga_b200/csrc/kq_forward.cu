@@ -343,15 +343,16 @@ int enqueue_block_io(FwdEngine* e, int layer, bool normed, const __half* in, __h
     const FwdLayer& L = e->layers[layer];
     const int H = e->info.hidden;
     if (L.merged && L.router_ext && (normed || L.norm16)) {
-        // router + shared gate in one GEMV (RMSNorm prologue), then K + 1 experts -- top-K and
-        // (shared, sigmoid(gate)) chosen inline -- whose down pass blends them into the residual
+        // router + shared gate in one GEMV (RMSNorm prologue), top-K + (shared, sigmoid(gate)),
+        // then K + 1 experts whose down pass blends them into the residual
         const int E = e->info.num_experts;
         const __half* nw = normed ? nullptr : L.norm16;
         int rc = dense_gemv_res(L.router_ext, in, KQ_DT_F16, 1, nw, e->eps, KQ_ACT_SILU, e->dlogits, KQ_DT_F32,
                                 nullptr, s);
-        if (rc == KQ_OK)  // routing (top-K + the shared expert) inline in both expert kernels
-            rc = moe_decode_ex(e->routed, layer, in, KQ_DT_F16, 1, e->dlogits, e->didx, e->dw, e->top_k + 1, nullptr,
-                               out, KQ_DT_F16, normed ? nullptr : in, nw, e->eps, e->ws, e->ws_bytes, s, E, E);
+        if (rc == KQ_OK) rc = route_with_shared(e->dlogits, E, e->top_k, E, e->didx, e->dw, s);
+        if (rc == KQ_OK)
+            rc = moe_decode_ex(e->routed, layer, in, KQ_DT_F16, 1, nullptr, e->didx, e->dw, e->top_k + 1, nullptr, out,
+                               KQ_DT_F16, normed ? nullptr : in, nw, e->eps, e->ws, e->ws_bytes, s);
         return rc;
     }
     const __half* x = in;

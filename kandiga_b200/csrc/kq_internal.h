@@ -39,14 +39,14 @@ struct BkexInfo {
 int bkex_parse(const uint8_t* hdr, size_t n, BkexInfo* info);
 
 // kq_moe_decode with an optional RMSNorm of x (norm_w fp16 [hidden], x fp16)
-// applied in the gate/up input staging.  route_E (-1: all of the table's
-// experts): logits [0, route_E) are routed; shared_id >= 0 (inline routing
-// only): assignment K-1 is that expert with weight sigmoid(logits[route_E]),
-// logit rows padded to a multiple of 16.
+// applied in the gate/up input staging.
 int moe_decode_ex(const kq_table* t, int layer, const void* x, int x_dtype, int T, const float* logits,
                   int32_t* idx, float* weights, int K, void* out_per_k, void* out, int out_dtype,
                   const void* residual, const void* norm_w, float eps, void* workspace, size_t workspace_bytes,
-                  void* stream, int route_E = -1, int shared_id = -1);
+                  void* stream);
+
+// One token: idx/w [K + 1] = top-K of logits[0, E), then (shared_id, sigmoid(logits[E])).
+int route_with_shared(const float* logits, int E, int K, int shared_id, int32_t* idx, float* w, cudaStream_t s);
 
 // kq_dense_gemv with a residual added in the epilogue: y = residual + W x
 // (residual in y_dtype, may alias y; not for gate/up pairs).

@@ -48,10 +48,7 @@ struct GemvParams {
     int x_dtype;
     const void* norm_w;
     float eps;
-    const float* logits;  // [T][logit_stride] when routing runs in the prologues, else null
-    int route_E;          // logits [0, route_E) are routed experts (route_E <= E)
-    int logit_stride;
-    int shared_id;        // >= 0: assignment K-1 is this expert, weight sigmoid(logits[route_E])
+    const float* logits;  // [T][E] when routing runs in the prologues, else null
     int32_t* idx;         // [T*K]
     float* w;             // [T*K]
     float* act;           // [T*K][I]
@@ -129,18 +126,6 @@ __device__ __forceinline__ void warp_topk(const float* __restrict__ l, int E, in
     const float esum = warp_sum(ev);
     out_idx = my_i;
     out_w = (lane < K && esum > 0.f) ? ev / esum : 0.f;
-}
-
-// Inline routing of token t in the decode kernels: top-(K or K-1) of the routed
-// logits, and with a shared expert, lane K-1 takes (shared_id, sigmoid(gate logit)).
-__device__ __forceinline__ void route_inline(const GemvParams& p, int t, int& ix, float& wt) {
-    const float* l = p.logits + (size_t)t * p.logit_stride;
-    const int kr = p.shared_id >= 0 ? p.K - 1 : p.K;
-    warp_topk<8>(l, p.route_E, kr, ix, wt);
-    if (p.shared_id >= 0 && (threadIdx.x & 31) == kr) {
-        ix = p.shared_id;
-        wt = 1.f / (1.f + expf(-__ldcg(l + p.route_E)));
-    }
 }
 
 __device__ __forceinline__ void warp_topk_any(const float* l, int E, int K, int& i, float& w) {
@@ -334,7 +319,7 @@ __global__ void __launch_bounds__(NW * 32) qunit_kernel(const GemvParams p) {
             if (p.logits) {
                 int ix;
                 float wt;
-                route_inline(p, t, ix, wt);
+                warp_topk<8>(p.logits + (size_t)t * p.E, p.E, p.K, ix, wt);
                 if (rt == 0 && k == 0 && lane < p.K) {  // one CTA per token publishes the routing
                     p.idx[(size_t)t * p.K + lane] = ix;
                     p.w[(size_t)t * p.K + lane] = wt;
@@ -463,7 +448,7 @@ __global__ void __launch_bounds__(DOWN_NW * 32, 1) moe_down_kernel(const GemvPar
         if (warp == 0) {
             int ix;
             float wt;
-            route_inline(p, t, ix, wt);
+            warp_topk<8>(p.logits + (size_t)t * p.E, p.E, p.K, ix, wt);
             if (lane < p.K) {
                 s_idx[lane] = ix;
                 s_w[lane] = wt;
@@ -655,6 +640,44 @@ static cudaError_t launch_router(const float* logits, int T, int E, int K, int32
     return cudaLaunchKernelEx(&cfg, router_topk_kernel, logits, T, E, K, idx, w);
 }
 
+// One token's routing plus a fixed shared expert: top-K of logits[0, E)
+// (softmax, strict '>', lowest index on ties, renormalised), then assignment K
+// = (shared_id, sigmoid(logits[E])) -- the shared expert's gate logit computed
+// by the same GEMV as the router (moe_block.metal:335-404, 515-584).
+__global__ void route_shared_kernel(const float* __restrict__ logits, int E, int K, int shared_id,
+                                    int32_t* __restrict__ idx, float* __restrict__ wout) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    int i;
+    float w;
+    warp_topk_any(logits, E, K, i, w);
+    if (lane < K) {
+        idx[lane] = i;
+        wout[lane] = w;
+    }
+    if (lane == 0) {
+        idx[K] = shared_id;
+        wout[K] = 1.f / (1.f + expf(-__ldcg(logits + E)));
+    }
+}
+
+int route_with_shared(const float* logits, int E, int K, int shared_id, int32_t* idx, float* w,
+                      cudaStream_t s) {
+    if (E > 1024 || K + 1 > MAX_K || K > 32) return KQ_ERR_UNSUPPORTED;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, route_shared_kernel, logits, E, K, shared_id, idx, w) == cudaSuccess ? KQ_OK
+                                                                                                       : KQ_ERR_CUDA;
+}
+
 int launch_router_ext(const float* logits, int T, int E, int K, int32_t* idx, float* w, cudaStream_t s) {
     if (E > 1024 || K > MAX_K) return KQ_ERR_UNSUPPORTED;
     return launch_router(logits, T, E, K, idx, w, s) == cudaSuccess ? KQ_OK : KQ_ERR_CUDA;
@@ -718,17 +741,14 @@ extern "C" int kq_moe_decode(const kq_table* t, int layer, const void* x, int x_
                              void* out_per_k, void* out, int out_dtype, const void* residual,
                              void* workspace, size_t workspace_bytes, void* stream) {
     return kq::moe_decode_ex(t, layer, x, x_dtype, T, logits, idx, weights, K, out_per_k, out, out_dtype, residual,
-                             nullptr, 0.f, workspace, workspace_bytes, stream, -1, -1);
+                             nullptr, 0.f, workspace, workspace_bytes, stream);
 }
 
 int kq::moe_decode_ex(const kq_table* t, int layer, const void* x, int x_dtype, int T, const float* logits,
                       int32_t* idx, float* weights, int K, void* out_per_k, void* out, int out_dtype,
                       const void* residual, const void* norm_w, float eps, void* workspace, size_t workspace_bytes,
-                      void* stream, int route_E, int shared_id) {
+                      void* stream) {
     if (!t) return KQ_ERR_ARG;
-    if (route_E < 0) route_E = t->d.num_experts;
-    if (route_E > t->d.num_experts || shared_id >= t->d.num_experts || (shared_id >= 0 && (!logits || K < 2)))
-        return KQ_ERR_ARG;
     if (norm_w && x_dtype != KQ_DT_F16) return KQ_ERR_ARG;
     if (layer < 0 || layer >= t->d.num_layers) return KQ_ERR_ARG;
     if (T < 0 || K <= 0 || K > MAX_K || K > t->d.num_experts) return KQ_ERR_ARG;
@@ -746,13 +766,9 @@ int kq::moe_decode_ex(const kq_table* t, int layer, const void* x, int x_dtype, 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     int32_t* idx_use = idx ? idx : reinterpret_cast<int32_t*>(ws + L.idx);
     float* w_use = weights ? weights : reinterpret_cast<float*>(ws + L.w);
-    // a shared expert rides on the inline routing only; its gate logit follows the
-    // routed logits in a row padded to a multiple of 16
-    const int stride = shared_id >= 0 ? (route_E + 1 + 15) / 16 * 16 : route_E;
-    const bool inline_route = logits && T <= ROUTE_INLINE_MAX_T && route_E <= 256;
-    if (shared_id >= 0 && !inline_route) return KQ_ERR_UNSUPPORTED;
+    const bool inline_route = logits && T <= ROUTE_INLINE_MAX_T && t->d.num_experts <= 256;
     if (logits && !inline_route) {
-        if (launch_router(logits, T, route_E, K, idx_use, w_use, s) != cudaSuccess) return KQ_ERR_CUDA;
+        if (launch_router(logits, T, t->d.num_experts, K, idx_use, w_use, s) != cudaSuccess) return KQ_ERR_CUDA;
     }
     GemvParams p{};
     p.base = t->base + (size_t)layer * t->layer_bytes;
@@ -761,9 +777,6 @@ int kq::moe_decode_ex(const kq_table* t, int layer, const void* x, int x_dtype, 
     p.T = T;
     p.K = K;
     p.logits = inline_route ? logits : nullptr;
-    p.route_E = route_E;
-    p.logit_stride = stride;
-    p.shared_id = shared_id;
     p.idx = idx_use;
     p.w = w_use;
     p.act = reinterpret_cast<float*>(ws + L.act);
