@@ -21,7 +21,9 @@ __global__ void __launch_bounds__(GEMM_TC_THREADS) gemm_f16_tc_kernel(const __ha
                                                                       int K, uint32_t ncols,
                                                                       uint32_t* status) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned in the shared window; an offset from smem_raw keeps the
+    // shared address space, so accesses through it compile to shared-memory ops
+    uint8_t* smem = smem_raw + ((1024u - ((uint32_t)__cvta_generic_to_shared(smem_raw) & 1023u)) & 1023u);
     uint8_t* sA = smem;                 // 128 x 128 B
     uint8_t* sB = smem + 128 * 128;     // N x 128 B
     __shared__ uint64_t bar;

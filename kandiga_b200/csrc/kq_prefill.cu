@@ -329,7 +329,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     constexpr int TB = TileT<BITS>::BYTES;
     constexpr int TS = tc_tile_slot<BITS>();
-    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned in the shared window; an offset from smem_raw keeps the
+    // shared address space, so accesses through it compile to shared-memory ops
+    uint8_t* sm = smem_raw + ((1024u - ((uint32_t)__cvta_generic_to_shared(smem_raw) & 1023u)) & 1023u);
     uint8_t* sA = sm;
     uint8_t* sB = sA + TC_NSTAGE * TC_STAGE_BYTES;
     uint8_t* sK = sB + TC_NB * TC_STAGE_BYTES;
