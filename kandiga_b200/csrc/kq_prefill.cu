@@ -444,8 +444,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const int s = kc % TC_NKQ;
                 mbar_wait_sleep(&kq_full[s], (kc / TC_NKQ) & 1, p.status);
                 const uint8_t* tile = sK + ((size_t)s * 8 + jt) * TS;
-                for (int g = 0; g < 8; ++g) {
-                    if ((st * 8 + g) % TC_NMMA != ds) continue;
+                // this set's groups of the super-tile: g = first, first + TC_NMMA, ... (one copy of the body)
+                const int first = (ds - (st * 8) % TC_NMMA + TC_NMMA) % TC_NMMA;
+#pragma unroll 1
+                for (int g = first; g < 8; g += TC_NMMA) {
                     const int gs = ds * TC_SLOTS + (int)(lc % TC_SLOTS);
                     uint32_t out[32];  // computed before the stage is awaited: a stage is held only for its stores
                     dequant_row<BITS, SB_DT>(tile, r16, g, out);
@@ -585,22 +587,35 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // ---- combine ----------------------------------------------------------------------------------
 
 // out[t][h] = [res[t][h]] + sum_k w[t][k] * ys[pos(t,k)][h]; per-k outputs optional.
+// One thread per 4 consecutive h (H % 4 == 0): 16-byte reads of the expert rows.
 __global__ void combine_kernel(const float* __restrict__ ys, const int32_t* __restrict__ inv_pos,
                                const float* __restrict__ w, int T, int K, int H, void* out, void* out_per_k,
                                int out_dtype, const void* residual) {
     const int t = blockIdx.y;
-    const int h = blockIdx.x * blockDim.x + threadIdx.x;
+    const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
     if (t >= T || h >= H) return;
-    float acc = 0.f;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int k = 0; k < K; ++k) {
         const int pos = inv_pos[(size_t)t * K + k];
-        const float y = pos >= 0 ? ys[(size_t)pos * H + h] : 0.f;
-        if (out_per_k) store_from_float(out_per_k, out_dtype, ((size_t)t * K + k) * H + h, y);
-        if (out) acc += y * w[(size_t)t * K + k];
+        const float4 y4 = pos >= 0 ? *reinterpret_cast<const float4*>(ys + (size_t)pos * H + h)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float y[4] = {y4.x, y4.y, y4.z, y4.w};
+        if (out_per_k)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) store_from_float(out_per_k, out_dtype, ((size_t)t * K + k) * H + h + j, y[j]);
+        if (out) {
+            const float wk = w[(size_t)t * K + k];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[j] += y[j] * wk;
+        }
     }
     if (!out) return;
-    if (residual) acc = load_as_float(residual, out_dtype, (size_t)t * H + h) + acc;
-    store_from_float(out, out_dtype, (size_t)t * H + h, acc);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float v = acc[j];
+        if (residual) v = load_as_float(residual, out_dtype, (size_t)t * H + h + j) + v;
+        store_from_float(out, out_dtype, (size_t)t * H + h + j, v);
+    }
 }
 
 // ---- host ---------------------------------------------------------------------------------------
@@ -837,7 +852,7 @@ extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x
     p.n_mt = H / 128;
     if (int rc = gemm(act_s, I)) return rc;
     // combine / per-k outputs
-    dim3 grid((H + 255) / 256, T);
+    dim3 grid((H / 4 + 255) / 256, T);
     combine_kernel<<<grid, 256, 0, s>>>(ys, inv_pos, w_use, T, K, H, out, out_per_k, out_dtype, residual);
     return cudaGetLastError() == cudaSuccess ? KQ_OK : KQ_ERR_CUDA;
 }
