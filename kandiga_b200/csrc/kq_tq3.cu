@@ -15,7 +15,9 @@
 // different blocks hits distinct banks), then one warp per row: lane l takes
 // blocks l, l+32, ...; pairs of indices (6-bit fields) look up a 64-entry
 // table of centroid pairs, so a pair of weights costs one bit-field extract,
-// one shared load and two FMAs.
+// one shared load and two FMAs.  The table is held in 16 interleaved copies,
+// copy c in bank pair c, and lane l reads copy l % 16: a half-warp's 8-byte
+// lookups (one shared-memory wavefront) never conflict, whatever the indices.
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
@@ -27,6 +29,7 @@ namespace kq {
 
 constexpr int TQ3_THREADS = 256;
 constexpr int TQ3_XSTRIDE = 36;  // floats per rotated 32-block in shared memory (16-byte aligned, bank-staggered)
+constexpr int TQ3_LUT_COPIES = 16;  // centroid-pair table copies: one per lane of a half-warp
 
 // kandiga/tq3/quantize.py:29-47 (centroids of the 3-bit Lloyd-Max quantizer; block sign pattern)
 __constant__ float tq3_centroids[8] = {-1.996684f, -1.291398f, -0.740341f, -0.247508f,
@@ -43,9 +46,13 @@ __global__ void __launch_bounds__(TQ3_THREADS) tq3_gemv_kernel(const uint8_t* __
     const int nb = cols / 32;
     float* xr = reinterpret_cast<float*>(tq3_sm);        // [TT][nb][TQ3_XSTRIDE]
     float* hs = xr + (size_t)TT * nb * TQ3_XSTRIDE;       // [TT][2 nb] half-block sums
-    float2* lut = reinterpret_cast<float2*>(hs + (size_t)TT * 2 * nb);  // [64]: (C[lo], C[hi])
+    float2* lut = reinterpret_cast<float2*>(hs + (size_t)TT * 2 * nb);  // [64][16]: (C[lo], C[hi]) per copy
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid < 64) lut[tid] = make_float2(tq3_centroids[tid & 7], tq3_centroids[tid >> 3]);
+    for (int i = tid; i < 64 * TQ3_LUT_COPIES; i += TQ3_THREADS) {
+        const int e = i / TQ3_LUT_COPIES;
+        lut[i] = make_float2(tq3_centroids[e & 7], tq3_centroids[e >> 3]);
+    }
+    const float2* lutl = lut + (lane % TQ3_LUT_COPIES);  // this lane's copy: entry e at lutl[e * 16]
     const float inv = sqrtf(32.f);
     // rotate x: warp per (token, block) of the T real tokens, lane = element;
     // XB blocks' loads in flight per warp (rows of slots t >= T are never stored)
@@ -124,8 +131,8 @@ __global__ void __launch_bounds__(TQ3_THREADS) tq3_gemv_kernel(const uint8_t* __
     #pragma unroll
                         for (int r = 0; r < 8; r += 4) {
                             const float4 xv = *reinterpret_cast<const float4*>(xb + g * 8 + r);
-                            const float2 c0 = lut[(grp[g] >> (3 * r)) & 63u];
-                            const float2 c1 = lut[(grp[g] >> (3 * r + 6)) & 63u];
+                            const float2 c0 = lutl[((grp[g] >> (3 * r)) & 63u) * TQ3_LUT_COPIES];
+                            const float2 c1 = lutl[((grp[g] >> (3 * r + 6)) & 63u) * TQ3_LUT_COPIES];
                             float& a = g < 2 ? a0 : a1;
                             a = fmaf(c0.x, xv.x, a);
                             a = fmaf(c0.y, xv.y, a);
@@ -171,7 +178,7 @@ static cudaError_t launch_tq3(const kq_tq3_mat* m, const void* x, int x_dtype, i
                               int y_dtype, cudaStream_t s) {
     static int configured[64] = {0};
     const int nb = m->cols / 32;
-    const size_t smem = ((size_t)TT * nb * TQ3_XSTRIDE + (size_t)TT * 2 * nb) * 4 + 64 * 8 + 16;
+    const size_t smem = ((size_t)TT * nb * TQ3_XSTRIDE + (size_t)TT * 2 * nb) * 4 + 64 * TQ3_LUT_COPIES * 8 + 16;
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
