@@ -69,6 +69,7 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1)
     __shared__ int off_s[GROUP_MAX_E];
     __shared__ int wsum[2][32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_wait();  // the routing is complete and visible
     for (int e = tid; e < E; e += GROUP_THREADS) cnt[e] = 0;
     __syncthreads();
     for (int a = tid; a < A; a += GROUP_THREADS) {
@@ -151,6 +152,7 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1)
 __global__ void gather_kernel(const void* __restrict__ x, int x_dtype, int H, const int32_t* __restrict__ s_tok,
                               const int* __restrict__ n_pos, __half* __restrict__ Xs, float* __restrict__ xinv) {
     const int pos = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    pdl_wait();  // the grouping is complete and visible
     if (pos >= *n_pos) return;
     const int tok = s_tok[pos];
     if (tok < 0) return;
@@ -377,6 +379,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
+    // The prologue above overlaps the previous kernel's tail.  Global memory
+    // is touched only after the wait; the next kernel may launch at once (it
+    // cannot share an SM with this one's shared memory, and waits in turn).
+    pdl_wait();
+    pdl_launch_dependents();
     const int n_items = *p.n_chunks * p.n_mt;
     const int groups = p.nst * 8;
 
@@ -593,6 +600,7 @@ __global__ void combine_kernel(const float* __restrict__ ys, const int32_t* __re
                                int out_dtype, const void* residual) {
     const int t = blockIdx.y;
     const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    pdl_wait();  // the down projection is complete and visible
     if (t >= T || h >= H) return;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int k = 0; k < K; ++k) {
@@ -708,6 +716,25 @@ static bool make_kq_tmap(CUtensorMap* m, const void* layer, size_t layer_bytes, 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Launch as a programmatic dependent of the previous work on the stream: the
+// kernel is scheduled while its predecessor drains and waits (griddepcontrol)
+// for it to complete before it reads or writes global memory.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_dep(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 template <int BITS, int SB_DT>
 static cudaError_t launch_tc_t(const TcParams& p, const CUtensorMap (&tm)[4], const CUtensorMap& tkq, cudaStream_t s,
                                int grid) {
@@ -722,8 +749,7 @@ static cudaError_t launch_tc_t(const TcParams& p, const CUtensorMap (&tm)[4], co
         if (err != cudaSuccess) return err;
         configured[dev] = (int)smem;
     }
-    kern<<<grid, TC_THREADS, smem, s>>>(p, tm[0], tm[1], tm[2], tm[3], tkq);
-    return cudaGetLastError();
+    return launch_dep(kern, dim3(grid), dim3(TC_THREADS), smem, s, p, tm[0], tm[1], tm[2], tm[3], tkq);
 }
 
 static cudaError_t launch_tc(int bits, int sb, const TcParams& p, const CUtensorMap (&tm)[4], const CUtensorMap& tkq,
@@ -793,10 +819,13 @@ extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x
     if (logits && launch_router_ext(logits, T, E, K, idx_use, w_use, s) != KQ_OK) return KQ_ERR_CUDA;
     {
         const int threads = 256;
-        group_kernel<<<1, GROUP_THREADS, 0, s>>>(idx_use, A, K, E, PF_CHUNK, PF_PAD, count, offset, s_tok, inv_pos,
-                                                 chunk_list, n_chunks, n_pos, status);
-        gather_kernel<<<(P * 32 + threads - 1) / threads, threads, 0, s>>>(x, x_dtype, H, s_tok, n_pos, Xs, xinv);
-        if (cudaError_t e = cudaGetLastError()) return pf_fail("grouping", e);
+        if (cudaError_t e = launch_dep(group_kernel, dim3(1), dim3(GROUP_THREADS), 0, s, (const int32_t*)idx_use, A,
+                                       K, E, PF_CHUNK, PF_PAD, count, offset, s_tok, inv_pos, chunk_list, n_chunks,
+                                       n_pos, status))
+            return pf_fail("grouping", e);
+        if (cudaError_t e = launch_dep(gather_kernel, dim3((P * 32 + threads - 1) / threads), dim3(threads), 0, s, x,
+                                       x_dtype, H, (const int32_t*)s_tok, (const int*)n_pos, Xs, xinv))
+            return pf_fail("gather", e);
     }
     // Rows of Xs / act_s at pad positions or past the placed ones are never
     // written; the epilogues ignore the MMA columns that read them.
@@ -853,6 +882,8 @@ extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x
     if (int rc = gemm(act_s, I)) return rc;
     // combine / per-k outputs
     dim3 grid((H / 4 + 255) / 256, T);
-    combine_kernel<<<grid, 256, 0, s>>>(ys, inv_pos, w_use, T, K, H, out, out_per_k, out_dtype, residual);
-    return cudaGetLastError() == cudaSuccess ? KQ_OK : KQ_ERR_CUDA;
+    return launch_dep(combine_kernel, grid, dim3(256), 0, s, (const float*)ys, (const int32_t*)inv_pos,
+                      (const float*)w_use, T, K, H, out, out_per_k, out_dtype, residual) == cudaSuccess
+               ? KQ_OK
+               : KQ_ERR_CUDA;
 }
