@@ -157,8 +157,22 @@ __global__ void gather_kernel(const void* __restrict__ x, int x_dtype, int H, co
     const int tok = s_tok[pos];
     if (tok < 0) return;
     const size_t src = (size_t)tok * H;
+    if (x_dtype == KQ_DT_F16) {  // a straight copy, four 16-byte loads in flight per lane
+        const uint4* s4 = reinterpret_cast<const uint4*>(static_cast<const __half*>(x) + src);
+        uint4* d4 = reinterpret_cast<uint4*>(Xs + (size_t)pos * H);
+        const int n = H / 8;
+        for (int c = lane; c < n; c += 128) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = c + 32 * u < n ? __ldg(s4 + c + 32 * u) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (c + 32 * u < n) d4[c + 32 * u] = v[u];
+        }
+        return;
+    }
     float scale = 1.f;
-    if (x_dtype != KQ_DT_F16) {
+    {
         float amax = 0.f;
         for (int c = lane; c < H / 8; c += 32) {
             float v[8];
