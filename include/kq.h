@@ -47,6 +47,7 @@ extern "C" {
 #define KQ_DEV_BAD_EXPERT 1u  /* an expert id outside [0, num_experts): output rows zeroed */
 #define KQ_DEV_WAIT_TIMEOUT 2u /* a bounded device-side wait gave up */
 #define KQ_DEV_BAD_INDEX 4u   /* a token/slot index outside its range */
+#define KQ_DEV_RANGE 16u      /* kq_moe_prefill: a dequantised weight |q*s + b| does not fit fp16 */
 
 /* element types */
 #define KQ_DT_F16 0
@@ -304,7 +305,11 @@ int kq_moe_decode_static(const kq_table* t, int layer, const void* x, int x_dtyp
  * accumulators in tensor memory.  replaces _gpu_prefill_experts
  * (kandiga/engine.py:386-516) and bakan_cpu_expert_mlp_prefill_f16
  * (kandiga/metal/kandiga_cpu_expert.m:773-838).  Requires hidden and inter to
- * be multiples of 512 and per-group |scale| < 64. */
+ * be multiples of 512.  Range: each weight is dequantised as W = q*s + b in
+ * fp16 with one rounding (a weight that does not fit fp16 latches
+ * KQ_DEV_RANGE); inputs of any magnitude are scaled by powers of two per
+ * token, and SwiGLU activations by powers of two per (token, expert) where
+ * they reach 2^15, so no fp16 intermediate overflows. */
 size_t kq_moe_prefill_workspace_size(const kq_table* t, int max_tokens, int top_k);
 int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x_dtype, int T,
                    const float* logits, int32_t* idx, float* weights, int K, void* out_per_k,

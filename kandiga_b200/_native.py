@@ -21,7 +21,7 @@ KQ_ERR_CAPACITY = 8
 ERRORS_INV = {v: k for k, v in ERRORS.items()}
 DT_F16, DT_BF16, DT_F32 = 0, 1, 2
 ACT_SILU, ACT_GELU_TANH = 0, 1
-DEV_BAD_EXPERT, DEV_WAIT_TIMEOUT, DEV_BAD_INDEX, DEV_CAPACITY = 1, 2, 4, 8
+DEV_BAD_EXPERT, DEV_WAIT_TIMEOUT, DEV_BAD_INDEX, DEV_CAPACITY, DEV_RANGE = 1, 2, 4, 8, 16
 
 
 class KQError(RuntimeError):

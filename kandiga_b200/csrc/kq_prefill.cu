@@ -64,12 +64,13 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1)
     group_kernel(const int32_t* __restrict__ idx, int A, int K, int E, int chunk, int pad, int* __restrict__ count,
                  int* __restrict__ offset, int32_t* __restrict__ s_tok, int32_t* __restrict__ inv_pos,
                  int4* __restrict__ chunk_list, int* __restrict__ n_chunks, int* __restrict__ n_pos,
-                 uint32_t* status) {
+                 uint32_t* status, uint32_t* act_flag) {
     __shared__ int cnt[GROUP_MAX_E];
     __shared__ int off_s[GROUP_MAX_E];
     __shared__ int wsum[2][32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     pdl_wait();  // the routing is complete and visible
+    if (tid == 0) *act_flag = 0u;
     for (int e = tid; e < E; e += GROUP_THREADS) cnt[e] = 0;
     __syncthreads();
     for (int a = tid; a < A; a += GROUP_THREADS) {
@@ -150,10 +151,12 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1)
 // scale so every value fits fp16, and xinv[pos] = 1/scale.  Pad positions
 // (s_tok < 0) are left unwritten.
 __global__ void gather_kernel(const void* __restrict__ x, int x_dtype, int H, const int32_t* __restrict__ s_tok,
-                              const int* __restrict__ n_pos, __half* __restrict__ Xs, float* __restrict__ xinv) {
+                              const int* __restrict__ n_pos, __half* __restrict__ Xs, float* __restrict__ xinv,
+                              int8_t* __restrict__ act_exp, int n_exp) {
     const int pos = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     pdl_wait();  // the grouping is complete and visible
     if (pos >= *n_pos) return;
+    for (int b = lane; b < n_exp; b += 32) act_exp[(size_t)pos * n_exp + b] = 0;  // see act_fixup_kernel
     const int tok = s_tok[pos];
     if (tok < 0) return;
     const size_t src = (size_t)tok * H;
@@ -217,6 +220,10 @@ struct TcParams {
     const float* xinv;    // [A] input scale inverse (gate/up), or null
     int act_kind;
     uint32_t* status;
+    // fp16 range of the activations (see act_fixup_kernel)
+    uint32_t* act_flag;   // nonzero: some activation row was stored scaled
+    int8_t* act_exp;      // [P][I / 16] exponent a 16-row block of act_s was stored with
+    float* act_inv;       // [P] factor the down projection of a position is multiplied by
 };
 
 constexpr int TC_NMMA = 3;            // MMA-issuing warps = dequantising warp sets (4 warps each)
@@ -263,22 +270,27 @@ __device__ __forceinline__ __half to_half16(uint32_t v16) {
 
 // Dequantise row r16 (0..15) x group g (0..7) of a KQ tile into 64 fp16 weights
 // W = q*s + b, written as one 128-byte row (row m) of a swizzled A stage.
+// A pair extracts as two exact fp16 values 2^(10-k) + q; subtracting the
+// constant 2^(10-k) leaves q exactly, and one HFMA2 forms W = q*s + b with a
+// single rounding.  No intermediate exceeds |W|, so any scale and bias whose
+// weights fit fp16 dequantise without overflow.
 template <int BITS, int SB_DT, int J>
 __device__ __forceinline__ void dq_pairs(const uint32_t* wd, const uint32_t* sh, __half2 s2, __half2 b2,
-                                         __half2 c1024, __half2 c_mid, __half2 c_lo, uint32_t* out) {
+                                         uint32_t* out) {
     if constexpr (J < 32) {
         const uint32_t h = pair_of<BITS, J>(wd, sh);
-        const float off = pair_offset<BITS>(J);
-        const __half2 c = off == 1024.f ? c1024 : (off == 16.f ? c_lo : c_mid);
-        __half2 w2 = __hfma2(*reinterpret_cast<const __half2*>(&h), s2, c);  // (2^(10-k) + q) s - 2^(10-k) s
-        w2 = __hadd2(w2, b2);
+        constexpr float off = pair_offset<BITS>(J);
+        const __half2 q2 = __hsub2(*reinterpret_cast<const __half2*>(&h), __float2half2_rn(off));
+        const __half2 w2 = __hfma2(q2, s2, b2);
         out[J] = *reinterpret_cast<const uint32_t*>(&w2);
-        dq_pairs<BITS, SB_DT, J + 1>(wd, sh, s2, b2, c1024, c_mid, c_lo, out);
+        dq_pairs<BITS, SB_DT, J + 1>(wd, sh, s2, b2, out);
     }
 }
 
+// Returns max(|b|, |qmax*s + b|) in fp16: the largest |W| of the group (inf
+// when a weight or the scale/bias itself does not fit fp16).
 template <int BITS, int SB_DT>
-__device__ __forceinline__ void dequant_row(const uint8_t* tile, int r16, int g, uint32_t (&out)[32]) {
+__device__ __forceinline__ __half dequant_row(const uint8_t* tile, int r16, int g, uint32_t (&out)[32]) {
     constexpr int W = TileT<BITS>::W;  // words per (lane, set); the scale/bias chunk is chunk W
     const int l = 4 * (r16 & 7) + (g & 3);
     const int set = 2 * (r16 >> 3) + (g >> 2);
@@ -297,11 +309,8 @@ __device__ __forceinline__ void dequant_row(const uint8_t* tile, int r16, int g,
         *reinterpret_cast<const uint32_t*>(tile + srow * 128 + (((l2 & 7) ^ (srow & 7)) << 4) + kk * 4);
     const __half s = to_half16<SB_DT>(sbw & 0xFFFFu), b = to_half16<SB_DT>(sbw >> 16);
     const __half2 s2 = __halves2half2(s, s), b2 = __halves2half2(b, b);
-    // -2^(10-k) * s is exact in fp16 (power-of-two multiple) for |s| < 64
-    const __half2 c1024 = __hmul2(s2, __float2half2_rn(-1024.f));
-    const __half2 c_mid = __hmul2(s2, __float2half2_rn(BITS == 3 ? -128.f : -64.f));
-    const __half2 c_lo = __hmul2(s2, __float2half2_rn(-16.f));
-    dq_pairs<BITS, SB_DT, 0>(wd, sh, s2, b2, c1024, c_mid, c_lo, out);
+    dq_pairs<BITS, SB_DT, 0>(wd, sh, s2, b2, out);
+    return __hmax(__habs(b), __habs(__hfma(s, __float2half_rn((float)((1 << BITS) - 1)), b)));
 }
 
 // out[32] as row m (one swizzled 128-byte row) of an A stage
@@ -460,6 +469,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int m = (tid - 64) & 127;  // A row 0..127
         const int jt = m >> 4, r16 = m & 15;
         uint32_t kc = 0, lc = 0;
+        __half wmax = __float2half_rn(0.f);  // largest |W| this thread dequantised
         for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
             for (int st = 0; st < p.nst; ++st, ++kc) {
                 const int s = kc % TC_NKQ;
@@ -471,7 +481,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 for (int g = first; g < 8; g += TC_NMMA) {
                     const int gs = ds * TC_SLOTS + (int)(lc % TC_SLOTS);
                     uint32_t out[32];  // computed before the stage is awaited: a stage is held only for its stores
-                    dequant_row<BITS, SB_DT>(tile, r16, g, out);
+                    wmax = __hmax(wmax, dequant_row<BITS, SB_DT>(tile, r16, g, out));
                     mbar_wait_sleep(&a_empty[gs], ((lc / TC_SLOTS) & 1) ^ 1, p.status);
                     a_row_store(out, sA + (size_t)gs * TC_STAGE_BYTES, m);
                     fence_proxy_async_smem();
@@ -481,6 +491,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 tc::mbar_arrive(&kq_empty[s]);
             }
         }
+        if (!(__half2float(wmax) < 65504.f)) set_status(p.status, KQ_DEV_RANGE);
     } else if (warp < MMA_WARP + TC_NMMA) {
         // ---------------- MMA issue ----------------
         // One thread issues an M=128, K=16 MMA about every 70 cycles at best,
@@ -549,6 +560,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ---------------- epilogue (last four warps) ----------------
         const int q = warp & 3;         // TMEM lane quarter this warp may access
         const int L = q * 32 + lane;    // accumulator row
+        const bool act_scaled = p.mode == 1 && *reinterpret_cast<volatile uint32_t*>(p.act_flag) != 0u;
         uint32_t ic = 0;
         int4 nd = (int)blockIdx.x < n_items ? tc_desc_load(p, blockIdx.x) : make_int4(0, 0, 0, 0);
         for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
@@ -580,18 +592,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         const float v = __uint_as_float(r[i]);
                         const float u = __shfl_down_sync(0xffffffffu, v, 8);  // up row sits 8 lanes below
                         const int n = c0 + i;
-                        if (r16 < 8 && n < it.n) {
-                            const float xi = p.xinv ? p.xinv[it.pos0 + n] : 1.f;
-                            const float a = activate(v * xi, u * xi, p.act_kind);
-                            p.act_s[(size_t)(it.pos0 + n) * p.I + irow] = __float2half_rn(a);
+                        const bool mine = r16 < 8 && n < it.n;
+                        const float xi = (p.xinv && n < it.n) ? p.xinv[it.pos0 + n] : 1.f;
+                        float a = mine ? activate(v * xi, u * xi, p.act_kind) : 0.f;
+                        // The warp's 16 activation rows of position n go to fp16 unscaled
+                        // unless one of them reaches 2^15; then all 16 are stored times a
+                        // power of two and the exponent is recorded for act_fixup_kernel.
+                        if (__any_sync(0xffffffffu, fabsf(a) >= 32768.f)) {
+                            const float sc = pow2_scale(warp_max(fabsf(a)));
+                            a *= sc;
+                            if (lane == 0 && n < it.n && sc < 1.f) {
+                                int e = 0;
+                                frexpf(sc, &e);  // sc = 2^(e - 1)
+                                p.act_exp[(size_t)(it.pos0 + n) * (p.I / 16) + it.mt * 4 + q] = (int8_t)(1 - e);
+                                atomicOr(p.act_flag, 1u);
+                            }
                         }
+                        if (mine) p.act_s[(size_t)(it.pos0 + n) * p.I + irow] = __float2half_rn(a);
                     }
                 } else {
                     const int hrow = it.mt * 128 + L;
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const int n = c0 + i;
-                        if (n < it.n) p.ys[(size_t)(it.pos0 + n) * p.H + hrow] = __uint_as_float(r[i]);
+                        if (n < it.n) {
+                            const float f = act_scaled ? p.act_inv[it.pos0 + n] : 1.f;
+                            p.ys[(size_t)(it.pos0 + n) * p.H + hrow] = __uint_as_float(r[i]) * f;
+                        }
                     }
                 }
             }
@@ -603,6 +630,50 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc::fence_before_sync();
     __syncthreads();
     if (warp == MMA_WARP) tc::tmem_dealloc(tmem, TC_TMEM_COLS);
+}
+
+// ---- activation range ---------------------------------------------------------------------------
+
+// The gate/up epilogue stores activations in fp16.  A 16-row block of a
+// position whose largest |act| reaches 2^15 is stored times 2^-m (m >= 1, in
+// act_exp; act_flag raised).  This pass gives every position one exponent,
+// the largest of its blocks: a block stored with m is multiplied by
+// 2^(m - m_max) in place (exact unless a value drops below the fp16 normal
+// range, i.e. under 2^-24 of the position's largest), and act_inv[pos] =
+// 2^m_max, by which the down projection's epilogue multiplies the position's
+// outputs.  With act_flag clear (every activation fits fp16) a CTA only reads
+// the flag.  One warp per position.
+__global__ void act_fixup_kernel(const uint32_t* __restrict__ act_flag, const int8_t* __restrict__ act_exp,
+                                 __half* __restrict__ act_s, float* __restrict__ act_inv,
+                                 const int* __restrict__ n_pos, int I) {
+    pdl_wait();  // the gate/up projection is complete and visible
+    pdl_launch_dependents();
+    if (*reinterpret_cast<const volatile uint32_t*>(act_flag) == 0u) return;
+    const int nb = I / 16, lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
+    const int np = *n_pos;
+    for (int pos = blockIdx.x * wpb + (threadIdx.x >> 5); pos < np; pos += gridDim.x * wpb) {
+        const int8_t* ex = act_exp + (size_t)pos * nb;
+        int mmax = 0;
+        for (int b = lane; b < nb; b += 32) mmax = max(mmax, (int)ex[b]);
+        mmax = __reduce_max_sync(0xffffffffu, mmax);
+        if (lane == 0) act_inv[pos] = ldexpf(1.f, mmax);
+        if (mmax == 0) continue;
+        uint4* row = reinterpret_cast<uint4*>(act_s + (size_t)pos * I);
+        for (int c = lane; c < I / 8; c += 32) {  // 8 halves of block c / 2
+            const int d = (int)ex[c >> 1] - mmax;
+            if (d == 0) continue;
+            const float f = ldexpf(1.f, d);
+            uint4 v = row[c];
+            uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+                const __half2 h = __floats2half2_rn(a.x * f, a.y * f);
+                w[k] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+            row[c] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
 }
 
 // ---- combine ----------------------------------------------------------------------------------
@@ -649,7 +720,8 @@ constexpr int PF_CHUNK = 128;
 constexpr int PF_PAD = 1;
 
 struct PrefillWs {
-    size_t status, idx, w, count, offset, chunks, n_chunks, n_pos, s_tok, inv_pos, xinv, Xs, act_s, ys, total;
+    size_t status, idx, w, count, offset, chunks, n_chunks, n_pos, s_tok, inv_pos, xinv, Xs, act_s, ys;
+    size_t act_flag, act_exp, act_inv, total;
     size_t pcap;  // position rows
 };
 
@@ -688,6 +760,12 @@ static PrefillWs prefill_ws_layout(const kq_table* t, int T, int K) {
     o = al(o + P * t->d.inter * 2);
     L.ys = o;
     o = al(o + P * t->d.hidden * 4);
+    L.act_flag = o;
+    o = al(o + 4);
+    L.act_exp = o;
+    o = al(o + P * (t->d.inter / 16));
+    L.act_inv = o;
+    o = al(o + P * 4);
     L.total = o;
     return L;
 }
@@ -828,6 +906,9 @@ extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x
     __half* Xs = reinterpret_cast<__half*>(ws + L.Xs);
     __half* act_s = reinterpret_cast<__half*>(ws + L.act_s);
     float* ys = reinterpret_cast<float*>(ws + L.ys);
+    uint32_t* act_flag = reinterpret_cast<uint32_t*>(ws + L.act_flag);
+    int8_t* act_exp = reinterpret_cast<int8_t*>(ws + L.act_exp);
+    float* act_inv = reinterpret_cast<float*>(ws + L.act_inv);
     const int P = (int)L.pcap;
 
     if (logits && launch_router_ext(logits, T, E, K, idx_use, w_use, s) != KQ_OK) return KQ_ERR_CUDA;
@@ -835,10 +916,10 @@ extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x
         const int threads = 256;
         if (cudaError_t e = launch_dep(group_kernel, dim3(1), dim3(GROUP_THREADS), 0, s, (const int32_t*)idx_use, A,
                                        K, E, PF_CHUNK, PF_PAD, count, offset, s_tok, inv_pos, chunk_list, n_chunks,
-                                       n_pos, status))
+                                       n_pos, status, act_flag))
             return pf_fail("grouping", e);
         if (cudaError_t e = launch_dep(gather_kernel, dim3((P * 32 + threads - 1) / threads), dim3(threads), 0, s, x,
-                                       x_dtype, H, (const int32_t*)s_tok, (const int*)n_pos, Xs, xinv))
+                                       x_dtype, H, (const int32_t*)s_tok, (const int*)n_pos, Xs, xinv, act_exp, I / 16))
             return pf_fail("gather", e);
     }
     // Rows of Xs / act_s at pad positions or past the placed ones are never
@@ -871,6 +952,9 @@ extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x
     p.xinv = x_dtype == KQ_DT_F16 ? nullptr : xinv;
     p.act_kind = t->d.activation;
     p.status = status;
+    p.act_flag = act_flag;
+    p.act_exp = act_exp;
+    p.act_inv = act_inv;
     const int boxes[4] = {16, 32, 64, 128};
     // One grouped GEMM over `src` [P][Kdim].
     auto gemm = [&](const __half* src, int Kdim) -> int {
@@ -889,6 +973,9 @@ extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x
     p.mat_off = 0;
     p.n_mt = I / 64;
     if (int rc = gemm(Xs, H)) return rc;
+    if (cudaError_t e = launch_dep(act_fixup_kernel, dim3(nsm), dim3(256), 0, s, (const uint32_t*)act_flag,
+                                   (const int8_t*)act_exp, act_s, act_inv, (const int*)n_pos, I))
+        return pf_fail("activation range pass", e);
     // down
     p.mode = 1;
     p.mat_off = t->gateup_bytes;

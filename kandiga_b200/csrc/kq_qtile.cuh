@@ -60,7 +60,7 @@ __host__ __device__ constexpr int tile_bytes(int bits) { return bits == 3 ? 3584
 
 // offset constant 2^(10-k) of pair j (fp32)
 template <int BITS>
-__host__ __device__ __forceinline__ float pair_offset(int j) {
+__host__ __device__ __forceinline__ constexpr float pair_offset(int j) {
     if (BITS == 3) {
         if (j >= 30) return 1024.f;
         int s = j % 5;

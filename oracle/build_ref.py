@@ -29,7 +29,17 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
-DEFAULT_REF = os.environ.get("KQ_REFERENCE_ROOT", "/root/reference")
+def reference_root():
+    """The kandiga project tree: $KQ_REFERENCE_ROOT, else a directory named
+    `reference` beside this repository's root; None when neither exists."""
+    env = os.environ.get("KQ_REFERENCE_ROOT")
+    if env:
+        return env if os.path.isdir(env) else None
+    beside = os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return beside if os.path.isdir(beside) else None
+
+
+DEFAULT_REF = reference_root()
 
 CFLAGS = ["-O2", "-ffp-contract=off", "-fPIC", "-shared", "-fopenmp", "-std=gnu11", "-w"]
 
@@ -132,7 +142,10 @@ int ref_lg_expert(int bits, int use_gelu, int hidden, int inter, const size_t* o
 """
 
 
-def build(ref_root: str = DEFAULT_REF) -> list[str]:
+def build(ref_root: str | None = None) -> list[str]:
+    ref_root = ref_root or DEFAULT_REF
+    if ref_root is None:
+        raise FileNotFoundError("reference tree not found: set KQ_REFERENCE_ROOT")
     small_path = os.path.join(ref_root, "kandiga", "metal", "kandiga_cpu_expert.m")
     lg_path = os.path.join(ref_root, "kandiga", "metal", "kandiga_cpu_expert_lg.m")
     if not (os.path.exists(small_path) and os.path.exists(lg_path)):
@@ -169,5 +182,5 @@ def build(ref_root: str = DEFAULT_REF) -> list[str]:
 
 
 if __name__ == "__main__":
-    for p in build(sys.argv[1] if len(sys.argv) > 1 else DEFAULT_REF):
+    for p in build(sys.argv[1] if len(sys.argv) > 1 else None):
         print(p)

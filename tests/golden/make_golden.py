@@ -1,7 +1,7 @@
 """Generate the golden fixtures in tests/golden/ from the reference itself.
 
-Runs only where the reference tree is mounted (default /root/reference, or
-$KQ_REFERENCE_ROOT).  The fixtures it writes are committed; the GPU box and the
+Runs only where the reference tree is mounted ($KQ_REFERENCE_ROOT, or a
+directory named `reference` beside this repository).  The fixtures it writes are committed; the GPU box and the
 test suite never read the reference tree.
 
 Fixtures:
@@ -35,8 +35,10 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("KQ_REFERENCE_ROOT", "/root/reference")
 sys.path.insert(0, REPO)
+from oracle.build_ref import reference_root  # noqa: E402
+
+REF = reference_root()
 
 
 def _load(name, path):

@@ -113,6 +113,38 @@ def test_set_kv_cache_then_decode(gpu):
         assert rel_l2(got, want) < TOL
 
 
+def test_configs2_layer_shape_at_kv_2048(gpu):
+    """The benched dense decoder's per-layer shape: H 2560, 16 q / 4 kv heads x
+    256 with q/k norms, SwiGLU 9216, 3-bit with fp16 scales, rope_theta 1e6,
+    the KV cache pre-filled to 2048 tokens ~N(0,1) through set_kv_cache.  Two
+    layers and a 4096-token vocabulary keep the numpy oracle small; the
+    attention runs the same context split (one chunk per SM) and merge as the
+    36-layer bench (kandiga/metal/full_forward_lg.m:1078-1354,
+    kandiga/metal/attention.metal:752-849)."""
+    cfg = dict(hidden_size=2560, intermediate_size=9216, num_hidden_layers=2, num_attention_heads=16,
+               num_key_value_heads=4, head_dim=256, vocab_size=4096, rms_norm_eps=1e-6, rope_theta=1e6,
+               max_cache_len=2048 + 8)
+    W = random_model(cfg, bits=3, sb="f16", seed=21, std=0.02)
+    ref = FullStepRef(cfg, W, 3, "f16")
+    e = engine(cfg, W, "f16")
+    rng = np.random.RandomState(4)
+    S = 2048
+    for l in range(cfg["num_hidden_layers"]):
+        k = rng.randn(4, S, 256).astype(np.float16)
+        v = rng.randn(4, S, 256).astype(np.float16)
+        assert e.set_kv_cache(l, k, v) == 0
+        ref.kc[l, :, :S], ref.vc[l, :, :S] = k, v
+    assert e.set_position(S) == 0
+    worst = 0.0
+    for i in range(4):
+        got, want = e.forward(7 + i, S + i), ref.step(7 + i, S + i)
+        err = rel_l2(got, want)
+        worst = max(worst, err)
+        assert err < TOL, (i, err)
+        assert int(np.argmax(got)) == int(np.argmax(want))
+    print("configs[2] layer shape worst rel L2", worst)
+
+
 def test_errors_are_reported(gpu):
     from kandiga_b200 import _native as N
     from kandiga_b200.full import FullForwardEngine

@@ -13,8 +13,8 @@ GOLD = os.path.join(os.path.dirname(__file__), "golden")
 
 def _ref_small():
     ref = O.ref_lib("small")
-    if ref is None and os.path.isdir(os.environ.get("KQ_REFERENCE_ROOT", "/root/reference")):
-        from oracle import build_ref
+    from oracle import build_ref
+    if ref is None and build_ref.reference_root() is not None:
         build_ref.build()
         O._REF.clear()
         ref = O.ref_lib("small")

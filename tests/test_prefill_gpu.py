@@ -180,3 +180,83 @@ def test_prefill_bench_shape(gpu):
     pk = a["per_k"].float().cpu().numpy()[rows]
     worst = max(rel_l2(pk[i, k], y[i, k]) for i in range(len(rows)) for k in range(K))
     assert worst < RTOL_L2, worst
+
+
+@pytest.mark.parametrize("xdt,mag", [(torch.bfloat16, 3e3), (torch.bfloat16, 1e4), (torch.float16, 2e3)])
+def test_prefill_large_activations(gpu, xdt, mag):
+    """Inputs of magnitude 1e3-1e4: gate/up outputs reach ~1e5 and SwiGLU
+    products ~1e7-1e9, far beyond fp16.  The activations are stored with a
+    power-of-two exponent per (token, expert, 16 rows) and brought to one
+    exponent per (token, expert) before the down projection; results match the
+    fp32 oracle to the usual 2e-3."""
+    E, H, I, K, T = 16, 2048, 512, 8, 48
+    layer = get_layer(4, H, I, E, "f16", seed=41)
+    t = make_table(layer)
+    rng = np.random.RandomState(41)
+    xf = rng.randn(T, H).astype(np.float32) * np.float32(mag)
+    xf[::7] *= 0.01  # some tokens stay in range: one call mixes scaled and unscaled positions
+    x = torch.from_numpy(xf).to(xdt).cuda()
+    logits = torch.from_numpy(rng.randn(T, E).astype(np.float32)).cuda()
+    r = t.moe(0, x, logits=logits, top_k=K, per_k=True, combine=True, out_dtype=torch.float32, path="prefill")
+    assert torch.isfinite(r["per_k"]).all() and torch.isfinite(r["out"]).all()
+    check(layer, t, x, r["idx"].cpu().numpy(), r["weights"].cpu().numpy(), r)
+    assert t.status() == 0
+    # the next call on in-range inputs is not affected by the scaled one before it
+    x2 = torch.from_numpy(rng.randn(T, H).astype(np.float32)).to(xdt).cuda()
+    r2 = t.moe(0, x2, logits=logits, top_k=K, per_k=True, combine=True, out_dtype=torch.float32, path="prefill")
+    check(layer, t, x2, r2["idx"].cpu().numpy(), r2["weights"].cpu().numpy(), r2)
+
+
+def _scaled_experts(layer, experts, factor):
+    """a copy of `layer` whose experts `experts` have every scale and bias
+    multiplied by `factor` (a power of two: exact in fp16 and bf16)"""
+    s = [a.copy() for a in layer.s]
+    b = [a.copy() for a in layer.b]
+    for m in range(3):
+        for e in experts:
+            s[m][e] = O.f32_to_sb(O.sb_to_f32(s[m][e], layer.sb_dtype) * np.float32(factor), layer.sb_dtype)
+            b[m][e] = O.f32_to_sb(O.sb_to_f32(b[m][e], layer.sb_dtype) * np.float32(factor), layer.sb_dtype)
+    return O.ExpertLayer(layer.bits, layer.hidden, layer.inter, layer.w, s, b, layer.sb_dtype, layer.act)
+
+
+@pytest.mark.parametrize("sb,factor", [("f16", 2.0 ** 13), ("bf16", 2.0 ** 18)])
+def test_prefill_large_scale_groups(gpu, sb, factor):
+    """Experts whose groups all have |scale| >= 64 (~120 with fp16 scales,
+    ~4e3 with bf16; weights up to ~4e2 / ~3e4, still fp16 numbers) beside
+    experts of ordinary scale.  The dequantisation forms q exactly and then
+    q*s + b in one rounding, so no intermediate overflows; the SwiGLU products
+    of the large experts (~1e6 / ~1e10) leave fp16 range and are stored with
+    power-of-two exponents.  Prefill and decode both match the fp32 oracle to
+    2e-3."""
+    E, H, I, K, T = 8, 1024, 512, 4, 64
+    layer = _scaled_experts(get_layer(3, H, I, E, sb, seed=43), [1, 4, 6], factor)
+    assert np.abs(O.sb_to_f32(layer.s[0][1], sb)).min() >= 64
+    t = make_table(layer)
+    rng = np.random.RandomState(43)
+    x = torch.from_numpy(rng.randn(T, H).astype(np.float16)).cuda()
+    logits = torch.from_numpy(rng.randn(T, E).astype(np.float32)).cuda()
+    for path in ("prefill", "decode"):
+        r = t.moe(0, x, logits=logits, top_k=K, per_k=True, combine=True, out_dtype=torch.float32, path=path)
+        assert torch.isfinite(r["per_k"]).all()
+        check(layer, t, x, r["idx"].cpu().numpy(), r["weights"].cpu().numpy(), r)
+        assert t.status() == 0
+
+
+def test_prefill_weight_out_of_fp16_range_is_reported(gpu):
+    """A bf16 group whose weights exceed the fp16 range (|q s + b| > 65504)
+    cannot be dequantised to fp16: the call latches KQ_DEV_RANGE."""
+    from kandiga_b200 import _native as N
+    E, H, I, K, T = 4, 1024, 512, 2, 16
+    layer = get_layer(3, H, I, E, "bf16", seed=44)
+    s = [a.copy() for a in layer.s]
+    b = [a.copy() for a in layer.b]
+    s[0][1, 3, 2] = O.f32_to_sb(np.array([3.0e4], np.float32), "bf16")[0]
+    b[0][1, 3, 2] = O.f32_to_sb(np.array([-1.0e5], np.float32), "bf16")[0]
+    layer = O.ExpertLayer(layer.bits, layer.hidden, layer.inter, layer.w, s, b, "bf16", layer.act)
+    t = make_table(layer)
+    x = torch.randn(T, H, device="cuda").half()
+    idx = torch.ones(T, K, device="cuda", dtype=torch.int32)
+    idx[:, 1] = 2
+    t.moe(0, x, idx=idx, per_k=True, combine=False, out_dtype=torch.float32, path="prefill")
+    assert t.status() & N.DEV_RANGE
+    assert t.status() == 0  # reading clears the word

@@ -211,3 +211,43 @@ def test_session_round_trip_of_compressed_cache(gpu, tmp_path):
         d.update(k2, v2)
         r.update(k2, v2)
         assert torch.equal(d.keys, r.keys) and torch.equal(d.values, r.values)
+
+
+def test_configs3_shape_append_and_attend(gpu):
+    """The benched TurboQuant shape itself: 8 KV heads x 32768 tokens x D128,
+    K and V fp16 N(0,1) with 1% of the (head, channel) pairs scaled x8, one
+    bulk append, then single-query attention (8 query heads).  32768 tokens
+    are 128 chunks per head, so the chunk-partial merge runs more than one
+    batch of chunks per warp.  Codes are compared with the numpy restatement of
+    kandiga/kv_compress.py:59-92 and the attention with softmax attention over
+    the reference reconstruction (kandiga/kv_compress.py:94-118) of the GPU's
+    own codes, with the bars of the smaller cases."""
+    rng = np.random.RandomState(3)
+    b, h, s, d = 1, 8, 32768, 128
+    k, v = kv_with_outliers(rng, b, h, s, d)
+    kt = torch.from_numpy(k).half()
+    vt = torch.from_numpy(v).half()
+    cache = TurboQuantCache(d, h, seed=42)
+    cache.update(kt.cuda(), vt.cuda())
+    assert cache.seq_len == s
+    ref = O.TurboQuantRef(d, h, 42)
+    for which, x in ((0, kt), (1, vt)):
+        q_ref, s_ref, z_ref, g_ref = ref.quantize(x.float().numpy())
+        codes, scales, zeros, signs = [t.cpu().numpy() for t in cache.export(which)]
+        np.testing.assert_allclose(scales, s_ref, rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(zeros, z_ref, rtol=1e-5, atol=1e-5)
+        assert np.mean(codes == q_ref) >= 0.995
+        assert np.max(np.abs(codes.astype(np.int32) - q_ref)) <= 1
+        assert np.mean(signs == g_ref) >= 0.99
+    q = rng.randn(b, h, d).astype(np.float32)
+    out, scores = cache.attend(torch.from_numpy(q).half().cuda(), return_scores=True)
+    kc = [t.cpu().numpy()[0] for t in cache.export(0)]
+    v_hat = ref.dequantize(*[t.cpu().numpy()[0] for t in cache.export(1)])
+    qh = q[0].astype(np.float16).astype(np.float32)
+    o_ref, s_ref = ref.attend(qh, *kc, v_hat)
+    got_s = scores[0].cpu().numpy()
+    assert np.max(np.abs(got_s - s_ref)) <= 2e-3 * max(1.0, np.max(np.abs(s_ref)))
+    assert rel_l2(out[0].cpu().numpy(), o_ref) < 2e-3
+    # the same query again gives bit-identical results (fixed merge order)
+    out2 = cache.attend(torch.from_numpy(q).half().cuda())
+    assert torch.equal(out, out2)
