@@ -297,6 +297,28 @@ int kq_moe_decode_static(const kq_table* t, int layer, const void* x, int x_dtyp
                          const float* logits, int32_t* idx, float* weights, int K, void* out_per_k,
                          void* out, int out_dtype, const void* residual, void* stream);
 
+/* Routed-expert decode of n independent single-token items in one persistent
+ * launch: item j is row j of x, routed by row j of logits (or idx/weights as
+ * inputs when logits is NULL, exactly as kq_moe_decode), through layer
+ * layers[j] (device int32 [n]; NULL: every item uses `layer`); out [n][H],
+ * out_per_k [n][K][H], residual [n][H], optional RMSNorm of x (norm_w [H] in
+ * the x dtype, fp16/bf16 x).  Each item is the reference's per-token expert
+ * path (kandiga/metal/kandiga_cpu_expert.m:471-552 with the routing of
+ * kandiga/metal/moe_block.metal:419-505 and the blend of :556-584), so with
+ * layers == NULL this equals kq_moe_decode for T = n tokens.  The items'
+ * weight tiles are one stream of equal work units spread over all SMs, so
+ * weights of later items are read from HBM while earlier items' gate/up ->
+ * down dependencies resolve; items must not depend on one another's outputs.
+ * One CTA per SM, launched cooperatively; the workspace (size independent of
+ * n) holds small rings of activations and counters, which the call zeroes on
+ * the stream before its launch.  K <= 32. */
+size_t kq_moe_decode_batch_workspace_size(const kq_table* t, int top_k);
+int kq_moe_decode_batch(const kq_table* t, int n, const int32_t* layers, int layer, const void* x,
+                        int x_dtype, const float* logits, int32_t* idx, float* weights, int K,
+                        void* out_per_k, void* out, int out_dtype, const void* residual,
+                        const void* norm_w, float eps, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
 /* Routed-expert MLP for many tokens (prefill), same arguments and outputs as
  * kq_moe_decode.  The T*K assignments are grouped by expert (stable, token
  * order inside an expert, as kandiga/engine.py:407-418) and every expert runs

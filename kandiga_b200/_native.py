@@ -97,6 +97,10 @@ SIGNATURES = {
     "kq_moe_prefill_workspace_size": (c_size_t, [c_void_p, c_int, c_int]),
     "kq_moe_prefill": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int,
                                c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "kq_moe_decode_batch_workspace_size": (c_size_t, [c_void_p, c_int]),
+    "kq_moe_decode_batch": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                                    c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_float,
+                                    c_void_p, c_size_t, c_void_p]),
     "kq_moe_decode_static": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                      c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "kq_qmat_create": (c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_void_p)]),

@@ -125,6 +125,11 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
         if (global_ns() - t0 > KQ_DRAIN_NS) return;
 }
 
+// plain arrive (one count) on a shared-memory mbarrier
+__device__ __forceinline__ void mbar_arrive_local(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

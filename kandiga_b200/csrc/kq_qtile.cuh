@@ -408,6 +408,139 @@ __device__ __forceinline__ void tile_compute(const TileRegs<BITS>& R, int st, co
     y1 += sb_lo<SB_DT>(sb.w) * (d[3] - cx.z) + sb_hi<SB_DT>(sb.w) * cx.w;
 }
 
+// ---- padded input layout ---------------------------------------------------------
+// A variant of the engine for kernels whose warps each run long sequences of
+// tiles.  The staged input keeps each 64-wide group in a row of PAD_ROW bytes
+// (128 of data + 16 of padding), so the eight groups a warp reads at once
+// start in eight different 16-byte bank windows; and each lane reads its B
+// operand halves through two pointers -- its own group's row, or a zero row
+// -- instead of selecting between x and 0 at every step.
+constexpr int PAD_ROW = 144;                  // bytes per staged group row
+constexpr int PAD_HALFS = PAD_ROW / 2;        // 72 halves
+
+__host__ __device__ constexpr size_t pad_bytes(int npad) { return (size_t)(npad / GS) * PAD_ROW; }
+
+// chunk c (8 consecutive inputs) of a padded staged vector
+__device__ __forceinline__ __half* pad_chunk(__half* xs, int c) { return xs + (c >> 3) * PAD_HALFS + (c & 7) * 8; }
+
+// store_chunk into the padded layout; returns (C part, X part) as store_chunk
+template <int BITS>
+__device__ __forceinline__ float2 store_chunk_pad(const float (&v)[8], float mul, const float (&off)[4],
+                                                  __half* xs, int c) {
+    uint32_t h[4];
+    float cc = 0.f, xx = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const __half2 hh = __floats2half2_rn(v[2 * k] * mul, v[2 * k + 1] * mul);
+        h[k] = *reinterpret_cast<const uint32_t*>(&hh);
+        const float2 f = __half22float2(hh);
+        const float pr = f.x + f.y;
+        cc += off[k] * pr;
+        xx += pr;
+    }
+    *reinterpret_cast<uint4*>(pad_chunk(xs, c)) = make_uint4(h[0], h[1], h[2], h[3]);
+    return make_float2(cc, xx);
+}
+
+// stage_fused into the padded layout (same arguments and rules)
+template <int BITS, int MAXB>
+__device__ __forceinline__ void stage_fused_pad(const void* src, int dtype, size_t off, int n, int npad, float mul,
+                                                bool cg, int rank, int nthr, __half* xs, float2* cx,
+                                                const void* w2 = nullptr) {
+    const int nch = n / 8, npch = npad / 8;
+    float offv[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) offv[k] = chunk_offset<BITS>(rank & 7, k);
+    for (int c0 = rank; c0 < npch; c0 += nthr * MAXB) {
+        float v[MAXB][8];
+#pragma unroll
+        for (int b = 0; b < MAXB; ++b) {
+            const int c = c0 + b * nthr;
+            if (c < nch) {
+                load8(src, dtype, off + (size_t)c * 8, cg, v[b]);
+                if (w2) {
+                    float wv[8];
+                    load8(w2, dtype, (size_t)c * 8, false, wv);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) v[b][k] *= wv[k];
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[b][k] = 0.f;
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < MAXB; ++b) {
+            const int c = c0 + b * nthr;
+            if (c < npch) {  // warp-uniform: npch is a multiple of 64, ranks come in whole warps
+                const float2 part = store_chunk_pad<BITS>(v[b], mul, offv, xs, c);
+                group_reduce_store(part, rank, c, cx, 0xffffffffu);
+            }
+        }
+    }
+}
+
+// MMA steps J..31 with B from two padded rows (x0: this lane's b0 row or the
+// zero row, x1: its b1 row or the zero row) and four accumulator chains.
+template <int BITS, int J>
+__device__ __forceinline__ void mma_steps_pad(float (&d)[4][4], const uint32_t (&wd)[4][TileT<BITS>::W],
+                                              const uint32_t (&sh)[4][TileT<BITS>::W], const uint4* x0,
+                                              const uint4* x1) {
+    if constexpr (J < 32) {
+        const uint4 v0 = x0[J / 4], v1 = x1[J / 4];
+        const uint32_t b0[4] = {v0.x, v0.y, v0.z, v0.w};
+        const uint32_t b1[4] = {v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            uint32_t a0, a1, a2, a3;
+            if (u == 0) {
+                a0 = pair_of<BITS, J + 0>(wd[0], sh[0]); a1 = pair_of<BITS, J + 0>(wd[2], sh[2]);
+                a2 = pair_of<BITS, J + 0>(wd[1], sh[1]); a3 = pair_of<BITS, J + 0>(wd[3], sh[3]);
+            } else if (u == 1) {
+                a0 = pair_of<BITS, J + 1>(wd[0], sh[0]); a1 = pair_of<BITS, J + 1>(wd[2], sh[2]);
+                a2 = pair_of<BITS, J + 1>(wd[1], sh[1]); a3 = pair_of<BITS, J + 1>(wd[3], sh[3]);
+            } else if (u == 2) {
+                a0 = pair_of<BITS, J + 2>(wd[0], sh[0]); a1 = pair_of<BITS, J + 2>(wd[2], sh[2]);
+                a2 = pair_of<BITS, J + 2>(wd[1], sh[1]); a3 = pair_of<BITS, J + 2>(wd[3], sh[3]);
+            } else {
+                a0 = pair_of<BITS, J + 3>(wd[0], sh[0]); a1 = pair_of<BITS, J + 3>(wd[2], sh[2]);
+                a2 = pair_of<BITS, J + 3>(wd[1], sh[1]); a3 = pair_of<BITS, J + 3>(wd[3], sh[3]);
+            }
+            mma_f16(d[u], a0, a1, a2, a3, b0[u], b1[u]);
+        }
+        mma_steps_pad<BITS, J + 4>(d, wd, sh, x0, x1);
+    }
+}
+
+// tile_compute on a padded staged input; zrow: PAD_ROW zero bytes (16-byte aligned)
+template <int BITS, int SB_DT>
+__device__ __forceinline__ void tile_compute_pad(const TileRegs<BITS>& R, int st, const __half* xs,
+                                                 const float2* cxv, const __half* zrow, float& y0, float& y1) {
+    constexpr int W = TileT<BITS>::W;
+    const int lane = threadIdx.x & 31;
+    const int n = lane >> 2, t = lane & 3;
+    uint32_t sh[4][W];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int w = 0; w < W; ++w) sh[q][w] = R.wd[q][w] >> (BITS == 3 ? 9 : 8);
+    // B operand: lane (n, t) feeds b0 for group t when n == t, b1 for group t+4 when n == t+4
+    const __half* row = xs + (size_t)st * TILE_GROUPS * PAD_HALFS;
+    const uint4* x0 = reinterpret_cast<const uint4*>(n == t ? row + t * PAD_HALFS : zrow);
+    const uint4* x1 = reinterpret_cast<const uint4*>(n == t + 4 ? row + (t + 4) * PAD_HALFS : zrow);
+    float acc[4][4] = {};
+    mma_steps_pad<BITS, 0>(acc, R.wd, sh, x0, x1);
+    float d[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = (acc[0][i] + acc[1][i]) + (acc[2][i] + acc[3][i]);
+    const float4 cx = *reinterpret_cast<const float4*>(cxv + st * TILE_GROUPS + 2 * t);
+    const uint4 sb = R.sb;
+    y0 += sb_lo<SB_DT>(sb.x) * (d[0] - cx.x) + sb_hi<SB_DT>(sb.x) * cx.y;
+    y0 += sb_lo<SB_DT>(sb.y) * (d[1] - cx.z) + sb_hi<SB_DT>(sb.y) * cx.w;
+    y1 += sb_lo<SB_DT>(sb.z) * (d[2] - cx.x) + sb_hi<SB_DT>(sb.z) * cx.y;
+    y1 += sb_lo<SB_DT>(sb.w) * (d[3] - cx.z) + sb_hi<SB_DT>(sb.w) * cx.w;
+}
+
 // finish the row dot products across the 4 lanes of a quad
 __device__ __forceinline__ void quad_reduce(float& y0, float& y1) {
     y0 += __shfl_xor_sync(0xffffffffu, y0, 1);

@@ -166,6 +166,46 @@ class ExpertTable:
                     weights=weights)
 
 
+    def decode_batch(self, x, *, layers=None, layer=0, logits=None, idx=None, weights=None, top_k=8,
+                     per_k=False, combine=True, residual=None, norm_w=None, eps=1e-6, out_dtype=None, out=None,
+                     out_per_k=None):
+        """n independent single-token items in one launch (kq_moe_decode_batch):
+        item j = row j of x through layer layers[j] (int32 CUDA tensor [n]; None:
+        all through `layer`), routed by row j of `logits` or given by `idx` /
+        `weights`.  Same outputs as moe(); items must not depend on each other."""
+        n = x.shape[0]
+        K = idx.shape[1] if idx is not None else top_k
+        out_dtype = out_dtype or (x.dtype if x.dtype != torch.float32 else torch.float32)
+        dev = x.device
+        if logits is not None:
+            if idx is None:
+                idx = torch.empty(n, K, dtype=torch.int32, device=dev)
+            if weights is None:
+                weights = torch.empty(n, K, dtype=torch.float32, device=dev)
+        if combine and out is None:
+            out = torch.empty(n, self.hidden, dtype=out_dtype, device=dev)
+        if per_k and out_per_k is None:
+            out_per_k = torch.empty(n, K, self.hidden, dtype=out_dtype, device=dev)
+        need = int(self.lib.kq_moe_decode_batch_workspace_size(self.handle, K))
+        if getattr(self, "_bws", None) is None or self._bws.numel() < need:
+            self._bws = torch.zeros(max(need, 1), dtype=torch.uint8, device=dev)
+        rc = self.lib.kq_moe_decode_batch(self.handle, n, _ptr(layers), layer, _ptr(x), _DT[x.dtype],
+                                          _ptr(logits), _ptr(idx), _ptr(weights), K,
+                                          _ptr(out_per_k) if per_k else None, _ptr(out) if combine else None,
+                                          _DT[out_dtype], _ptr(residual), _ptr(norm_w), eps, _ptr(self._bws),
+                                          self._bws.numel(), _stream())
+        N.check(rc, "kq_moe_decode_batch")
+        return dict(out=out if combine else None, per_k=out_per_k if per_k else None, idx=idx,
+                    weights=weights)
+
+    def batch_status(self) -> int:
+        """device status word of decode_batch (read and cleared)"""
+        if getattr(self, "_bws", None) is None:
+            return 0
+        st = ctypes.c_uint32(0)
+        N.check(self.lib.kq_status_read(_ptr(self._bws), ctypes.byref(st), _stream()), "kq_status_read")
+        return st.value
+
     def moe_block(self, layer, x, logits, top_k, shared_gate, shared_id=None, gate_bits=4, gate_sb="f16",
                   residual=None, out_dtype=None, path="auto"):
         """MoE block with a shared expert (kandiga/metal/moe_block.metal:134-584):
