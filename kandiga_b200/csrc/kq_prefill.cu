@@ -241,25 +241,31 @@ constexpr int TC_STAGE_BYTES = 16384; // 128 rows x 128 B
 constexpr int TC_TMEM_COLS = 512;     // 2 buffers x 256 (TC_NMMA x 64) columns, or TC_NMMA x 128 for a 128-token box
 static_assert(TC_NMMA * 64 <= 256 && TC_NMMA * 128 <= TC_TMEM_COLS, "accumulators must fit tensor memory");
 
-// Packed tiles land in shared memory through a 2D tensor map that views the
-// layer as rows of 128 bytes with the 128-byte swizzle: byte (row, 16*slot + b)
-// of a tile sits at row*128 + 16*(slot ^ (row & 7)) + b.  A dequantising
-// quarter-warp (rows r16 = 0..7 of one tile, one 64-wide group) then reads
-// eight distinct 16-byte bank groups.  Tile slots are 1024-byte aligned.
+// A super-tile (the 8 tiles of 128 weight rows x 512 columns) lands in shared
+// memory by ONE 3D TMA load: the layer viewed as 128-byte rows (dimension 1)
+// and tiles nst * tile_bytes apart (dimension 2), box = 128 bytes x one tile's
+// rows x 8 tiles, 128-byte swizzle.  (Each SM's copy engine completes only a
+// few copies per microsecond whatever their size: eight per-tile loads held a
+// super-tile to ~17 GB/s per SM.)  The tiles sit back to back, tile j from
+// 128-byte row j * rows_per_tile of the 1024-aligned slot, and byte
+// (R, 16 * c + b) of the slot at R * 128 + 16 * (c ^ (R & 7)) + b, so a
+// dequantising quarter-warp (rows r16 = 0..7 of one tile, one 64-wide group)
+// reads eight distinct 16-byte bank groups.
 template <int BITS>
-__host__ __device__ constexpr int tc_tile_slot() {
-    return (TileT<BITS>::BYTES + 1023) / 1024 * 1024;
+__host__ __device__ constexpr int tc_super_slot() {
+    return (8 * TileT<BITS>::BYTES + 1023) / 1024 * 1024;
 }
 
 template <int BITS>
 __host__ __device__ constexpr size_t tc_smem_bytes() {
-    return 1024 + (size_t)(TC_NSTAGE + TC_NB) * TC_STAGE_BYTES + (size_t)TC_NKQ * 8 * tc_tile_slot<BITS>() + 256;
+    return 1024 + (size_t)(TC_NSTAGE + TC_NB) * TC_STAGE_BYTES + (size_t)TC_NKQ * tc_super_slot<BITS>() + 256;
 }
 
-// 16-byte unit `lane` of 512-byte chunk `chunk` of a swizzled tile
-__device__ __forceinline__ uint4 tile_u4(const uint8_t* tile, int chunk, int lane) {
+// 16-byte unit `lane` of 512-byte chunk `chunk` of a swizzled tile whose first
+// 128-byte row is row `row0` of its 1024-aligned slot
+__device__ __forceinline__ uint4 tile_u4(const uint8_t* tile, int row0, int chunk, int lane) {
     const int row = chunk * 4 + (lane >> 3);
-    return *reinterpret_cast<const uint4*>(tile + row * 128 + (((lane & 7) ^ (row & 7)) << 4));
+    return *reinterpret_cast<const uint4*>(tile + row * 128 + (((lane & 7) ^ ((row0 + row) & 7)) << 4));
 }
 
 template <int SB_DT>
@@ -290,12 +296,12 @@ __device__ __forceinline__ void dq_pairs(const uint32_t* wd, const uint32_t* sh,
 // Returns max(|b|, |qmax*s + b|) in fp16: the largest |W| of the group (inf
 // when a weight or the scale/bias itself does not fit fp16).
 template <int BITS, int SB_DT>
-__device__ __forceinline__ __half dequant_row(const uint8_t* tile, int r16, int g, uint32_t (&out)[32]) {
+__device__ __forceinline__ __half dequant_row(const uint8_t* tile, int row0, int r16, int g, uint32_t (&out)[32]) {
     constexpr int W = TileT<BITS>::W;  // words per (lane, set); the scale/bias chunk is chunk W
     const int l = 4 * (r16 & 7) + (g & 3);
     const int set = 2 * (r16 >> 3) + (g >> 2);
     const int q0 = set * W;  // first word of the set; q0 % 4 is 0 (4-bit) or 0/2 (3-bit)
-    const uint4 u0 = tile_u4(tile, q0 >> 2, l), u1 = tile_u4(tile, (q0 >> 2) + 1, l);
+    const uint4 u0 = tile_u4(tile, row0, q0 >> 2, l), u1 = tile_u4(tile, row0, (q0 >> 2) + 1, l);
     const uint32_t arr[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
     const bool odd = (q0 & 3) != 0;
     uint32_t wd[W], sh[W];
@@ -306,7 +312,7 @@ __device__ __forceinline__ __half dequant_row(const uint8_t* tile, int r16, int 
     const int l2 = 4 * (r16 & 7) + (g >> 1), kk = 2 * (r16 >> 3) + (g & 1);
     const int srow = W * 4 + (l2 >> 3);
     const uint32_t sbw =
-        *reinterpret_cast<const uint32_t*>(tile + srow * 128 + (((l2 & 7) ^ (srow & 7)) << 4) + kk * 4);
+        *reinterpret_cast<const uint32_t*>(tile + srow * 128 + (((l2 & 7) ^ ((row0 + srow) & 7)) << 4) + kk * 4);
     const __half s = to_half16<SB_DT>(sbw & 0xFFFFu), b = to_half16<SB_DT>(sbw >> 16);
     const __half2 s2 = __halves2half2(s, s), b2 = __halves2half2(b, b);
     dq_pairs<BITS, SB_DT, 0>(wd, sh, s2, b2, out);
@@ -353,14 +359,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                   const __grid_constant__ CUtensorMap tkq) {
     extern __shared__ uint8_t smem_raw[];
     constexpr int TB = TileT<BITS>::BYTES;
-    constexpr int TS = tc_tile_slot<BITS>();
+    constexpr int TR = TB / 128;             // 128-byte rows per tile
+    constexpr int SS = tc_super_slot<BITS>();
     // 1024-byte aligned in the shared window; an offset from smem_raw keeps the
     // shared address space, so accesses through it compile to shared-memory ops
     uint8_t* sm = smem_raw + ((1024u - ((uint32_t)__cvta_generic_to_shared(smem_raw) & 1023u)) & 1023u);
     uint8_t* sA = sm;
     uint8_t* sB = sA + TC_NSTAGE * TC_STAGE_BYTES;
     uint8_t* sK = sB + TC_NB * TC_STAGE_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sK + TC_NKQ * 8 * TS);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sK + TC_NKQ * SS);
     uint64_t* kq_full = bars;                        // [TC_NKQ]
     uint64_t* kq_empty = kq_full + TC_NKQ;           // [TC_NKQ]
     uint64_t* a_full = kq_empty + TC_NKQ;            // [TC_NSTAGE]
@@ -424,12 +431,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const int s = kc % TC_NKQ;
                     mbar_wait_sleep(&kq_empty[s], ((kc / TC_NKQ) & 1) ^ 1, p.status);
                     mbar_expect_tx(&kq_full[s], 8 * TB);
-                    for (int j = 0; j < 8; ++j) {
-                        const int rt = it.mt * 8 + j;
-                        const size_t off = ebase + ((size_t)rt * p.nst + st) * TB;  // multiple of 128
-                        tc::tma_load_2d_hint(sK + ((size_t)s * 8 + j) * TS, &tkq, 0, (int)(off >> 7), &kq_full[s],
-                                             pol);
-                    }
+                    const size_t off = ebase + ((size_t)it.mt * 8 * p.nst + st) * TB;  // multiple of 128
+                    tc::tma_load_3d_hint(sK + (size_t)s * SS, &tkq, 0, (int)(off >> 7), 0, &kq_full[s], pol);
                 }
             }
             for (uint32_t f = kc > TC_NKQ ? kc - TC_NKQ : 0; f < kc; ++f)  // own fills landed
@@ -438,7 +441,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     } else if (warp == 1) {
         // ---------------- producer: token K-chunks (B operand) ----------------
         // A B stage holds gpb = 16384 / (box * 128) consecutive groups of the item
-        // (box rows x 64 fp16 each, one swizzled block per group).
+        // (box rows x 64 fp16 each, one swizzled block per group), fetched by one
+        // 3D load through the token tensor map of the item's box size.
         if (lane == 0) {
             const uint64_t pol = tc::policy_evict_last();
             uint32_t bc = 0;
@@ -449,15 +453,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const void* tm = it.box == 16 ? (const void*)&tb16
                                               : (it.box == 32 ? (const void*)&tb32
                                                               : (it.box == 64 ? (const void*)&tb64 : (const void*)&tb128));
-                const int gpb = TC_STAGE_BYTES / (it.box * 128);
+                const int gpb = TC_STAGE_BYTES / (it.box * 128);  // divides groups (a multiple of 8)
                 for (int g0 = 0; g0 < groups; g0 += gpb, ++bc) {
                     const int bs = bc % TC_NB;
-                    const int ng = min(gpb, groups - g0);
                     mbar_wait_sleep(&b_empty[bs], ((bc / TC_NB) & 1) ^ 1, p.status);
-                    mbar_expect_tx(&b_full[bs], (uint32_t)(ng * it.box * 128));
-                    for (int j = 0; j < ng; ++j)
-                        tc::tma_load_2d_hint(sB + (size_t)bs * TC_STAGE_BYTES + (size_t)j * it.box * 128, tm,
-                                             (g0 + j) * 64, it.pos0, &b_full[bs], pol);
+                    mbar_expect_tx(&b_full[bs], (uint32_t)TC_STAGE_BYTES);
+                    // one 3D load: gpb groups of box rows x 64 fp16, group j at j * box * 128 bytes
+                    tc::tma_load_3d_hint(sB + (size_t)bs * TC_STAGE_BYTES, tm, 0, it.pos0, g0, &b_full[bs], pol);
                 }
             }
             for (uint32_t f = bc > TC_NB ? bc - TC_NB : 0; f < bc; ++f)  // own fills landed
@@ -474,14 +476,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int st = 0; st < p.nst; ++st, ++kc) {
                 const int s = kc % TC_NKQ;
                 mbar_wait_sleep(&kq_full[s], (kc / TC_NKQ) & 1, p.status);
-                const uint8_t* tile = sK + ((size_t)s * 8 + jt) * TS;
+                const uint8_t* tile = sK + (size_t)s * SS + (size_t)jt * TB;
                 // this set's groups of the super-tile: g = first, first + TC_NMMA, ... (one copy of the body)
                 const int first = (ds - (st * 8) % TC_NMMA + TC_NMMA) % TC_NMMA;
 #pragma unroll 1
                 for (int g = first; g < 8; g += TC_NMMA) {
                     const int gs = ds * TC_SLOTS + (int)(lc % TC_SLOTS);
                     uint32_t out[32];  // computed before the stage is awaited: a stage is held only for its stores
-                    wmax = __hmax(wmax, dequant_row<BITS, SB_DT>(tile, r16, g, out));
+                    wmax = __hmax(wmax, dequant_row<BITS, SB_DT>(tile, jt * TR, r16, g, out));
                     mbar_wait_sleep(&a_empty[gs], ((lc / TC_SLOTS) & 1) ^ 1, p.status);
                     a_row_store(out, sA + (size_t)gs * TC_STAGE_BYTES, m);
                     fence_proxy_async_smem();
@@ -782,28 +784,32 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// fp16 row-major [rows][cols] tensor, 64 x box_rows boxes, 128-byte swizzle
+// fp16 row-major [rows][cols] tensor viewed as (64 columns of a group, row,
+// group): boxes of 64 x box_rows x (128 / box_rows) groups (one 16 KB B stage),
+// 128-byte swizzle; rows past `rows` read as zeros
 static bool make_tmap(CUtensorMap* m, const void* base, int rows, int cols, int box_rows) {
     auto fn = encode_fn();
     if (!fn) return false;
-    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
-    cuuint32_t es[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+    cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(cols / 64)};
+    cuuint64_t strides[2] = {(cuuint64_t)cols * 2, 128};
+    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)(128 / box_rows)};
+    cuuint32_t es[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// the layer's packed bytes as [rows][128] uint8, boxes of one tile (tile_bytes / 128 rows), 128-byte swizzle
-static bool make_kq_tmap(CUtensorMap* m, const void* layer, size_t layer_bytes, int tile_bytes) {
+// the layer's packed bytes as (128 bytes, 128-byte row, tile of a super-tile):
+// rows 128 bytes apart, the 8 tiles of a super-tile nst * tile_bytes apart;
+// boxes of 128 x (tile_bytes / 128) x 8 -- a whole super-tile -- 128-byte swizzle
+static bool make_kq_tmap(CUtensorMap* m, const void* layer, size_t layer_bytes, int tile_bytes, int nst) {
     auto fn = encode_fn();
     if (!fn) return false;
-    cuuint64_t dims[2] = {128, (cuuint64_t)(layer_bytes / 128)};
-    cuuint64_t strides[1] = {128};
-    cuuint32_t box[2] = {128, (cuuint32_t)(tile_bytes / 128)};
-    cuuint32_t es[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(layer), dims, strides, box, es,
+    cuuint64_t dims[3] = {128, (cuuint64_t)(layer_bytes / 128), 8};
+    cuuint64_t strides[2] = {128, (cuuint64_t)nst * tile_bytes};
+    cuuint32_t box[3] = {128, (cuuint32_t)(tile_bytes / 128), 8};
+    cuuint32_t es[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(layer), dims, strides, box, es,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -930,12 +936,10 @@ extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     }
-    CUtensorMap tkq;
     const uint8_t* layer_base = t->base + (size_t)layer * t->layer_bytes;
     if ((reinterpret_cast<uintptr_t>(layer_base) & 127) || (t->layer_bytes & 127) || (t->expert_bytes & 127) ||
         (t->gateup_bytes & 127) || (t->tb & 127))
         return KQ_ERR_UNSUPPORTED;  // tiles must start on 128-byte rows
-    if (!make_kq_tmap(&tkq, layer_base, t->layer_bytes, (int)t->tb)) return pf_fail("tile tensor map");
     const int max_chunks = E + A / PF_CHUNK + 1;  // live chunks: sum over experts of ceil(n_e / PF_CHUNK)
     TcParams p{};
     p.base = layer_base;
@@ -961,6 +965,8 @@ extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x
         p.nst = Kdim / 512;
         const int items = max_chunks * p.n_mt;  // upper bound; the kernel reads the live count
         const int grid = std::min(items, nsm);
+        CUtensorMap tkq;
+        if (!make_kq_tmap(&tkq, layer_base, t->layer_bytes, (int)t->tb, p.nst)) return pf_fail("tile tensor map");
         CUtensorMap tm[4];
         for (int i = 0; i < 4; ++i)
             if (!make_tmap(&tm[i], src, P, Kdim, boxes[i])) return pf_fail("token tensor map");

@@ -150,6 +150,16 @@ __device__ __forceinline__ void tma_load_2d_hint(void* dst, const void* tmap, in
         : "memory");
 }
 
+// 3D tiled TMA load with an L2 cache policy
+__device__ __forceinline__ void tma_load_3d_hint(void* dst, const void* tmap, int x, int y, int z, uint64_t* bar,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_last() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
