@@ -274,7 +274,9 @@ int kq_router_topk(const float* logits, int T, int E, int K, int32_t* idx, float
  *   x          [T][H] in x_dtype (f16, bf16 or f32)
  *   logits     [T][E] fp32 or NULL.  If given, routing runs first and idx /
  *              weights are OUTPUTS; if NULL they are INPUTS.
- *   idx        [T][K] int32;  weights [T][K] fp32 (may be NULL when out is NULL)
+ *   idx        [T][K] int32;  weights [T][K] fp32 (may be NULL when out is NULL).
+ *              An id of -1 is an empty slot: its output is zero and nothing
+ *              is latched; other ids outside [0, E) latch KQ_DEV_BAD_EXPERT.
  *   out_per_k  [T][K][H] out_dtype, unweighted per-expert outputs, or NULL
  *   out        [T][H] out_dtype: residual + sum_k w_k y_k
  *              (kandiga/metal/moe_block.metal:515-584), or NULL
@@ -516,6 +518,80 @@ int kq_tq_attend(const kq_tq_cache* c, const void* q, int q_dtype, int q_heads, 
  * path of the prefill expert GEMM, exposed for direct checks.  No counterpart
  * in the reference (its prefill matmuls run in Metal / MLX). */
 int kq_gemm_f16_tc(const void* A, const void* B, float* C, int M, int N, int K, void* stream);
+
+/* ---- expert parallelism across the GPUs of one node ---------------------------
+ * The routed experts of a layer are partitioned over `world` ranks (one process,
+ * or one context, per GPU); tokens are data-parallel.  The reference has no
+ * cross-device code: the parallelism this replaces is its per-token loop over
+ * the K experts (kandiga/metal/kandiga_cpu_expert.m:522-543).  Each rank owns an
+ * exchange buffer of the same layout; peers map it (CUDA IPC) and every
+ * transfer is a store into the destination's buffer (no loads from a peer).
+ * A token row travels once to every rank owning one of its experts; that rank
+ * runs the grouped MLP of its experts on all rows it received and sends back
+ * the weighted partial sum; the owner adds residual + partials + shared.
+ * No host synchronisation: counts live on the device and the bounded waits
+ * (default 2 s, kq_ep_set_wait_ns) poll flags that only grow, so a layer's
+ * calls can be captured in a CUDA graph.  Every rank must make the same calls
+ * in the same order.  A wait that gives up latches KQ_DEV_WAIT_TIMEOUT
+ * (kq_ep_status); the ranks stay out of step until every rank's status is
+ * cleared and the buffers are recreated. */
+#define KQ_EP_MAX_RANKS 8
+#define KQ_EP_HANDLE_BYTES 64
+typedef struct kq_ep kq_ep;
+
+/* Bytes of one rank's exchange buffer. */
+size_t kq_ep_buffer_bytes(int world, int max_tokens, int hidden, int top_k);
+/* Allocate this rank's buffer on the current device (the only allocation; all
+ * later calls allocate nothing).  max_tokens: most tokens any rank passes in one
+ * call; x_dtype f16 or bf16 (rows travel and partial sums return in it). */
+int kq_ep_create(int rank, int world, int max_tokens, int hidden, int top_k, int x_dtype, kq_ep** out);
+/* KQ_EP_HANDLE_BYTES describing this rank's buffer to the other processes. */
+int kq_ep_ipc_handle(const kq_ep* ep, void* handle_out);
+/* Map the peers' buffers: handles = world * KQ_EP_HANDLE_BYTES in rank order
+ * (this rank's entry is ignored).  All ranks must connect before any dispatch. */
+int kq_ep_connect(kq_ep* ep, const void* handles);
+/* n contexts of one process on one device, ranks 0..n-1, joined by plain
+ * pointers.  For emulating n ranks on one GPU: issue every rank's dispatch
+ * before any receive, and every return before any combine, on one stream, so
+ * that no wait is ever pending while another launch would satisfy it. */
+int kq_ep_connect_local(kq_ep* const* eps, int n);
+void kq_ep_destroy(kq_ep* ep);
+int kq_ep_set_wait_ns(kq_ep* ep, uint64_t ns);
+
+/* The steps of one layer, in this order, on one stream:
+ *   kq_ep_dispatch  route plan + push rows: x [T][H] (16-byte aligned), idx /
+ *                   weights [T][K] (global expert ids, -1 = empty), owner[E] /
+ *                   local[E] int32 (rank of expert e, its index in that rank's
+ *                   table); T <= max_tokens
+ *   kq_ep_receive   wait for every source; the received rows as a batch of
+ *                   world * max_tokens rows [rows][H] with ids [rows][K] local to
+ *                   this rank (-1 for empty slots) and weights [rows][K]
+ *   kq_ep_compute   kq_moe_prefill (kq_moe_decode below 16 rows) of the local
+ *                   table on that batch, weighted sum into kq_ep_partials()
+ *   kq_ep_return    push each partial row back to its token's owner
+ *   kq_ep_combine   wait for every destination; out [T][H] = residual +
+ *                   sum of partials + gate[t] * shared[t] (gate NULL: 1)
+ * kq_ep_moe issues all five. */
+int kq_ep_dispatch(kq_ep* ep, const void* x, const int32_t* idx, const float* weights, int T,
+                   const int32_t* owner, const int32_t* local, int num_experts, void* stream);
+int kq_ep_receive(kq_ep* ep, void** recv_x, int32_t** recv_idx, float** recv_w, int* rows, void* stream);
+size_t kq_ep_moe_workspace_size(const kq_ep* ep, const kq_table* t);
+int kq_ep_compute(kq_ep* ep, const kq_table* t, int layer, void* workspace, size_t workspace_bytes, void* stream);
+void* kq_ep_partials(kq_ep* ep);
+int kq_ep_return(kq_ep* ep, void* stream);
+int kq_ep_combine(kq_ep* ep, int T, const void* residual, int res_dtype, const void* shared, int shared_dtype,
+                  const float* gate, void* out, int out_dtype, void* stream);
+int kq_ep_moe(kq_ep* ep, const kq_table* t, int layer, const void* x, int T, const int32_t* idx,
+              const float* weights, int num_experts, const int32_t* owner, const int32_t* local,
+              const void* residual, int res_dtype, const void* shared, int shared_dtype, const float* gate,
+              void* out, int out_dtype, void* workspace, size_t workspace_bytes, void* stream);
+/* Status bits (KQ_DEV_*) of this rank's exchange kernels and, in site[4], the
+ * first wait that gave up: (1 receive | 2 combine, source rank, flag value
+ * seen, CTA).  Synchronises the stream. */
+int kq_ep_status(kq_ep* ep, uint32_t* status_out, uint32_t* site_out, void* stream);
+int kq_ep_clear_status(kq_ep* ep, void* stream);
+/* Layer calls issued so far (synchronous read). */
+int kq_ep_calls(kq_ep* ep, uint32_t* calls_out);
 
 #ifdef __cplusplus
 }

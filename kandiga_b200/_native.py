@@ -144,7 +144,33 @@ SIGNATURES = {
     "kq_spill_residency": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "kq_tq_attend_workspace_size": (c_size_t, [c_void_p, c_int]),
     "kq_tq_attend": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    # expert parallelism over peer memory
+    "kq_ep_buffer_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "kq_ep_create": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_void_p)]),
+    "kq_ep_ipc_handle": (c_int, [c_void_p, c_void_p]),
+    "kq_ep_connect": (c_int, [c_void_p, c_void_p]),
+    "kq_ep_connect_local": (c_int, [ctypes.POINTER(c_void_p), c_int]),
+    "kq_ep_destroy": (None, [c_void_p]),
+    "kq_ep_set_wait_ns": (c_int, [c_void_p, ctypes.c_uint64]),
+    "kq_ep_dispatch": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p]),
+    "kq_ep_receive": (c_int, [c_void_p, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p),
+                              ctypes.POINTER(c_void_p), ctypes.POINTER(c_int), c_void_p]),
+    "kq_ep_moe_workspace_size": (c_size_t, [c_void_p, c_void_p]),
+    "kq_ep_compute": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "kq_ep_partials": (c_void_p, [c_void_p]),
+    "kq_ep_return": (c_int, [c_void_p, c_void_p]),
+    "kq_ep_combine": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int,
+                              c_void_p]),
+    "kq_ep_moe": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p,
+                          c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p,
+                          c_size_t, c_void_p]),
+    "kq_ep_status": (c_int, [c_void_p, c_u32p, c_u32p, c_void_p]),
+    "kq_ep_clear_status": (c_int, [c_void_p, c_void_p]),
+    "kq_ep_calls": (c_int, [c_void_p, c_u32p]),
 }
+
+EP_HANDLE_BYTES = 64
+EP_MAX_RANKS = 8
 
 _lib = None
 

@@ -232,9 +232,9 @@ __global__ void __launch_bounds__(NW * 32) qunit_kernel(const GemvParams p) {
         int e = *s_e;
         inv = *s_inv;
         valid = (unsigned)e < (unsigned)p.E;
-        if (!valid) {
-            e = 0;  // a real expert was addressed; rows are zeroed and the condition latched
-            if (tid == 0) set_status(p.status, KQ_DEV_BAD_EXPERT);
+        if (!valid) {  // rows are zeroed; an id other than -1 (an empty slot) is latched
+            if (tid == 0 && e != -1) set_status(p.status, KQ_DEV_BAD_EXPERT);
+            e = 0;         // a real expert is addressed
         }
         mbase += (size_t)e * p.expert_bytes;
     } else {
@@ -388,7 +388,7 @@ __global__ void __launch_bounds__(DOWN_NW * 32, 1) moe_down_kernel(const GemvPar
         }
         quad_reduce(y0, y1);
         const float g = valid ? y0 * inv : 0.f, h = valid ? y1 * inv : 0.f;
-        if (!valid && lane == 0) set_status(p.status, KQ_DEV_BAD_EXPERT);
+        if (!valid && lane == 0 && s_idx[kk] != -1) set_status(p.status, KQ_DEV_BAD_EXPERT);
         if ((lane & 3) == 0) {
             const int r = lane >> 2;
             if (p.out_per_k) {

@@ -59,7 +59,8 @@ constexpr int GROUP_MAX_E = 4096;  // experts per layer the one-CTA grouping sup
 // s_tok = -1 and *n_pos is the padded total.  The order of an expert's
 // assignments inside its segment is unspecified; each position is an
 // independent MMA column, so results do not depend on it.
-// Ids outside [0, E) get inv_pos = -1 and latch KQ_DEV_BAD_EXPERT.
+// Ids outside [0, E) get inv_pos = -1; all but -1 (an empty slot) latch
+// KQ_DEV_BAD_EXPERT.
 __global__ void __launch_bounds__(GROUP_THREADS, 1)
     group_kernel(const int32_t* __restrict__ idx, int A, int K, int E, int chunk, int pad, int* __restrict__ count,
                  int* __restrict__ offset, int32_t* __restrict__ s_tok, int32_t* __restrict__ inv_pos,
@@ -79,7 +80,7 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1)
             inv_pos[a] = atomicAdd(&cnt[v], 1);
         } else {
             inv_pos[a] = -1;
-            set_status(status, KQ_DEV_BAD_EXPERT);
+            if (v != -1) set_status(status, KQ_DEV_BAD_EXPERT);  // -1: an empty slot
         }
     }
     __syncthreads();

@@ -15,10 +15,16 @@ its own tokens).  Per layer and rank:
 6. weighted combine with the residual and the gated shared expert, computed
    on the owner (kq_combine).
 
-The exchanges are NCCL all-to-all-v through torch.distributed (gloo on CPU for
-the host-logic tests).  Router, expert compute and combine are pluggable so the
-same exchange code runs with the GPU kernels or, in CPU tests, with a
-restatement of them.
+Two exchanges implement these steps:
+
+* ``ExpertParallelMoE``: NCCL (or gloo) all-to-all-v through torch.distributed,
+  one row per (token, k) assignment, split sizes read on the host.  Router,
+  expert compute and combine are pluggable, so the same exchange code runs with
+  the GPU kernels or, in CPU tests, with a restatement of them.
+* ``PeerExpertParallelMoE``: the libkq exchange over peer memory (kq_ep_*):
+  one row per (token, destination rank), counts kept on the device, the
+  destination returns the weighted sum of its experts; no host
+  synchronisation, so a whole multi-layer step is one CUDA graph.
 """
 from __future__ import annotations
 
@@ -81,6 +87,10 @@ def zipf_bias(num_experts: int, s: float = 1.1, seed: int = 0) -> np.ndarray:
 
 def _stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
 
 def gpu_router(logits: torch.Tensor, k: int):
@@ -187,3 +197,176 @@ class ExpertParallelMoE:
         if return_parts:
             return out, dict(idx=idx, weights=w, per_k=per_k, send=s_split, recv=r_split)
         return out
+
+
+# ---- exchange over peer memory (kq_ep) --------------------------------------------------------------
+
+class PeerExchange:
+    """This rank's exchange buffer (kq_ep_create): every rank of the group holds
+    one of the same layout and peers store into it directly (CUDA IPC mapping).
+
+    max_tokens: most tokens any rank passes to one layer call; dtype: the token
+    rows' type (fp16 / bf16), also the type partial sums travel back in."""
+
+    def __init__(self, rank: int, world: int, max_tokens: int, hidden: int, top_k: int,
+                 dtype=torch.float16, wait_ns: Optional[int] = None):
+        self.lib = N.load()
+        self.rank, self.world, self.max_tokens, self.hidden, self.top_k = rank, world, max_tokens, hidden, top_k
+        self.dtype = dtype
+        h = ctypes.c_void_p()
+        N.check(self.lib.kq_ep_create(rank, world, max_tokens, hidden, top_k, _DT[dtype], ctypes.byref(h)),
+                "kq_ep_create")
+        self.handle = h
+        if wait_ns is not None:
+            N.check(self.lib.kq_ep_set_wait_ns(h, int(wait_ns)), "kq_ep_set_wait_ns")
+
+    def ipc_handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(N.EP_HANDLE_BYTES)
+        N.check(self.lib.kq_ep_ipc_handle(self.handle, buf), "kq_ep_ipc_handle")
+        return buf.raw
+
+    def connect(self, group=None, gather: Optional[Callable] = None):
+        """Exchange the IPC handles over the process group (all ranks call this),
+        map the peers' buffers, then wait for every rank to have mapped.
+        gather(own_handle) -> every rank's handle in rank order replaces the
+        process-group exchange (and the barrier)."""
+        mine = self.ipc_handle()
+        if gather is None:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, mine, group=group)
+        else:
+            handles = gather(mine)
+        if len(handles) != self.world or any(len(h) != N.EP_HANDLE_BYTES for h in handles):
+            raise N.KQError("kq_ep_connect: malformed handle list")
+        N.check(self.lib.kq_ep_connect(self.handle, b"".join(handles)), "kq_ep_connect")
+        if gather is None:
+            dist.barrier(group=group)
+
+    @staticmethod
+    def connect_local(exchanges):
+        """Join contexts of this process on one device as ranks 0..n-1 (one-GPU emulation)."""
+        arr = (ctypes.c_void_p * len(exchanges))(*[e.handle.value for e in exchanges])
+        N.check(exchanges[0].lib.kq_ep_connect_local(arr, len(exchanges)), "kq_ep_connect_local")
+
+    def status(self):
+        """(KQ_DEV_* bits, (site, source, value seen, CTA) of the first wait that gave up)."""
+        st = ctypes.c_uint32(0)
+        site = (ctypes.c_uint32 * 4)()
+        N.check(self.lib.kq_ep_status(self.handle, ctypes.byref(st), site, _stream()), "kq_ep_status")
+        return st.value, tuple(site)
+
+    def clear_status(self):
+        N.check(self.lib.kq_ep_clear_status(self.handle, _stream()), "kq_ep_clear_status")
+
+    def calls(self) -> int:
+        v = ctypes.c_uint32(0)
+        N.check(self.lib.kq_ep_calls(self.handle, ctypes.byref(v)), "kq_ep_calls")
+        return v.value
+
+    def close(self):
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            self.lib.kq_ep_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class PeerExpertParallelMoE:
+    """Expert-parallel routed MoE through kq_ep: rows cross NVLink as stores into
+    the owners' buffers, counts never leave the device, and a layer is five
+    launches plus the grouped expert MLP (graph-capturable; no host sync).
+
+    placements: one ExpertPlacement for every layer, or a list indexed by layer.
+    table: this rank's ExpertTable whose layer l holds placements[l].experts_of(rank)
+    in local order (extra experts after them, e.g. a shared expert, are allowed)."""
+
+    def __init__(self, placements, rank: int, top_k: int, table, exchange: PeerExchange):
+        self.rank, self.k, self.table, self.ex = rank, top_k, table, exchange
+        self.lib = N.load()
+        self._pl = placements
+        self._maps = {}
+        need = int(self.lib.kq_ep_moe_workspace_size(exchange.handle, table.handle))
+        self.ws = torch.zeros(max(need, 1), dtype=torch.uint8, device="cuda")
+
+    def placement(self, layer: int) -> ExpertPlacement:
+        return self._pl[layer] if isinstance(self._pl, (list, tuple)) else self._pl
+
+    def maps(self, layer: int, dev):
+        key = layer if isinstance(self._pl, (list, tuple)) else 0
+        m = self._maps.get(key)
+        if m is None:
+            pl = self.placement(layer)
+            m = (torch.from_numpy(pl.owner.astype(np.int32)).to(dev),
+                 torch.from_numpy(pl.local.astype(np.int32)).to(dev), len(pl.owner))
+            self._maps[key] = m
+        return m
+
+    def route(self, logits=None, idx=None, weights=None):
+        if logits is not None:
+            return gpu_router(logits, self.k)
+        return idx.to(torch.int32).contiguous(), weights.to(torch.float32).contiguous()
+
+    # the five steps (forward issues them in order; the one-GPU emulation interleaves ranks)
+    def dispatch(self, layer, x, idx, w):
+        owner, local, E = self.maps(layer, x.device)
+        if x.dtype != self.ex.dtype:
+            raise ValueError("x must be in the exchange dtype")
+        N.check(self.lib.kq_ep_dispatch(self.ex.handle, _ptr(x), _ptr(idx), _ptr(w), x.shape[0], _ptr(owner),
+                                        _ptr(local), E, _stream()), "kq_ep_dispatch")
+
+    def receive(self):
+        N.check(self.lib.kq_ep_receive(self.ex.handle, None, None, None, None, _stream()), "kq_ep_receive")
+
+    def compute(self, layer):
+        N.check(self.lib.kq_ep_compute(self.ex.handle, self.table.handle, layer, _ptr(self.ws), self.ws.numel(),
+                                       _stream()), "kq_ep_compute")
+
+    def send_back(self):
+        N.check(self.lib.kq_ep_return(self.ex.handle, _stream()), "kq_ep_return")
+
+    def combine(self, T, residual=None, shared=None, gate=None, out_dtype=torch.float16, out=None):
+        if out is None:
+            out = torch.empty(T, self.ex.hidden, dtype=out_dtype, device="cuda")
+        N.check(self.lib.kq_ep_combine(self.ex.handle, T, _ptr(residual),
+                                       _DT[residual.dtype] if residual is not None else 0, _ptr(shared),
+                                       _DT[shared.dtype] if shared is not None else 0, _ptr(gate), _ptr(out),
+                                       _DT[out.dtype], _stream()), "kq_ep_combine")
+        return out
+
+    def forward(self, layer, x, logits=None, idx=None, weights=None, residual=None, shared=None, gate=None,
+                out_dtype=None, out=None):
+        """out [T, H] = residual + routed MoE of x + gate * shared, for this rank's tokens."""
+        T = x.shape[0]
+        idx, w = self.route(logits, idx, weights)
+        out_dtype = out_dtype or x.dtype
+        if out is None:
+            out = torch.empty(T, self.ex.hidden, dtype=out_dtype, device=x.device)
+        owner, local, E = self.maps(layer, x.device)
+        N.check(self.lib.kq_ep_moe(self.ex.handle, self.table.handle, layer, _ptr(x), T, _ptr(idx), _ptr(w), E,
+                                   _ptr(owner), _ptr(local), _ptr(residual),
+                                   _DT[residual.dtype] if residual is not None else 0, _ptr(shared),
+                                   _DT[shared.dtype] if shared is not None else 0, _ptr(gate), _ptr(out),
+                                   _DT[out.dtype], _ptr(self.ws), self.ws.numel(), _stream()), "kq_ep_moe")
+        return out
+
+
+def emulate_ranks(moes, layer, xs, routes, residuals=None, shareds=None, gates=None, out_dtype=torch.float32):
+    """Run one layer of n emulated ranks (PeerExpertParallelMoE objects joined by
+    PeerExchange.connect_local) on one GPU and one stream: every dispatch, then
+    every receive + compute, then every return, then every combine, so each
+    wait finds its flags already set.  routes[r] = (idx, weights)."""
+    n = len(moes)
+    for r in range(n):
+        moes[r].dispatch(layer, xs[r], *routes[r])
+    for r in range(n):
+        moes[r].receive()
+        moes[r].compute(layer)
+    for r in range(n):
+        moes[r].send_back()
+    return [moes[r].combine(xs[r].shape[0], residual=None if residuals is None else residuals[r],
+                            shared=None if shareds is None else shareds[r],
+                            gate=None if gates is None else gates[r], out_dtype=out_dtype) for r in range(n)]

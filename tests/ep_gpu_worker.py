@@ -1,5 +1,6 @@
 """One rank of the 2-GPU expert-parallel check (run by tests/test_ep_gpu.py under
-torch.distributed.run): EP forward over NCCL against the full layer on one GPU."""
+torch.distributed.run): EP forward over NCCL, then over the peer-memory
+exchange (kq_ep), against the full layer on one GPU."""
 import os
 import sys
 
@@ -47,6 +48,29 @@ def main():
         err = (torch.linalg.norm(out - ref) / torch.linalg.norm(ref)).item()
         print(f"rank {rank} T {T} rel_l2 {err:.3e}", flush=True)
         ok &= err < 2e-3 and local.status() == 0
+    # the same layer through the peer-memory exchange (kq_ep over CUDA IPC)
+    from kandiga_b200.ep import PeerExchange, PeerExpertParallelMoE
+    ex = PeerExchange(rank, world, 40, H, K, torch.float16)
+    ex.connect()
+    pm = PeerExpertParallelMoE(pl, rank, K, local, ex)
+    for T in (3, 40, 0, 17):
+        gt = torch.Generator(device=dev).manual_seed(200 + rank + T)
+        x = torch.randn(T, H, generator=gt, device=dev).half()
+        logits = torch.randn(T, E, generator=gt, device=dev) + torch.from_numpy(zipf_bias(E, 1.1, 7)).to(dev)
+        res = torch.randn(T, H, generator=gt, device=dev)
+        out = pm.forward(0, x, logits=logits, residual=res, out_dtype=torch.float32)
+        st, site = ex.status()
+        if T == 0:
+            ok &= st == 0 and out.shape[0] == 0
+            continue
+        ref = full.moe(0, x, logits=logits, top_k=K, combine=True, residual=res, out_dtype=torch.float32,
+                       path="decode")["out"]
+        err = (torch.linalg.norm(out - ref) / torch.linalg.norm(ref - res)).item()
+        print(f"rank {rank} peer T {T} rel_l2 {err:.3e} status {st} site {site}", flush=True)
+        ok &= err < 2e-3 and st == 0 and local.status() == 0
+    torch.cuda.synchronize()
+    dist.barrier()
+    ex.close()
     flag = torch.tensor([0 if ok else 1], device=dev)
     dist.all_reduce(flag)
     dist.destroy_process_group()
