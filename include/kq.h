@@ -461,9 +461,9 @@ int kq_tq3_dequant(const kq_tq3_mat* m, float* w, void* stream);
 /* ---- TurboQuant KV cache (PolarQuant 3-bit + 1-bit QJL) ----------------------- */
 
 /* A compressed K/V cache of `batch` x `num_heads` x capacity vectors of
- * head_dim (64 or 128) elements.  replaces TurboQuantCache
+ * head_dim elements (1..128; KQ_ERR_UNSUPPORTED above).  replaces TurboQuantCache
  * (kandiga/kv_compress.py:22-57): `rotation` (R, x_rot = x R) and `qjl`
- * (P) are the caller's D x D fp32 host matrices, built as in
+ * (P) are the caller's head_dim x head_dim fp32 host matrices, built as in
  * kandiga/kv_compress.py:34-44.  Per vector the cache holds, for K and for V,
  * one nibble per element (3-bit code << 1 | QJL sign) and fp32 scale and zero
  * (the reference's int8 codes, int8 signs, fp32 scales/zeros, packed). */
@@ -474,6 +474,9 @@ int kq_tq_create(int head_dim, int num_heads, int batch, int capacity, const flo
                  kq_tq_cache** out);
 int kq_tq_destroy(kq_tq_cache* c);
 int kq_tq_seq_len(const kq_tq_cache* c);
+/* Width at which vectors are stored: head_dim rounded up to 64 or 128 (the
+ * packed rows of kq_tq_save / kq_tq_restore hold storage_dim / 2 bytes). */
+int kq_tq_storage_dim(const kq_tq_cache* c);
 int kq_tq_capacity(const kq_tq_cache* c);
 /* Grow the capacity to at least `capacity` vectors per head, keeping the contents. */
 int kq_tq_reserve(kq_tq_cache* c, int capacity, void* stream);
@@ -492,7 +495,7 @@ int kq_tq_export(const kq_tq_cache* c, int which, int8_t* codes, int8_t* signs, 
                  void* stream);
 /* Session persistence of the compressed cache (kandiga/engine.py:1342-1479
  * saves and restores a session's caches).  kq_tq_save copies keys' (which = 0)
- * or values' (1) packed storage, compact: packed [batch][heads][seq_len][head_dim/2]
+ * or values' (1) packed storage, compact: packed [batch][heads][seq_len][storage_dim/2]
  * bytes (two nibbles a byte), scales and zeros fp32 [batch][heads][seq_len]
  * (device).  kq_tq_restore sets the cache to `len` vectors per head from
  * arrays in that layout, growing the capacity if needed. */

@@ -85,7 +85,8 @@ MoeWs moe_ws_layout(const kq_table* t, int T, int K);
 }  // namespace kq
 
 struct kq_tq_cache {
-    int D = 0, H = 0, B = 0, cap = 0, len = 0;
+    int D = 0, H = 0, B = 0, cap = 0, len = 0;  // D: storage width (head_dim rounded up to 64 or 128)
+    int Dr = 0;                                 // head_dim
     float* R = nullptr;              // [D][D] rotation: x_rot = x R
     float* RT = nullptr;             // [D][D] R transposed
     float* P = nullptr;              // [D][D] QJL projection

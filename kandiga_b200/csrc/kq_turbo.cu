@@ -19,6 +19,14 @@
 //   tq_combine_kernel  merges the per-chunk softmax partials and un-rotates
 //                      once per query head: out = (sum p V~) R^T.
 //
+// Any head_dim up to 128 is stored at a width D of 64 or 128: R is extended by
+// the identity and P by zeros on the added dimensions, inputs are read and
+// outputs written at the caller's stride Dr with zeros in the added
+// dimensions, and each vector's min / max run over its Dr dimensions only, so
+// the Dr real codes, scales, zeros, signs, scores and outputs are those of the
+// unpadded arithmetic (an added dimension of x R is 0 and meets a zero row of
+// P, and q R is 0 there, so it enters no score or output).
+//
 // Arithmetic that the reference fixes (kandiga/kv_compress.py:75-88) is done
 // with explicitly rounded operations (no contraction): scale = (max - min) / 7,
 // q = clip(round_half_even((r - min) / scale), 0, 7), dequant = q * scale + min,
@@ -40,6 +48,7 @@ struct TqVecParams {
     const void* src[2];  // append: keys, values [B][H][T][D]
     int dtype;
     int B, H, T, cap, len;  // append: T new tokens written at len; dequant: T = len
+    int Dr;                 // caller's head_dim (<= D; input / output stride)
     const float* R;
     const float* RT;
     const float* P;
@@ -110,9 +119,9 @@ __global__ void __launch_bounds__(TQ_WARPS * 32, 1) tq_append_kernel(TqVecParams
             const long vi = v0 + v;
             if (vi < nvec) {
                 const int which = vi >= per ? 1 : 0;
-                const size_t base = (size_t)(vi - which * per) * D;
+                const size_t base = (size_t)(vi - which * per) * p.Dr;
                 const void* src = which ? p.src[1] : p.src[0];
-                for (int d = lane; d < D; d += 32) xs[v * D + d] = load_as_float(src, p.dtype, base + d);
+                for (int d = lane; d < D; d += 32) xs[v * D + d] = d < p.Dr ? load_as_float(src, p.dtype, base + d) : 0.f;
             } else {
                 for (int d = lane; d < D; d += 32) xs[v * D + d] = 0.f;
             }
@@ -125,11 +134,13 @@ __global__ void __launch_bounds__(TQ_WARPS * 32, 1) tq_append_kernel(TqVecParams
         uint32_t codes[TQ_VPW];
 #pragma unroll
         for (int v = 0; v < TQ_VPW; ++v) {
-            float mn = acc[v][0], mx = acc[v][0];
+            float mn = INFINITY, mx = -INFINITY;  // over the head_dim real dimensions
 #pragma unroll
-            for (int c = 1; c < CPL; ++c) {
-                mn = fminf(mn, acc[v][c]);
-                mx = fmaxf(mx, acc[v][c]);
+            for (int c = 0; c < CPL; ++c) {
+                if (lane * CPL + c < p.Dr) {
+                    mn = fminf(mn, acc[v][c]);
+                    mx = fmaxf(mx, acc[v][c]);
+                }
             }
             mn = warp_min(mn);
             mx = warp_max(mx);
@@ -219,22 +230,23 @@ __global__ void __launch_bounds__(TQ_WARPS * 32, 1) tq_dequant_kernel(TqVecParam
         for (int v = 0; v < TQ_VPW; ++v) {
             const long vi = v0 + v;
             if (vi >= nvec) break;
-            __half* o = p.out + (size_t)vi * D + lane * CPL;
+            __half* o = p.out + (size_t)vi * p.Dr;
 #pragma unroll
-            for (int c = 0; c < CPL; ++c) o[c] = __float2half_rn(acc[v][c]);
+            for (int c = 0; c < CPL; ++c)
+                if (lane * CPL + c < p.Dr) o[lane * CPL + c] = __float2half_rn(acc[v][c]);
         }
         __syncwarp();
     }
 }
 
 __global__ void tq_export_kernel(const uint8_t* __restrict__ packed, const float* __restrict__ scale,
-                                 const float* __restrict__ zero, int D, int BH, int cap, int len, int8_t* codes,
-                                 int8_t* signs, float* scales, float* zeros) {
-    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;  // element index [BH][len][D]
-    const long n = (long)BH * len * D;
+                                 const float* __restrict__ zero, int D, int Dr, int BH, int cap, int len,
+                                 int8_t* codes, int8_t* signs, float* scales, float* zeros) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;  // element index [BH][len][Dr]
+    const long n = (long)BH * len * Dr;
     if (i >= n) return;
-    const long vec = i / D;
-    const int d = (int)(i % D);
+    const long vec = i / Dr;
+    const int d = (int)(i % Dr);
     const size_t slot = (size_t)(vec / len) * cap + (size_t)(vec % len);
     const uint32_t nib = (packed[slot * (D / 2) + d / 2] >> (4 * (d & 1))) & 15u;
     if (codes) codes[i] = (int8_t)(nib >> 1);
@@ -273,6 +285,7 @@ struct TqAttParams {
     const void* q;
     int q_dtype;
     int B, H, G, cap, len, nchunk;
+    int Dr;         // head_dim (q / out stride, softmax scale)
     float* qrot;    // [B][Hq][D + 1]: q R and its sum
     float* part;    // [B][Hq][nchunk][D + 2]: sum p V~ (rotated), chunk max, sum p
     float* scores;  // [B][Hq][len] or null
@@ -291,8 +304,8 @@ __global__ void __launch_bounds__(256) tq_rotate_q_kernel(TqAttParams p) {
     const int qh = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
     const int j = tid % D, half = tid / D;
     const int Hq = p.H * p.G;
-    const size_t qoff = ((size_t)b * Hq + qh) * D;
-    if (tid < D) qs[tid] = load_as_float(p.q, p.q_dtype, qoff + tid);
+    const size_t qoff = ((size_t)b * Hq + qh) * p.Dr;
+    if (tid < D) qs[tid] = tid < p.Dr ? load_as_float(p.q, p.q_dtype, qoff + tid) : 0.f;
     __syncthreads();
     // all of this thread's R loads are issued before the first FMA: one memory round trip
     const int d0 = half * (D / SPLIT);
@@ -375,7 +388,7 @@ __global__ void __launch_bounds__(TQ_ATT_THREADS) tq_attend_kernel(TqAttParams p
         qr[i] = p.qrot[((size_t)b * Hq + (size_t)h * G) * (D + 1) + i];
     __syncthreads();
     mbar_wait(bar, 0, p.status);
-    const float sqrt_d = sqrtf((float)D);
+    const float sqrt_d = sqrtf((float)p.Dr);
 
     // scores on the codes; a thread's 16 query elements stay in registers for all its tokens
     const int npass = (n + TPP - 1) / TPP;
@@ -540,10 +553,10 @@ __global__ void __launch_bounds__(256) tq_combine_kernel(TqAttParams p) {
     for (int k = 0; k < D / KS; ++k) o = fmaf(orot[k0 + k], rt[k], o);
     pacc[hk][d] = o;  // pacc is free again: its sums were read before the barrier above
     __syncthreads();
-    if (tid < D) {
+    if (tid < p.Dr) {
         float v = 0.f;
         for (int h2 = 0; h2 < KS; ++h2) v += pacc[h2][tid];
-        p.out[((size_t)b * Hq + qh) * D + tid] = v;
+        p.out[((size_t)b * Hq + qh) * p.Dr + tid] = v;
     }
 }
 
@@ -647,11 +660,14 @@ extern "C" int kq_tq_create(int head_dim, int num_heads, int batch, int capacity
                             const float* qjl, kq_tq_cache** out) {
     if (!out) return KQ_ERR_ARG;
     *out = nullptr;
-    if ((head_dim != 64 && head_dim != 128) || num_heads <= 0 || batch <= 0 || capacity < 0 || !rotation || !qjl)
-        return KQ_ERR_ARG;
+    if (head_dim <= 0 || num_heads <= 0 || batch <= 0 || capacity < 0 || !rotation || !qjl) return KQ_ERR_ARG;
+    if (head_dim > 128) return KQ_ERR_UNSUPPORTED;
+    const int Dr = head_dim;
+    head_dim = Dr <= 64 ? 64 : 128;  // storage width
     kq_tq_cache* c = new (std::nothrow) kq_tq_cache();
     if (!c) return KQ_ERR_ALLOC;
     c->D = head_dim;
+    c->Dr = Dr;
     c->H = num_heads;
     c->B = batch;
     capacity = round_cap(capacity);
@@ -665,17 +681,27 @@ extern "C" int kq_tq_create(int head_dim, int num_heads, int batch, int capacity
         return KQ_ERR_ALLOC;
     }
     c->cap = capacity;
-    float* rt = new (std::nothrow) float[(size_t)head_dim * head_dim];
-    if (!rt) {
+    // R and P at the storage width: R extended by the identity, P by zeros
+    const size_t nn = (size_t)head_dim * head_dim;
+    float* host = new (std::nothrow) float[3 * nn];
+    if (!host) {
         kq_tq_destroy(c);
         return KQ_ERR_ALLOC;
     }
+    float *r = host, *rt = host + nn, *pj = host + 2 * nn;
     for (int i = 0; i < head_dim; ++i)
-        for (int j = 0; j < head_dim; ++j) rt[(size_t)j * head_dim + i] = rotation[(size_t)i * head_dim + j];
-    const bool up = cudaMemcpy(c->RT, rt, mb, cudaMemcpyHostToDevice) == cudaSuccess;
-    delete[] rt;
-    if (!up || cudaMemcpy(c->R, rotation, mb, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(c->P, qjl, mb, cudaMemcpyHostToDevice) != cudaSuccess) {
+        for (int j = 0; j < head_dim; ++j) {
+            const bool in = i < Dr && j < Dr;
+            r[(size_t)i * head_dim + j] = in ? rotation[(size_t)i * Dr + j] : (i == j ? 1.f : 0.f);
+            pj[(size_t)i * head_dim + j] = in ? qjl[(size_t)i * Dr + j] : 0.f;
+        }
+    for (int i = 0; i < head_dim; ++i)
+        for (int j = 0; j < head_dim; ++j) rt[(size_t)j * head_dim + i] = r[(size_t)i * head_dim + j];
+    const bool up = cudaMemcpy(c->R, r, mb, cudaMemcpyHostToDevice) == cudaSuccess &&
+                    cudaMemcpy(c->RT, rt, mb, cudaMemcpyHostToDevice) == cudaSuccess &&
+                    cudaMemcpy(c->P, pj, mb, cudaMemcpyHostToDevice) == cudaSuccess;
+    delete[] host;
+    if (!up) {
         kq_tq_destroy(c);
         return KQ_ERR_CUDA;
     }
@@ -694,6 +720,7 @@ extern "C" int kq_tq_destroy(kq_tq_cache* c) {
 }
 
 extern "C" int kq_tq_seq_len(const kq_tq_cache* c) { return c ? c->len : -1; }
+extern "C" int kq_tq_storage_dim(const kq_tq_cache* c) { return c ? c->D : -1; }
 extern "C" int kq_tq_capacity(const kq_tq_cache* c) { return c ? c->cap : -1; }
 
 extern "C" int kq_tq_reserve(kq_tq_cache* c, int capacity, void* stream) {
@@ -751,6 +778,7 @@ extern "C" int kq_tq_append(kq_tq_cache* c, const void* keys, const void* values
     p.T = T;
     p.cap = c->cap;
     p.len = c->len;
+    p.Dr = c->Dr;
     p.R = c->R;
     p.P = c->P;
     for (int w = 0; w < 2; ++w) {
@@ -774,6 +802,7 @@ extern "C" int kq_tq_dequant(const kq_tq_cache* c, int which, void* out_f16, voi
     p.H = c->H;
     p.cap = c->cap;
     p.len = c->len;
+    p.Dr = c->Dr;
     p.R = c->R;
     p.RT = c->RT;
     for (int w = 0; w < 2; ++w) {
@@ -792,11 +821,11 @@ extern "C" int kq_tq_export(const kq_tq_cache* c, int which, int8_t* codes, int8
                             float* zeros, void* stream) {
     if (!c || (which != 0 && which != 1)) return KQ_ERR_ARG;
     if (c->len == 0) return KQ_OK;
-    const long n = (long)c->B * c->H * c->len * c->D;
+    const long n = (long)c->B * c->H * c->len * c->Dr;
     const int threads = 256;
     tq_export_kernel<<<(int)((n + threads - 1) / threads), threads, 0, static_cast<cudaStream_t>(stream)>>>(
-        c->packed[which], c->scale[which], c->zero[which], c->D, c->B * c->H, c->cap, c->len, codes, signs, scales,
-        zeros);
+        c->packed[which], c->scale[which], c->zero[which], c->D, c->Dr, c->B * c->H, c->cap, c->len, codes, signs,
+        scales, zeros);
     return cudaGetLastError() == cudaSuccess ? KQ_OK : KQ_ERR_CUDA;
 }
 
@@ -878,6 +907,7 @@ extern "C" int kq_tq_attend(const kq_tq_cache* c, const void* q, int q_dtype, in
     p.cap = c->cap;
     p.len = c->len;
     p.nchunk = nchunk;
+    p.Dr = c->Dr;
     // workspace: status word (16 B), q R, chunk partials
     p.status = static_cast<uint32_t*>(workspace);
     p.qrot = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 16);

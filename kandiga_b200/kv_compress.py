@@ -44,9 +44,10 @@ class TurboQuantCache:
     """Drop-in compressed KV cache: [batch, heads, seq, head_dim] keys and values."""
 
     def __init__(self, head_dim: int, num_heads: int, seed: int = 42, capacity: int = 256, device=None):
-        if head_dim not in (64, 128):
-            raise ValueError("head_dim must be 64 or 128")
+        if not 1 <= head_dim <= 128:
+            raise ValueError("head_dim must be in [1, 128]")
         self.head_dim = head_dim
+        self._dstore = 64 if head_dim <= 64 else 128  # storage width of the packed rows
         self.num_heads = num_heads
         self._seed = seed
         self._capacity0 = max(int(capacity), 1)
@@ -185,7 +186,7 @@ class TurboQuantCache:
         shp = (self._batch, self.num_heads, self.seq_len)
         out = []
         for which in (0, 1):
-            packed = torch.empty(*shp, self.head_dim // 2, dtype=torch.uint8, device=self._device)
+            packed = torch.empty(*shp, self._dstore // 2, dtype=torch.uint8, device=self._device)
             scales = torch.empty(*shp, dtype=torch.float32, device=self._device)
             zeros = torch.empty_like(scales)
             N.check(self._lib.kq_tq_save(self._c, which, ctypes.c_void_p(packed.data_ptr()),
@@ -199,8 +200,8 @@ class TurboQuantCache:
         if len(state) != 6:
             raise ValueError("a TurboQuantCache state holds six arrays")
         kp = torch.as_tensor(state[0])
-        if kp.dim() != 4 or kp.shape[1] != self.num_heads or kp.shape[3] != self.head_dim // 2:
-            raise ValueError(f"packed codes must be [batch, {self.num_heads}, seq, {self.head_dim // 2}]")
+        if kp.dim() != 4 or kp.shape[1] != self.num_heads or kp.shape[3] != self._dstore // 2:
+            raise ValueError(f"packed codes must be [batch, {self.num_heads}, seq, {self._dstore // 2}]")
         b, _, t, _ = kp.shape
         dev = torch.device(device) if device is not None else (self._device or torch.device("cuda"))
         if self._c is None:

@@ -58,6 +58,12 @@ def test_argument_validation_without_device(lib):
     assert lib.kq_moe_decode(None, 0, None, 0, 1, None, None, None, 8, None, None, 0, None, None, 0,
                              None) == 1
     assert lib.kq_qmat_create(100, 512, 3, 0, 0, ctypes.byref(h)) == 1  # rows % 16
+    m = (ctypes.c_float * 4)()
+    assert lib.kq_tq_create(0, 2, 1, 4, m, m, ctypes.byref(h)) == 1     # head_dim 0
+    assert lib.kq_tq_create(200, 2, 1, 4, m, m, ctypes.byref(h)) == 6   # head_dim above 128
+    assert lib.kq_ep_create(0, 9, 16, 1024, 8, 0, ctypes.byref(h)) == 1  # more ranks than KQ_EP_MAX_RANKS
+    assert lib.kq_ep_create(2, 2, 16, 1024, 8, 0, ctypes.byref(h)) == 1  # rank outside the group
+    assert lib.kq_ep_buffer_bytes(2, 16, 1024, 8) > 2 * 2 * 16 * 1024 * 2
     assert lib.bakan_cpu_expert_num_layers(None) == 0
     assert lib.bakan_cpu_expert_mlp_f16(None, 0, None, None, 8, None) == -1
 

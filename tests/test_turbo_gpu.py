@@ -251,3 +251,48 @@ def test_configs3_shape_append_and_attend(gpu):
     # the same query again gives bit-identical results (fixed merge order)
     out2 = cache.attend(torch.from_numpy(q).half().cuda())
     assert torch.equal(out, out2)
+
+
+@pytest.mark.parametrize("d,h,hq,s", [(96, 2, 4, 300), (80, 4, 4, 513), (40, 2, 2, 77)])
+def test_any_head_dim(gpu, d, h, hq, s):
+    """head_dim other than 64 / 128 (the reference takes any, kandiga/kv_compress.py:30-57):
+    the same oracle comparisons for append, reconstruction and attention, and a
+    save / restore round trip of the packed storage."""
+    rng = np.random.RandomState(d + s)
+    b = 1
+    k, v = kv_with_outliers(rng, b, h, s, d)
+    cache = TurboQuantCache(d, h, seed=42, capacity=32)
+    cache.update(torch.from_numpy(k[:, :, :s // 2]).half().cuda(), torch.from_numpy(v[:, :, :s // 2]).half().cuda())
+    cache.update(torch.from_numpy(k[:, :, s // 2:]).half().cuda(), torch.from_numpy(v[:, :, s // 2:]).half().cuda())
+    ref = O.TurboQuantRef(d, h, 42)
+    for which, x, acc in ((0, k, cache.keys), (1, v, cache.values)):
+        xh = x.astype(np.float16).astype(np.float32)
+        q_ref, s_ref, z_ref, g_ref = ref.quantize(xh)
+        codes, scales, zeros, signs = [t.cpu().numpy() for t in cache.export(which)]
+        assert codes.shape == (b, h, s, d)
+        np.testing.assert_allclose(scales, s_ref, rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(zeros, z_ref, rtol=1e-5, atol=1e-5)
+        assert np.mean(codes == q_ref) >= 0.995
+        assert np.max(np.abs(codes.astype(np.int32) - q_ref)) <= 1
+        assert np.mean(signs == g_ref) >= 0.99
+        want = ref.dequantize(codes, scales, zeros, signs).astype(np.float32)
+        got = acc.float().cpu().numpy()
+        assert got.shape == (b, h, s, d) and rel_l2(got, want) < 1e-3
+    q = rng.randn(b, hq, d).astype(np.float32)
+    out, scores = cache.attend(torch.from_numpy(q).half().cuda(), return_scores=True)
+    assert tuple(out.shape) == (b, hq, d)
+    kc = [t.cpu().numpy()[0] for t in cache.export(0)]
+    v_hat = ref.dequantize(*[t.cpu().numpy()[0] for t in cache.export(1)])
+    g = hq // h
+    qh = q[0].astype(np.float16).astype(np.float32)
+    for kv in range(h):
+        sub = O.TurboQuantRef(d, 1, 42)
+        o_ref, s_ref = sub.attend(qh[kv * g:(kv + 1) * g], *(np.repeat(c[kv:kv + 1], g, axis=0) for c in kc),
+                                  np.repeat(v_hat[kv:kv + 1], g, axis=0))
+        got_s = scores[0, kv * g:(kv + 1) * g].cpu().numpy()
+        assert np.max(np.abs(got_s - s_ref)) <= 2e-3 * max(1.0, np.max(np.abs(s_ref)))
+        assert rel_l2(out[0, kv * g:(kv + 1) * g].cpu().numpy(), o_ref) < 2e-3
+    st = cache.state()
+    other = TurboQuantCache(d, h, seed=42)
+    other.load_state(st)
+    assert torch.equal(other.keys, cache.keys) and torch.equal(other.values, cache.values)
