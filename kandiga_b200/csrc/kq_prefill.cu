@@ -230,14 +230,14 @@ struct TcParams {
 constexpr int TC_NMMA = 3;            // MMA-issuing warps = dequantising warp sets (4 warps each)
 constexpr int TC_SLOTS = 2;           // A stages per issuer
 constexpr int TC_NSTAGE = TC_NMMA * TC_SLOTS;  // A stages (one 64-wide group of 128 weight rows each)
-constexpr int TC_NB = 2;              // B stages (16 KB: 16384 / (box * 128) groups of tokens each)
 constexpr int TC_NKQ = 2;             // packed super-tile stages
 constexpr int TC_NDQ = TC_NMMA;
 // Group gi of an item (item-local index) is dequantised by set gi % TC_NMMA
 // into that set's private ring of TC_SLOTS A stages and consumed by the
 // issuer of the same number.  An mbarrier wait tells apart only two phases,
 // so each stage must have exactly one filler and one consumer, in order.
-constexpr int TC_THREADS = 32 * (2 + 4 * TC_NDQ + TC_NMMA + 4);  // producers, dequant, MMA, epilogue
+constexpr int TC_NEPI = 8;            // epilogue warps (TC_NEPI / 4 per TMEM lane quarter)
+constexpr int TC_THREADS = 32 * (2 + 4 * TC_NDQ + TC_NMMA + TC_NEPI);  // producers, dequant, MMA, epilogue
 constexpr int TC_STAGE_BYTES = 16384; // 128 rows x 128 B
 constexpr int TC_TMEM_COLS = 512;     // 2 buffers x 256 (TC_NMMA x 64) columns, or TC_NMMA x 128 for a 128-token box
 static_assert(TC_NMMA * 64 <= 256 && TC_NMMA * 128 <= TC_TMEM_COLS, "accumulators must fit tensor memory");
@@ -257,10 +257,25 @@ __host__ __device__ constexpr int tc_super_slot() {
     return (8 * TileT<BITS>::BYTES + 1023) / 1024 * 1024;
 }
 
+// B stages (16 KB: 16384 / (box * 128) groups of tokens each): as many as shared
+// memory holds beside the A stages and the packed super-tile slots.  A
+// 128-token box fills a stage with one group, and a stage is refilled only
+// after the MMAs that read it retire, so the ring's depth is the number of
+// groups whose (strided, L2- or DRAM-latency) token loads are in flight.
+template <int BITS>
+__host__ __device__ constexpr int tc_nb() {
+    return BITS == 3 ? 4 : 3;
+}
+
 template <int BITS>
 __host__ __device__ constexpr size_t tc_smem_bytes() {
-    return 1024 + (size_t)(TC_NSTAGE + TC_NB) * TC_STAGE_BYTES + (size_t)TC_NKQ * tc_super_slot<BITS>() + 256;
+    return 1024 + (size_t)(TC_NSTAGE + tc_nb<BITS>()) * TC_STAGE_BYTES + (size_t)TC_NKQ * tc_super_slot<BITS>() + 256;
 }
+static_assert(tc_smem_bytes<3>() <= 232448 && tc_smem_bytes<4>() <= 232448, "shared memory per CTA");
+// mbarriers (kq full/empty, A full/empty, B full/empty, D full/empty, drain) and the TMEM slot word
+static_assert((2 * TC_NKQ + 2 * TC_NSTAGE + 2 * tc_nb<3>() + 4 + TC_NMMA) * 8 + 4 <= 256 &&
+                  (2 * TC_NKQ + 2 * TC_NSTAGE + 2 * tc_nb<4>() + 4 + TC_NMMA) * 8 + 4 <= 256,
+              "barrier area");
 
 // 16-byte unit `lane` of 512-byte chunk `chunk` of a swizzled tile whose first
 // 128-byte row is row `row0` of its 1024-aligned slot
@@ -362,6 +377,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     constexpr int TB = TileT<BITS>::BYTES;
     constexpr int TR = TB / 128;             // 128-byte rows per tile
     constexpr int SS = tc_super_slot<BITS>();
+    constexpr int TC_NB = tc_nb<BITS>();
     // 1024-byte aligned in the shared window; an offset from smem_raw keeps the
     // shared address space, so accesses through it compile to shared-memory ops
     uint8_t* sm = smem_raw + ((1024u - ((uint32_t)__cvta_generic_to_shared(smem_raw) & 1023u)) & 1023u);
@@ -388,7 +404,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&d_full[i], TC_NMMA);
-            mbar_init(&d_empty[i], 128);
+            mbar_init(&d_empty[i], 32 * TC_NEPI);
         }
         for (int i = 0; i < TC_NMMA; ++i) mbar_init(&drain[i], 1);
         for (int i = 0; i < TC_NSTAGE; ++i) {
@@ -509,7 +525,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // across both buffers, so it (and the item after it) first waits for
         // the previous item's epilogue.  Issuers without groups in a B stage
         // still wait for and release it, so every barrier sees all issuers.
-        const int mi = warp - MMA_WARP;
+        // The issuer index and the TMEM base pass through a shuffle so the
+        // compiler knows them warp-uniform: the descriptors then live in
+        // uniform registers instead of being moved there for every MMA.
+        const int mi = __shfl_sync(0xffffffffu, warp - MMA_WARP, 0);
+        const uint32_t tmem_u = __shfl_sync(0xffffffffu, tmem, 0);
         const uint32_t leader = lane == 0;
         {
             uint32_t lc = 0, ic = 0, bc = 0;
@@ -527,7 +547,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 prev_full = full;
                 __syncwarp();
                 tc::fence_after_sync();
-                const uint32_t d_tmem = tmem + (full ? (uint32_t)(mi * 128) : (uint32_t)(db * 256 + mi * 64));
+                const uint32_t d_tmem = tmem_u + (full ? (uint32_t)(mi * 128) : (uint32_t)(db * 256 + mi * 64));
                 const uint32_t idesc = tc::idesc_f16(128, it.box, false);
                 for (int g0 = 0; g0 < groups; g0 += gpb, ++bc) {
                     const int bs = bc % TC_NB;
@@ -560,9 +580,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_drain(&drain[mi], 0);
         }
     } else {
-        // ---------------- epilogue (last four warps) ----------------
+        // ---------------- epilogue (last TC_NEPI warps) ----------------
         const int q = warp & 3;         // TMEM lane quarter this warp may access
         const int L = q * 32 + lane;    // accumulator row
+        const int half = (warp - (MMA_WARP + TC_NMMA)) >> 2;  // 16-column chunks half, half + TC_NEPI / 4, ...
         const bool act_scaled = p.mode == 1 && *reinterpret_cast<volatile uint32_t*>(p.act_flag) != 0u;
         uint32_t ic = 0;
         int4 nd = (int)blockIdx.x < n_items ? tc_desc_load(p, blockIdx.x) : make_int4(0, 0, 0, 0);
@@ -575,7 +596,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const bool full = it.box == 128;
             const uint32_t acc_cols = full ? 128u : 64u;
             const uint32_t taddr = tmem + (full ? 0u : (uint32_t)(db * 256)) + ((uint32_t)(q * 32) << 16);
-            for (int c0 = 0; c0 < it.box; c0 += 16) {
+            for (int c0 = half * 16; c0 < it.box; c0 += 16 * (TC_NEPI / 4)) {
                 uint32_t r[16];
                 tc::tmem_ld16(taddr + (uint32_t)c0, r);
 #pragma unroll
@@ -588,31 +609,55 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
                 tc::tmem_ld_wait();
                 if (p.mode == 0) {
+                    // Rows 0..7 of a 16-row tile are gate rows, 8..15 the matching up
+                    // rows.  A gate lane and its up lane (8 lanes apart) swap half of
+                    // their 16 columns, so that each computes 8 activations: the gate
+                    // lane those of columns c0..c0+7, the up lane c0+8..c0+15, both for
+                    // intermediate row irow.
                     const int jt = L >> 4, r16 = L & 15;
+                    const bool gate_lane = r16 < 8;
                     const int irow = it.mt * 64 + jt * 8 + (r16 & 7);
+                    const int nb = c0 + (gate_lane ? 0 : 8);
+                    float a[8];
+                    float amax = 0.f;
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const float v = __uint_as_float(r[i]);
-                        const float u = __shfl_down_sync(0xffffffffu, v, 8);  // up row sits 8 lanes below
-                        const int n = c0 + i;
-                        const bool mine = r16 < 8 && n < it.n;
+                    for (int i = 0; i < 8; ++i) {
+                        const float lo = __uint_as_float(r[i]), hi = __uint_as_float(r[8 + i]);
+                        const float mine_v = gate_lane ? lo : hi;
+                        const float other = __shfl_xor_sync(0xffffffffu, gate_lane ? hi : lo, 8);
+                        const int n = nb + i;
                         const float xi = (p.xinv && n < it.n) ? p.xinv[it.pos0 + n] : 1.f;
-                        float a = mine ? activate(v * xi, u * xi, p.act_kind) : 0.f;
-                        // The warp's 16 activation rows of position n go to fp16 unscaled
-                        // unless one of them reaches 2^15; then all 16 are stored times a
-                        // power of two and the exponent is recorded for act_fixup_kernel.
-                        if (__any_sync(0xffffffffu, fabsf(a) >= 32768.f)) {
-                            const float sc = pow2_scale(warp_max(fabsf(a)));
-                            a *= sc;
-                            if (lane == 0 && n < it.n && sc < 1.f) {
-                                int e = 0;
-                                frexpf(sc, &e);  // sc = 2^(e - 1)
-                                p.act_exp[(size_t)(it.pos0 + n) * (p.I / 16) + it.mt * 4 + q] = (int8_t)(1 - e);
-                                atomicOr(p.act_flag, 1u);
+                        const float g = (gate_lane ? mine_v : other) * xi, u = (gate_lane ? other : mine_v) * xi;
+                        a[i] = n < it.n ? (p.act_kind == KQ_ACT_GELU_TANH ? activate(g, u, p.act_kind)
+                                                                          : __fdividef(g * u, 1.f + __expf(-g)))
+                                        : 0.f;
+                        amax = fmaxf(amax, fabsf(a[i]));
+                    }
+                    // The warp's 16 activation rows of position n go to fp16 unscaled
+                    // unless one of them reaches 2^15; then all 16 are stored times a
+                    // power of two and the exponent is recorded for act_fixup_kernel.
+                    if (__any_sync(0xffffffffu, amax >= 32768.f)) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float mg = warp_max(gate_lane ? fabsf(a[i]) : 0.f);
+                            const float mu = warp_max(gate_lane ? 0.f : fabsf(a[i]));
+                            const float cmax = gate_lane ? mg : mu;  // this column's 16 rows
+                            if (cmax >= 32768.f) {
+                                const float sc = pow2_scale(cmax);
+                                a[i] *= sc;
+                                const int n = nb + i;
+                                if ((lane & 15) == (gate_lane ? 0 : 8) && lane < 16 && n < it.n && sc < 1.f) {
+                                    int e = 0;
+                                    frexpf(sc, &e);  // sc = 2^(e - 1)
+                                    p.act_exp[(size_t)(it.pos0 + n) * (p.I / 16) + it.mt * 4 + q] = (int8_t)(1 - e);
+                                    atomicOr(p.act_flag, 1u);
+                                }
                             }
                         }
-                        if (mine) p.act_s[(size_t)(it.pos0 + n) * p.I + irow] = __float2half_rn(a);
                     }
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        if (nb + i < it.n) p.act_s[(size_t)(it.pos0 + nb + i) * p.I + irow] = __float2half_rn(a[i]);
                 } else {
                     const int hrow = it.mt * 128 + L;
 #pragma unroll
