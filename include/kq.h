@@ -432,8 +432,10 @@ int kq_dense_gemv(const kq_qmat* m, const void* x, int x_dtype, int T, const voi
 /* Re-quantize an MLX-layout affine matrix (rows x cols, group 64; weight
  * bytes [rows][cols*src_bits/8], 16-bit scales/biases [rows][cols/64] in
  * sb_dtype; device) to dst_bits: dequantize each element to the scale dtype,
- * then per group scale = (max - min) / (2^bits - 1), bias = min, both rounded
- * to sb_dtype, code = round_half_even((v - bias) / scale) clipped.  The
+ * then quantize each group as MLX's affine quantizer does (fp32: the edge of
+ * larger magnitude made exactly representable, scale = edge / round(edge /
+ * ((max - min) / (2^bits - 1))), bias = edge; codes from those values; scale
+ * and bias then rounded to sb_dtype; scales may be negative).  The
  * 4-bit -> 3-bit expert repack of scripts/repack_experts_3bit.py:76-103. */
 int kq_requantize_mlx(const void* weight, const void* scales, const void* biases, long rows, int cols, int src_bits,
                       int dst_bits, int sb_dtype, void* weight_out, void* scales_out, void* biases_out,

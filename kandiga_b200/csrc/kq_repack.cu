@@ -8,11 +8,15 @@
 //   dequantize: v = fp32(q * s + b), rounded to the scale dtype (the dequantized
 //               matrix is held in the scale dtype, as the reference's
 //               dequantize returns it);
-//   quantize:   per group, mn = min v, mx = max v, scale = (mx - mn) / (2^bits - 1)
-//               (1 for a constant group), scale and bias = mn rounded to the
-//               scale dtype, q = clip(round_half_even((v - bias) / scale), 0, 2^bits - 1)
-//               with IEEE fp32 subtract and divide -- the affine quantizer the
-//               package uses everywhere (kandiga_b200/quant.py);
+//   quantize:   MLX's affine quantizer per group, in IEEE fp32: mn = min v,
+//               mx = max v, scale = max((mx - mn) / (2^bits - 1), 1e-7), negated
+//               unless |mn| > |mx|; edge = mn if |mn| > |mx| else mx;
+//               q0 = round_half_even(edge / scale); where q0 != 0, scale =
+//               edge / q0 and bias = edge (else bias 0), so the edge of larger
+//               magnitude and zero are exactly representable;
+//               q = clip(round_half_even((v - bias) / scale), 0, 2^bits - 1)
+//               from those fp32 values; scale and bias then rounded to the scale
+//               dtype (the quantizer of kandiga_b200/quant.py, mode "edge");
 //   pack:       MLX layout, fields LSB first: 4-bit = 8 nibbles per uint32,
 //               3-bit = 8 codes per 3 bytes (kandiga/metal/kandiga_cpu_expert.m:194-201,285-291).
 #include "kq_internal.h"
@@ -63,14 +67,19 @@ __global__ void requant_kernel(const uint8_t* __restrict__ w, const uint16_t* __
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     }
     const float nb = (float)((1 << dst_bits) - 1);
-    float scale = __fdiv_rn(__fsub_rn(mx, mn), nb);
-    if (scale == 0.f) scale = 1.f;
-    const uint16_t s16 = sb_bits<SB>(scale), b16 = sb_bits<SB>(mn);
-    float s32 = sb_lo<SB>(s16);
-    if (s32 == 0.f) s32 = 1.f;
-    const float b32 = sb_lo<SB>(b16);
-    const int q0 = (int)fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(v0, b32), s32)), 0.f), nb);
-    const int q1 = (int)fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(v1, b32), s32)), 0.f), nb);
+    float scale = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), nb), 1e-7f);
+    const bool side = fabsf(mn) > fabsf(mx);
+    scale = side ? scale : -scale;
+    const float edge = side ? mn : mx;
+    const float qe = rintf(__fdiv_rn(edge, scale));
+    float bias = 0.f;
+    if (qe != 0.f) {
+        scale = __fdiv_rn(edge, qe);
+        bias = edge;
+    }
+    const uint16_t s16 = sb_bits<SB>(scale), b16 = sb_bits<SB>(bias);
+    const int q0 = (int)fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(v0, bias), scale)), 0.f), nb);
+    const int q1 = (int)fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(v1, bias), scale)), 0.f), nb);
     // lanes 4p..4p+3 hold the 8 codes of pack p (elements 8p..8p+7 of the group)
     uint32_t part = ((uint32_t)q0 << (dst_bits * (2 * (lane & 3)))) | ((uint32_t)q1 << (dst_bits * (2 * (lane & 3) + 1)));
     part |= __shfl_down_sync(0xffffffffu, part, 1);

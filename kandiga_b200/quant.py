@@ -1,10 +1,16 @@
 """MLX-layout affine group quantization on the GPU (torch).
 
-Restates the documented affine scheme of mlx.core.quantize (called by the
-reference at scripts/repack_experts_3bit.py:91-94 and scripts/convert_3bit.py:58):
-per group of 64 columns, bias = min, scale = (max - min) / (2^bits - 1)
-(scale 1 for a constant group), both rounded to the 16-bit storage dtype, then
-q = clip(round_half_even((w - bias) / scale), 0, 2^bits - 1).
+Restates the published affine quantizer of mlx.core.quantize (called by the
+reference at scripts/repack_experts_3bit.py:91-94 and scripts/convert_3bit.py:58).
+Per group of 64 columns, in fp32: scale = max((max - min) / (2^bits - 1), 1e-7),
+negated unless |min| > |max|; edge = the end of larger magnitude; q0 =
+round_half_even(edge / scale); where q0 != 0, scale = edge / q0 and bias = edge
+(else bias 0), so that edge, and zero, are exactly representable; codes
+q = clip(round_half_even((w - bias) / scale), 0, 2^bits - 1) from those fp32
+values, then scale and bias rounded to the 16-bit storage dtype (mode "edge").
+Mode "minmax" is the older formula: bias = min, scale = (max - min) /
+(2^bits - 1) (1 for a constant group), both rounded first, codes from the
+rounded values.
 
 Packing is the MLX byte layout: 3-bit codes LSB-first in 3-byte packs of 8
 (uint8 [rows, cols*3/8], the bytes of MLX's uint32 [rows, cols*3/32]); 4-bit
@@ -21,15 +27,26 @@ def _to_sb(x: torch.Tensor, sb_dtype: str) -> torch.Tensor:
     return x.to(dt)
 
 
-def quantize_affine(w: torch.Tensor, bits: int, group_size: int = 64, sb_dtype: str = "f16"):
+def quantize_affine(w: torch.Tensor, bits: int, group_size: int = 64, sb_dtype: str = "f16", mode: str = "edge"):
     """w [rows, cols] float -> (packed, scales, biases); scales/biases are
     float16 or bfloat16 tensors [rows, cols/group_size]."""
-    assert bits in (3, 4) and w.dim() == 2 and w.shape[1] % group_size == 0
+    assert bits in (3, 4) and w.dim() == 2 and w.shape[1] % group_size == 0 and mode in ("edge", "minmax")
     rows, cols = w.shape
     g = w.float().reshape(rows, cols // group_size, group_size)
     mn = g.amin(-1)
     mx = g.amax(-1)
     nb = float((1 << bits) - 1)
+    if mode == "edge":
+        scale = torch.clamp_min((mx - mn) / nb, 1e-7)
+        side = mn.abs() > mx.abs()
+        scale = torch.where(side, scale, -scale)
+        edge = torch.where(side, mn, mx)
+        q0 = torch.round(edge / scale)
+        nz = q0 != 0
+        scale = torch.where(nz, edge / torch.where(nz, q0, torch.ones_like(q0)), scale)
+        bias = torch.where(nz, edge, torch.zeros_like(edge))
+        q = torch.clamp(torch.round((g - bias[..., None]) / scale[..., None]), 0, nb)
+        return pack_codes(q.to(torch.int64).reshape(rows, cols), bits), _to_sb(scale, sb_dtype), _to_sb(bias, sb_dtype)
     scale = (mx - mn) / nb
     scale = torch.where(scale == 0, torch.ones_like(scale), scale)
     s16 = _to_sb(scale, sb_dtype)

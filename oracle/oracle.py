@@ -10,9 +10,10 @@ project root):
 * C oracle via ctypes (oracle/kq_oracle.c): unpack, affine matvec, expert MLP,
   MoE layer, router top-K, combine.  Pinned bit-for-bit against the
   reference's own scalar C (oracle/_ref, built by oracle/build_ref.py).
-* ``quantize_affine``: MLX-style affine group quantizer (min/max, group 64),
-  restating the documented formula of mlx.core.quantize as called at
-  scripts/repack_experts_3bit.py:91-94 and scripts/convert_3bit.py:52-70.
+* ``quantize_affine``: MLX's affine group quantizer (group 64; the edge
+  selection that makes zero exactly representable, and the older min/max
+  formula as a mode), restating the published algorithm of mlx.core.quantize
+  as called at scripts/repack_experts_3bit.py:91-94 and scripts/convert_3bit.py:52-70.
   MLX is not installed here: quantizer parity is UNPINNED.  Kernel parity does
   not depend on it (kernels and oracle consume the same codes/scales/biases).
 * ``TurboQuantRef``: kandiga/kv_compress.py:30-118 op for op in numpy float32.
@@ -130,20 +131,45 @@ def f32_to_sb(f: np.ndarray, sb_dtype: str) -> np.ndarray:
 # MLX-layout affine quantizer (parity unpinned: MLX is not installed)
 # ---------------------------------------------------------------------------
 
-def quantize_affine(w: np.ndarray, bits: int, gs: int = 64, sb_dtype: str = "f16"):
+def quantize_affine(w: np.ndarray, bits: int, gs: int = 64, sb_dtype: str = "f16", mode: str = "edge"):
     """w [rows, cols] fp32 -> (packed, scales_u16, biases_u16), MLX layout.
 
-    Per group of `gs` columns: bias = min, scale = (max - min) / (2^bits - 1)
-    (scale 1 if the group is constant), both rounded to the storage dtype; then
-    q = clip(round_half_even((w - bias) / scale), 0, 2^bits - 1).
+    mode "edge" restates the published affine quantizer of MLX
+    (mlx.core.quantize, mode "affine"; the call sites are
+    scripts/repack_experts_3bit.py:91-94 and scripts/convert_3bit.py:52-70).
+    Per group of `gs` columns, in fp32:
+      scale = max((max - min) / (2^bits - 1), 1e-7), negated unless |min| > |max|;
+      edge  = min if |min| > |max| else max;
+      q0    = round_half_even(edge / scale);
+      scale = edge / q0 and bias = edge when q0 != 0 (else scale kept, bias 0),
+    so the edge of larger magnitude, and zero with it, are exactly
+    representable; codes q = clip(round_half_even((w - bias) / scale), 0,
+    2^bits - 1) use those fp32 values, and the scale and bias are then rounded
+    to the storage dtype.  Scales are negative for groups whose max has the
+    larger magnitude.
+    mode "minmax": the older formula (bias = min, scale = (max - min) /
+    (2^bits - 1), 1 for a constant group; both rounded to the storage dtype
+    first, and q from the rounded values).
     packed is uint8 [rows, cols*3/8] for 3-bit and uint32 [rows, cols/8] for 4-bit.
     """
     rows, cols = w.shape
-    assert cols % gs == 0
+    assert cols % gs == 0 and mode in ("edge", "minmax")
     g = w.reshape(rows, cols // gs, gs).astype(np.float32)
     mn = g.min(-1)
     mx = g.max(-1)
-    nb = float((1 << bits) - 1)
+    nb = np.float32((1 << bits) - 1)
+    if mode == "edge":
+        with np.errstate(divide="ignore", invalid="ignore"):
+            scale = np.maximum((mx - mn) / nb, np.float32(1e-7)).astype(np.float32)
+            side = np.abs(mn) > np.abs(mx)
+            scale = np.where(side, scale, -scale).astype(np.float32)
+            edge = np.where(side, mn, mx).astype(np.float32)
+            q0 = np.round(edge / scale).astype(np.float32)
+            nz = q0 != 0
+            scale = np.where(nz, edge / np.where(nz, q0, np.float32(1)), scale).astype(np.float32)
+            bias = np.where(nz, edge, np.float32(0)).astype(np.float32)
+            q = np.clip(np.round((g - bias[..., None]) / scale[..., None]), 0, nb).astype(np.uint8)
+        return pack_codes(q.reshape(rows, cols), bits), f32_to_sb(scale, sb_dtype), f32_to_sb(bias, sb_dtype)
     scale = (mx - mn) / nb
     scale = np.where(scale == 0, np.float32(1.0), scale).astype(np.float32)
     s16 = f32_to_sb(scale, sb_dtype)

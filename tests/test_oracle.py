@@ -59,15 +59,48 @@ def test_pack_unpack_roundtrip_vectorised_matches_c():
 def test_quantizer_properties():
     rng = np.random.RandomState(0)
     w = (rng.randn(32, 512) * 0.02).astype(np.float32)
-    w[0, :64] = 0.5  # constant group -> scale 1
+    w[0, :64] = 0.5  # constant group
+    w[1, :64] = 0.0  # all-zero group
     for bits in (3, 4):
-        p, s, b = O.quantize_affine(w, bits, 64, "f16")
+        p, s, b = O.quantize_affine(w, bits, 64, "f16", mode="minmax")
         q = O.unpack_codes(p, bits, 512)
         assert q.max() <= (1 << bits) - 1
         deq = O.dequantize_affine(p, s, b, bits, 512)
         err = np.abs(deq - w).reshape(32, 8, 64).max(-1)
         step = O.sb_to_f32(s, "f16")
         assert (err <= step * 0.5 + 1e-3).all()
+        # MLX's edge selection: the end of larger magnitude, and zero, exact
+        p, s, b = O.quantize_affine(w, bits, 64, "f16")
+        q = O.unpack_codes(p, bits, 512).reshape(32, 8, 64)
+        assert q.max() <= (1 << bits) - 1
+        deq = O.dequantize_affine(p, s, b, bits, 512).reshape(32, 8, 64)
+        step = np.abs(O.sb_to_f32(s, "f16"))
+        err = np.abs(deq - w.reshape(32, 8, 64)).max(-1)
+        assert (err <= step * 1.5 + 1e-3).all()  # the far end may clip by up to half a step more
+        assert np.all(deq[1, 0] == 0) and np.allclose(deq[0, 0], 0.5, rtol=1e-3)
+
+
+def test_quantizer_known_answers():
+    """Groups worked by hand through MLX's affine quantizer (3-bit, fp32 then fp16 storage)."""
+    g = np.zeros((1, 64), np.float32)
+    g[0, 0], g[0, 1], g[0, 2] = -1.0, 0.5, 0.1   # |min| > |max|: edge = min
+    # scale0 = 1.5 / 7; q0 = round(-1 / scale0) = round(-4.67) = -5; scale = -1 / -5 = 0.2; bias = -1
+    p, s, b = O.quantize_affine(g, 3, 64, "f16")
+    assert O.sb_to_f32(s, "f16")[0, 0] == np.float32(np.float16(0.2))
+    assert O.sb_to_f32(b, "f16")[0, 0] == -1.0
+    q = O.unpack_codes(p, 3, 64)[0]
+    # w = -1 -> 0; w = 0.5 -> round(7.5) = 8 -> clipped to 7; w = 0.1 -> round(5.5) = 6;
+    # w = 0 -> 5 (zero exact: 5 * 0.2 - 1 = 0)
+    assert (q[0], q[1], q[2], q[3]) == (0, 7, 6, 5)
+    g2 = -g                                       # |max| > |min|: edge = max, negative scale
+    p, s, b = O.quantize_affine(g2, 3, 64, "f16")
+    assert O.sb_to_f32(s, "f16")[0, 0] == np.float32(np.float16(-0.2))
+    assert O.sb_to_f32(b, "f16")[0, 0] == 1.0
+    q = O.unpack_codes(p, 3, 64)[0]
+    assert (q[0], q[1], q[2], q[3]) == (0, 7, 6, 5)
+    z = np.zeros((1, 64), np.float32)             # all zero: q0 = 0, bias 0, scale -1e-7
+    p, s, b = O.quantize_affine(z, 4, 64, "f16")
+    assert O.sb_to_f32(b, "f16")[0, 0] == 0.0 and np.all(O.unpack_codes(p, 4, 64) == 0)
 
 
 # ---- expert MLP: C oracle vs the reference's scalar C ---------------------------------
