@@ -532,8 +532,11 @@ int kq_gemm_f16_tc(const void* A, const void* B, float* C, int M, int N, int K, 
  * exchange buffer of the same layout; peers map it (CUDA IPC) and every
  * transfer is a store into the destination's buffer (no loads from a peer).
  * A token row travels once to every rank owning one of its experts; that rank
- * runs the grouped MLP of its experts on all rows it received and sends back
- * the weighted partial sum; the owner adds residual + partials + shared.
+ * runs the grouped MLP of its experts on all rows it received and writes the
+ * weighted partial sum straight into the owner's buffer; the owner adds
+ * residual + partials (+ shared).  A shared expert replicated on every rank
+ * can ride along as one more slot of the owner's own segment (top_k of the
+ * context = routed K + 1), so it runs inside the same grouped MLP.
  * No host synchronisation: counts live on the device and the bounded waits
  * (default 2 s, kq_ep_set_wait_ns) poll flags that only grow, so a layer's
  * calls can be captured in a CUDA graph.  Every rank must make the same calls
@@ -548,7 +551,8 @@ typedef struct kq_ep kq_ep;
 size_t kq_ep_buffer_bytes(int world, int max_tokens, int hidden, int top_k);
 /* Allocate this rank's buffer on the current device (the only allocation; all
  * later calls allocate nothing).  max_tokens: most tokens any rank passes in one
- * call; x_dtype f16 or bf16 (rows travel and partial sums return in it). */
+ * call; top_k: slots per row (routed K, + 1 with a shared-expert slot);
+ * x_dtype f16 or bf16 (rows travel and partial sums return in it). */
 int kq_ep_create(int rank, int world, int max_tokens, int hidden, int top_k, int x_dtype, kq_ep** out);
 /* KQ_EP_HANDLE_BYTES describing this rank's buffer to the other processes. */
 int kq_ep_ipc_handle(const kq_ep* ep, void* handle_out);
@@ -565,20 +569,27 @@ int kq_ep_set_wait_ns(kq_ep* ep, uint64_t ns);
 
 /* The steps of one layer, in this order, on one stream:
  *   kq_ep_dispatch  route plan + push rows: x [T][H] (16-byte aligned), idx /
- *                   weights [T][K] (global expert ids, -1 = empty), owner[E] /
- *                   local[E] int32 (rank of expert e, its index in that rank's
- *                   table); T <= max_tokens
+ *                   weights [T][k_route] (global expert ids, -1 = empty),
+ *                   owner[E] / local[E] int32 (rank of expert e, its index in
+ *                   that rank's table); T <= max_tokens.  shared_id >= 0:
+ *                   a shared expert (that local id on every rank) runs as
+ *                   slot k_route of each token's row on its own rank, weighted
+ *                   by shared_w [T] (then k_route + 1 == the context's top_k);
+ *                   shared_id -1: no such slot
  *   kq_ep_receive   wait for every source; the received rows as a batch of
  *                   world * max_tokens rows [rows][H] with ids [rows][K] local to
  *                   this rank (-1 for empty slots) and weights [rows][K]
- *   kq_ep_compute   kq_moe_prefill (kq_moe_decode below 16 rows) of the local
- *                   table on that batch, weighted sum into kq_ep_partials()
- *   kq_ep_return    push each partial row back to its token's owner
+ *   kq_ep_compute   kq_moe_prefill of the local table on that batch, its
+ *                   weighted sums written into the owners' buffers (below 16
+ *                   rows: kq_moe_decode into kq_ep_partials())
+ *   kq_ep_return    release the owners' return flags (below 16 rows: push
+ *                   each partial row back first)
  *   kq_ep_combine   wait for every destination; out [T][H] = residual +
  *                   sum of partials + gate[t] * shared[t] (gate NULL: 1)
  * kq_ep_moe issues all five. */
-int kq_ep_dispatch(kq_ep* ep, const void* x, const int32_t* idx, const float* weights, int T,
-                   const int32_t* owner, const int32_t* local, int num_experts, void* stream);
+int kq_ep_dispatch(kq_ep* ep, const void* x, const int32_t* idx, const float* weights, int T, int k_route,
+                   const int32_t* owner, const int32_t* local, int num_experts, int shared_id,
+                   const float* shared_w, void* stream);
 int kq_ep_receive(kq_ep* ep, void** recv_x, int32_t** recv_idx, float** recv_w, int* rows, void* stream);
 size_t kq_ep_moe_workspace_size(const kq_ep* ep, const kq_table* t);
 int kq_ep_compute(kq_ep* ep, const kq_table* t, int layer, void* workspace, size_t workspace_bytes, void* stream);
@@ -587,9 +598,10 @@ int kq_ep_return(kq_ep* ep, void* stream);
 int kq_ep_combine(kq_ep* ep, int T, const void* residual, int res_dtype, const void* shared, int shared_dtype,
                   const float* gate, void* out, int out_dtype, void* stream);
 int kq_ep_moe(kq_ep* ep, const kq_table* t, int layer, const void* x, int T, const int32_t* idx,
-              const float* weights, int num_experts, const int32_t* owner, const int32_t* local,
-              const void* residual, int res_dtype, const void* shared, int shared_dtype, const float* gate,
-              void* out, int out_dtype, void* workspace, size_t workspace_bytes, void* stream);
+              const float* weights, int k_route, int num_experts, const int32_t* owner, const int32_t* local,
+              int shared_id, const float* shared_w, const void* residual, int res_dtype, const void* shared,
+              int shared_dtype, const float* gate, void* out, int out_dtype, void* workspace,
+              size_t workspace_bytes, void* stream);
 /* Status bits (KQ_DEV_*) of this rank's exchange kernels and, in site[4], the
  * first wait that gave up: (1 receive | 2 combine, source rank, flag value
  * seen, CTA).  Synchronises the stream. */

@@ -153,7 +153,8 @@ SIGNATURES = {
     "kq_ep_connect_local": (c_int, [ctypes.POINTER(c_void_p), c_int]),
     "kq_ep_destroy": (None, [c_void_p]),
     "kq_ep_set_wait_ns": (c_int, [c_void_p, ctypes.c_uint64]),
-    "kq_ep_dispatch": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p]),
+    "kq_ep_dispatch": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_int,
+                               c_void_p, c_void_p]),
     "kq_ep_receive": (c_int, [c_void_p, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p),
                               ctypes.POINTER(c_void_p), ctypes.POINTER(c_int), c_void_p]),
     "kq_ep_moe_workspace_size": (c_size_t, [c_void_p, c_void_p]),
@@ -162,9 +163,9 @@ SIGNATURES = {
     "kq_ep_return": (c_int, [c_void_p, c_void_p]),
     "kq_ep_combine": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int,
                               c_void_p]),
-    "kq_ep_moe": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p,
-                          c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p,
-                          c_size_t, c_void_p]),
+    "kq_ep_moe": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p,
+                          c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int,
+                          c_void_p, c_size_t, c_void_p]),
     "kq_ep_status": (c_int, [c_void_p, c_u32p, c_u32p, c_void_p]),
     "kq_ep_clear_status": (c_int, [c_void_p, c_void_p]),
     "kq_ep_calls": (c_int, [c_void_p, c_u32p]),

@@ -15,7 +15,8 @@
 // Per layer, on the stream of the call:
 //
 //   plan      1 CTA: calls += 1; for each (token t, rank d) whether t has an
-//             expert on d, and its slot pos[t][d] in d's receive segment of
+//             expert on d (with a shared expert, every token also goes to its
+//             own rank), and its slot pos[t][d] in d's receive segment of
 //             this rank (tokens in order); n_out[d]
 //   dispatch  one warp per (t, d) pair: the row x[t] and, per k, the expert's
 //             id local to d (or -1) and its weight, into d's segment; the
@@ -24,10 +25,13 @@
 //   receive   one CTA per source s: wait until data_flag[s] >= calls, then
 //             mark the unused rows of segment s empty (ids -1, weights 0)
 //   compute   the grouped expert MLP of the local table on all segments
-//             (kq_moe_prefill; kq_moe_decode below 16 rows), weighted combine
-//             over the K slots into part[s][row]
-//   return    one warp per received row: part[s][row] into s's ret[t][rank];
-//             the last CTA releases ret_flag[rank] = calls on every s
+//             (kq_moe_prefill), whose weighted combine over the K slots
+//             writes each received row's partial sum straight into its
+//             owner's ret[t][rank] (row destinations built by receive; empty
+//             rows skipped); below 16 rows kq_moe_decode into part[s][row]
+//   return    grouped path: one thread releases ret_flag[rank] = calls on
+//             every s; decode path: one warp per received row copies
+//             part[s][row] into s's ret[t][rank], the last CTA releases
 //   combine   every CTA waits until ret_flag[d] >= calls for all d, then
 //             out[t] = residual[t] + sum_{d: pos[t][d] >= 0} ret[t][d] + shared[t]
 //
@@ -75,7 +79,7 @@ enum : int {
 enum : int { EP_SITE_RECEIVE = 1, EP_SITE_COMBINE = 2 };
 
 struct EpLayout {
-    size_t ctl, pos, recv_tok, recv_idx, recv_w, recv_x, part, ret, total;
+    size_t ctl, pos, recv_tok, recv_idx, recv_w, recv_x, part, ret, rowptr, total;
 };
 
 static EpLayout ep_layout(int world, int T, int H, int K) {
@@ -98,6 +102,8 @@ static EpLayout ep_layout(int world, int T, int H, int K) {
     o = al(o + (size_t)world * T * H * 2);
     L.ret = o;
     o = al(o + (size_t)T * world * H * 2);
+    L.rowptr = o;  // local: destination of each received row's partial sum
+    o = al(o + (size_t)world * T * 8);
     L.total = o;
     return L;
 }
@@ -157,14 +163,15 @@ __device__ bool ep_wait_flag(const uint32_t* flag, uint32_t target, uint64_t wai
 }
 
 // Copy one row of H 16-bit values (H % 8 == 0), one warp, 16-byte accesses,
-// four loads in flight per lane.
+// eight loads in flight per lane (a 6 KB row in two rounds).
 __device__ __forceinline__ void warp_copy_row(const uint4* __restrict__ src, uint4* dst, int n16, int lane) {
-    for (int c = lane; c < n16; c += 128) {
-        uint4 v[4];
+    constexpr int U = 8;
+    for (int c = lane; c < n16; c += 32 * U) {
+        uint4 v[U];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) v[u] = c + 32 * u < n16 ? src[c + 32 * u] : make_uint4(0, 0, 0, 0);
+        for (int u = 0; u < U; ++u) v[u] = c + 32 * u < n16 ? src[c + 32 * u] : make_uint4(0, 0, 0, 0);
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < U; ++u)
             if (c + 32 * u < n16) dst[c + 32 * u] = v[u];
     }
 }
@@ -175,7 +182,8 @@ __device__ __forceinline__ void warp_copy_row(const uint4* __restrict__ src, uin
 // outside [0, E) other than -1 latch KQ_DEV_BAD_EXPERT and are dropped; -1 is
 // an empty slot.
 __global__ void __launch_bounds__(EP_PLAN_THREADS, 1)
-    ep_plan_kernel(EpParams p, const int32_t* __restrict__ idx, int T, const int32_t* __restrict__ owner, int E) {
+    ep_plan_kernel(EpParams p, const int32_t* __restrict__ idx, int T, int k_route, bool self_slot,
+                   const int32_t* __restrict__ owner, int E) {
     __shared__ int wsum[EP_MAXR][32];
     __shared__ int run[EP_MAXR];
     uint32_t* c = ctl(p.self);
@@ -189,8 +197,9 @@ __global__ void __launch_bounds__(EP_PLAN_THREADS, 1)
         const int t = t0 + tid;
         uint32_t mask = 0;
         if (t < T) {
-            for (int k = 0; k < p.K; ++k) {
-                const int e = idx[(size_t)t * p.K + k];
+            if (self_slot) mask = 1u << p.rank;
+            for (int k = 0; k < k_route; ++k) {
+                const int e = idx[(size_t)t * k_route + k];
                 if ((unsigned)e < (unsigned)E) {
                     const int d = owner[e];
                     if ((unsigned)d < (unsigned)p.world) mask |= 1u << d;
@@ -242,8 +251,8 @@ __global__ void __launch_bounds__(EP_PLAN_THREADS, 1)
 // ---- dispatch ------------------------------------------------------------------
 __global__ void __launch_bounds__(EP_THREADS)
     ep_dispatch_kernel(EpParams p, const void* __restrict__ x, const int32_t* __restrict__ idx,
-                       const float* __restrict__ w, int T, const int32_t* __restrict__ owner,
-                       const int32_t* __restrict__ local, int E) {
+                       const float* __restrict__ w, int T, int k_route, const int32_t* __restrict__ owner,
+                       const int32_t* __restrict__ local, int E, int shared_id, const float* __restrict__ shared_w) {
     uint32_t* c = ctl(p.self);
     const int lane = threadIdx.x & 31;
     const int gw = (blockIdx.x * EP_THREADS + threadIdx.x) >> 5, nw = gridDim.x * (EP_THREADS / 32);
@@ -255,19 +264,23 @@ __global__ void __launch_bounds__(EP_THREADS)
         if (slot < 0) continue;
         uint8_t* dst = p.peer[d];
         const size_t row = (size_t)p.rank * p.T_max + slot;  // this rank's segment on d
-        if (lane < p.K) {
-            const int e = idx[(size_t)t * p.K + lane];
+        if (lane < k_route) {
+            const int e = idx[(size_t)t * k_route + lane];
             const bool mine = (unsigned)e < (unsigned)E && owner[e] == d;
             reinterpret_cast<int32_t*>(dst + p.L.recv_idx)[row * p.K + lane] = mine ? local[e] : -1;
-            reinterpret_cast<float*>(dst + p.L.recv_w)[row * p.K + lane] = mine ? w[(size_t)t * p.K + lane] : 0.f;
+            reinterpret_cast<float*>(dst + p.L.recv_w)[row * p.K + lane] = mine ? w[(size_t)t * k_route + lane] : 0.f;
+        } else if (lane < p.K) {  // the shared expert's slot: only in the owner's own segment
+            const bool mine = shared_id >= 0 && d == p.rank;
+            reinterpret_cast<int32_t*>(dst + p.L.recv_idx)[row * p.K + lane] = mine ? shared_id : -1;
+            reinterpret_cast<float*>(dst + p.L.recv_w)[row * p.K + lane] = mine ? shared_w[t] : 0.f;
         }
         if (lane == 0) reinterpret_cast<int32_t*>(dst + p.L.recv_tok)[row] = t;
         warp_copy_row(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + (size_t)t * p.H),
                       reinterpret_cast<uint4*>(dst + p.L.recv_x + row * p.H * 2), n16, lane);
     }
-    __threadfence_system();
-    __syncthreads();
+    __syncthreads();  // the CTA's rows are written; one fence covers them (release is cumulative)
     if (threadIdx.x == 0) {
+        __threadfence_system();
         const uint32_t prev = atomicAdd(c + EPC_DONE_DISP, 1u);
         if (prev == gridDim.x - 1) {  // the last CTA: every row of this call has been written
             __threadfence_system();
@@ -306,6 +319,31 @@ __global__ void __launch_bounds__(EP_THREADS) ep_receive_kernel(EpParams p) {
         ids[i] = -1;
         ws[i] = 0.f;
     }
+    // where each row's partial sum goes: the owner's ret[token][rank] (null: skip)
+    const int32_t* tok = reinterpret_cast<const int32_t*>(p.self + p.L.recv_tok) + (size_t)s * p.T_max;
+    uint8_t** rp = reinterpret_cast<uint8_t**>(p.self + p.L.rowptr) + (size_t)s * p.T_max;
+    for (int j = threadIdx.x; j < p.T_max; j += EP_THREADS) {
+        uint8_t* d = nullptr;
+        if (j < n) {
+            const int t = tok[j];
+            if ((unsigned)t < (unsigned)p.T_max)
+                d = p.peer[s] + p.L.ret + ((size_t)t * p.world + p.rank) * p.H * 2;
+            else
+                atomicOr(c + EPC_STATUS, KQ_DEV_BAD_INDEX);
+        }
+        rp[j] = d;
+    }
+}
+
+// The grouped compute wrote every partial row into its owner's buffer (and
+// fenced): release the return flags.
+__global__ void ep_signal_kernel(EpParams p) {
+    uint32_t* c = ctl(p.self);
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        const uint32_t calls = c[EPC_CALLS];
+        for (int s = 0; s < p.world; ++s) st_release_sys(ctl(p.peer[s]) + EPC_RET_FLAG + p.rank, calls);
+    }
 }
 
 // ---- return --------------------------------------------------------------------
@@ -327,9 +365,9 @@ __global__ void __launch_bounds__(EP_THREADS) ep_return_kernel(EpParams p) {
         warp_copy_row(reinterpret_cast<const uint4*>(p.self + p.L.part + (size_t)r * p.H * 2),
                       reinterpret_cast<uint4*>(dst), n16, lane);
     }
-    __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
+        __threadfence_system();
         const uint32_t prev = atomicAdd(c + EPC_DONE_RET, 1u);
         if (prev == gridDim.x - 1) {
             __threadfence_system();
@@ -405,6 +443,7 @@ struct kq_ep {
     bool opened[EP_MAXR] = {};
     uint64_t wait_ns = 2000000000ull;
     int nsm = 148;
+    bool fused_return = false;  // the last compute wrote the partial rows to their owners
 };
 
 static EpParams ep_params(const kq_ep* ep) {
@@ -522,18 +561,23 @@ extern "C" int kq_ep_set_wait_ns(kq_ep* ep, uint64_t ns) {
 }
 
 extern "C" int kq_ep_dispatch(kq_ep* ep, const void* x, const int32_t* idx, const float* weights, int T,
-                              const int32_t* owner, const int32_t* local, int num_experts, void* stream) {
+                              int k_route, const int32_t* owner, const int32_t* local, int num_experts,
+                              int shared_id, const float* shared_w, void* stream) {
     if (!ep || !ep_connected(ep)) return KQ_ERR_ARG;
     if (T < 0 || T > ep->T_max || num_experts < 1 || !owner || !local) return KQ_ERR_ARG;
+    const bool has_shared = shared_id >= 0;  // the shared expert's slot (its gate per token in shared_w)
+    if (k_route < 1 || k_route + (has_shared ? 1 : 0) != ep->K) return KQ_ERR_ARG;
+    if (has_shared && T > 0 && !shared_w) return KQ_ERR_ARG;
     if (T > 0 && (!x || !idx || !weights)) return KQ_ERR_ARG;
     if (reinterpret_cast<uintptr_t>(x) & 15) return KQ_ERR_ARG;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const EpParams p = ep_params(ep);
-    ep_plan_kernel<<<1, EP_PLAN_THREADS, 0, s>>>(p, idx, T, owner, num_experts);
+    ep_plan_kernel<<<1, EP_PLAN_THREADS, 0, s>>>(p, idx, T, k_route, has_shared, owner, num_experts);
     if (cudaError_t e = cudaGetLastError()) return ep_fail("plan", e);
     const int pairs = T * ep->world, wpb = EP_THREADS / 32;
     const int grid = std::max(1, std::min((pairs + wpb - 1) / wpb, ep->nsm * 8));
-    ep_dispatch_kernel<<<grid, EP_THREADS, 0, s>>>(p, x, idx, weights, T, owner, local, num_experts);
+    ep_dispatch_kernel<<<grid, EP_THREADS, 0, s>>>(p, x, idx, weights, T, k_route, owner, local, num_experts,
+                                                   shared_id, shared_w);
     if (cudaError_t e = cudaGetLastError()) return ep_fail("dispatch", e);
     return KQ_OK;
 }
@@ -555,6 +599,11 @@ extern "C" void* kq_ep_partials(kq_ep* ep) { return ep ? ep->base + ep->L.part :
 extern "C" int kq_ep_return(kq_ep* ep, void* stream) {
     if (!ep || !ep_connected(ep)) return KQ_ERR_ARG;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (ep->fused_return) {
+        ep_signal_kernel<<<1, 32, 0, s>>>(ep_params(ep));
+        if (cudaError_t e = cudaGetLastError()) return ep_fail("signal", e);
+        return KQ_OK;
+    }
     const int rows = ep->world * ep->T_max, wpb = EP_THREADS / 32;
     const int grid = std::max(1, std::min((rows + wpb - 1) / wpb, ep->nsm * 8));
     ep_return_kernel<<<grid, EP_THREADS, 0, s>>>(ep_params(ep));
@@ -599,18 +648,24 @@ extern "C" int kq_ep_compute(kq_ep* ep, const kq_table* t, int layer, void* work
     int32_t* idx = reinterpret_cast<int32_t*>(ep->base + ep->L.recv_idx);
     float* w = reinterpret_cast<float*>(ep->base + ep->L.recv_w);
     void* part = ep->base + ep->L.part;
-    return ep_grouped(ep, t) ? kq_moe_prefill(t, layer, x, ep->x_dtype, rows, nullptr, idx, w, ep->K, nullptr, part,
-                                              ep->x_dtype, nullptr, workspace, workspace_bytes, stream)
-                             : kq_moe_decode(t, layer, x, ep->x_dtype, rows, nullptr, idx, w, ep->K, nullptr, part,
-                                             ep->x_dtype, nullptr, workspace, workspace_bytes, stream);
+    ep->fused_return = ep_grouped(ep, t);
+    if (ep->fused_return)
+        return moe_prefill_ex(t, layer, x, ep->x_dtype, rows, nullptr, idx, w, ep->K, nullptr, nullptr, ep->x_dtype,
+                              nullptr, reinterpret_cast<void* const*>(ep->base + ep->L.rowptr), workspace,
+                              workspace_bytes, stream);
+    return kq_moe_decode(t, layer, x, ep->x_dtype, rows, nullptr, idx, w, ep->K, nullptr, part, ep->x_dtype, nullptr,
+                         workspace, workspace_bytes, stream);
 }
 
 extern "C" int kq_ep_moe(kq_ep* ep, const kq_table* t, int layer, const void* x, int T, const int32_t* idx,
-                         const float* weights, int num_experts, const int32_t* owner, const int32_t* local,
-                         const void* residual, int res_dtype, const void* shared, int shared_dtype, const float* gate,
-                         void* out, int out_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+                         const float* weights, int k_route, int num_experts, const int32_t* owner,
+                         const int32_t* local, int shared_id, const float* shared_w, const void* residual,
+                         int res_dtype, const void* shared, int shared_dtype, const float* gate, void* out,
+                         int out_dtype, void* workspace, size_t workspace_bytes, void* stream) {
     if (!ep || !t) return KQ_ERR_ARG;
-    if (int rc = kq_ep_dispatch(ep, x, idx, weights, T, owner, local, num_experts, stream)) return rc;
+    if (int rc = kq_ep_dispatch(ep, x, idx, weights, T, k_route, owner, local, num_experts, shared_id, shared_w,
+                                stream))
+        return rc;
     if (int rc = kq_ep_receive(ep, nullptr, nullptr, nullptr, nullptr, stream)) return rc;
     if (int rc = kq_ep_compute(ep, t, layer, workspace, workspace_bytes, stream)) return rc;
     if (int rc = kq_ep_return(ep, stream)) return rc;

@@ -45,6 +45,14 @@ int moe_decode_ex(const kq_table* t, int layer, const void* x, int x_dtype, int 
                   const void* residual, const void* norm_w, float eps, void* workspace, size_t workspace_bytes,
                   void* stream);
 
+// kq_moe_prefill whose combined row t goes to out_rows[t] (device array of
+// device addresses, a peer's memory included; null rows skipped; out unused)
+// when out_rows is given.
+int moe_prefill_ex(const kq_table* t, int layer, const void* x, int x_dtype, int T, const float* logits,
+                   int32_t* idx, float* weights, int K, void* out_per_k, void* out, int out_dtype,
+                   const void* residual, void* const* out_rows, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
 // One token: idx/w [K + 1] = top-K of logits[0, E), then (shared_id, sigmoid(logits[E])).
 int route_with_shared(const float* logits, int E, int K, int shared_id, int32_t* idx, float* w, cudaStream_t s);
 

@@ -74,13 +74,32 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1)
     if (tid == 0) *act_flag = 0u;
     for (int e = tid; e < E; e += GROUP_THREADS) cnt[e] = 0;
     __syncthreads();
-    for (int a = tid; a < A; a += GROUP_THREADS) {
-        const int v = idx[a];
-        if ((unsigned)v < (unsigned)E) {
-            inv_pos[a] = atomicAdd(&cnt[v], 1);
-        } else {
-            inv_pos[a] = -1;
-            if (v != -1) set_status(status, KQ_DEV_BAD_EXPERT);  // -1: an empty slot
+    // Eight ids per thread are loaded before any is counted (one CTA: a load
+    // per loop trip would leave it latency-bound), and lanes of a warp with
+    // the same id take their ranks with one shared-memory atomic.  The loop
+    // bound is the warp's (a0 = warp's first index), so every lane reaches the
+    // warp-wide match and shuffle; lanes past A carry id -1.
+    constexpr int GU = 8;
+    for (int a0 = tid - lane; a0 < A; a0 += GROUP_THREADS * GU) {
+        int v[GU];
+#pragma unroll
+        for (int u = 0; u < GU; ++u) {
+            const int a = a0 + lane + u * GROUP_THREADS;
+            v[u] = a < A ? idx[a] : -1;
+        }
+#pragma unroll
+        for (int u = 0; u < GU; ++u) {
+            const int a = a0 + lane + u * GROUP_THREADS;
+            const bool ok = (unsigned)v[u] < (unsigned)E;
+            const unsigned grp = __match_any_sync(0xffffffffu, ok ? v[u] : -1);
+            const int leader = __ffs(grp) - 1;
+            int base = 0;
+            if (ok && lane == leader) base = atomicAdd(&cnt[v[u]], __popc(grp));
+            base = __shfl_sync(0xffffffffu, base, leader);
+            if (a < A) {
+                inv_pos[a] = ok ? base + __popc(grp & ((1u << lane) - 1u)) : -1;
+                if (!ok && v[u] != -1) set_status(status, KQ_DEV_BAD_EXPERT);  // -1: an empty slot
+            }
         }
     }
     __syncthreads();
@@ -138,12 +157,22 @@ __global__ void __launch_bounds__(GROUP_THREADS, 1)
         *n_pos = n_run;
     }
     __syncthreads();
-    for (int a = tid; a < A; a += GROUP_THREADS) {
-        const int r = inv_pos[a];  // written by this thread above
-        if (r < 0) continue;
-        const int pos = off_s[idx[a]] + r;
-        s_tok[pos] = a / K;
-        inv_pos[a] = pos;
+    for (int a0 = tid - lane; a0 < A; a0 += GROUP_THREADS * GU) {
+        int r[GU], v[GU];
+#pragma unroll
+        for (int u = 0; u < GU; ++u) {
+            const int a = a0 + lane + u * GROUP_THREADS;
+            r[u] = a < A ? inv_pos[a] : -1;  // written by this thread above
+            v[u] = a < A ? idx[a] : 0;
+        }
+#pragma unroll
+        for (int u = 0; u < GU; ++u) {
+            if (r[u] < 0) continue;
+            const int a = a0 + lane + u * GROUP_THREADS;
+            const int pos = off_s[v[u]] + r[u];
+            s_tok[pos] = a / K;
+            inv_pos[a] = pos;
+        }
     }
 }
 
@@ -728,34 +757,51 @@ __global__ void act_fixup_kernel(const uint32_t* __restrict__ act_flag, const in
 
 // out[t][h] = [res[t][h]] + sum_k w[t][k] * ys[pos(t,k)][h]; per-k outputs optional.
 // One thread per 4 consecutive h (H % 4 == 0): 16-byte reads of the expert rows.
+// out_rows (optional): row t goes to out_rows[t] (any device address, a
+// peer's memory included; rows with a null pointer are skipped) instead of
+// out + t * H; each CTA then fences once at system scope after a barrier (a
+// release is cumulative over the CTA's writes ordered before it), so a flag
+// released after this kernel covers the rows for a reader on another GPU.
 __global__ void combine_kernel(const float* __restrict__ ys, const int32_t* __restrict__ inv_pos,
                                const float* __restrict__ w, int T, int K, int H, void* out, void* out_per_k,
-                               int out_dtype, const void* residual) {
+                               int out_dtype, const void* residual, void* const* __restrict__ out_rows) {
     const int t = blockIdx.y;
     const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
     pdl_wait();  // the down projection is complete and visible
-    if (t >= T || h >= H) return;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int k = 0; k < K; ++k) {
-        const int pos = inv_pos[(size_t)t * K + k];
-        const float4 y4 = pos >= 0 ? *reinterpret_cast<const float4*>(ys + (size_t)pos * H + h)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float y[4] = {y4.x, y4.y, y4.z, y4.w};
-        if (out_per_k)
+    size_t orow = (size_t)t * H;
+    if (out_rows) {  // uniform over the CTA: one row per blockIdx.y
+        out = t < T ? out_rows[t] : nullptr;
+        orow = 0;
+    }
+    if (t < T && h < H && (out || out_per_k)) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int k = 0; k < K; ++k) {
+            const int pos = inv_pos[(size_t)t * K + k];
+            const float4 y4 = pos >= 0 ? *reinterpret_cast<const float4*>(ys + (size_t)pos * H + h)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float y[4] = {y4.x, y4.y, y4.z, y4.w};
+            if (out_per_k)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) store_from_float(out_per_k, out_dtype, ((size_t)t * K + k) * H + h + j, y[j]);
+                for (int j = 0; j < 4; ++j)
+                    store_from_float(out_per_k, out_dtype, ((size_t)t * K + k) * H + h + j, y[j]);
+            if (out) {
+                const float wk = w[(size_t)t * K + k];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[j] += y[j] * wk;
+            }
+        }
         if (out) {
-            const float wk = w[(size_t)t * K + k];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[j] += y[j] * wk;
+            for (int j = 0; j < 4; ++j) {
+                float v = acc[j];
+                if (residual) v = load_as_float(residual, out_dtype, (size_t)t * H + h + j) + v;
+                store_from_float(out, out_dtype, orow + h + j, v);
+            }
         }
     }
-    if (!out) return;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        float v = acc[j];
-        if (residual) v = load_as_float(residual, out_dtype, (size_t)t * H + h + j) + v;
-        store_from_float(out, out_dtype, (size_t)t * H + h + j, v);
+    if (out_rows) {  // no thread of the CTA has returned above
+        __syncthreads();
+        if (threadIdx.x == 0 && out) __threadfence_system();
     }
 }
 
@@ -926,6 +972,14 @@ extern "C" size_t kq_moe_prefill_workspace_size(const kq_table* t, int max_token
 extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x_dtype, int T, const float* logits,
                               int32_t* idx, float* weights, int K, void* out_per_k, void* out, int out_dtype,
                               const void* residual, void* workspace, size_t workspace_bytes, void* stream) {
+    return kq::moe_prefill_ex(t, layer, x, x_dtype, T, logits, idx, weights, K, out_per_k, out, out_dtype, residual,
+                              nullptr, workspace, workspace_bytes, stream);
+}
+
+int kq::moe_prefill_ex(const kq_table* t, int layer, const void* x, int x_dtype, int T, const float* logits,
+                       int32_t* idx, float* weights, int K, void* out_per_k, void* out, int out_dtype,
+                       const void* residual, void* const* out_rows, void* workspace, size_t workspace_bytes,
+                       void* stream) {
     if (!t) return KQ_ERR_ARG;
     if (layer < 0 || layer >= t->d.num_layers) return KQ_ERR_ARG;
     if (T < 0 || K <= 0 || K > 32 || K > t->d.num_experts) return KQ_ERR_ARG;
@@ -933,8 +987,8 @@ extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x
     if (!x || (x_dtype != KQ_DT_F16 && x_dtype != KQ_DT_BF16 && x_dtype != KQ_DT_F32)) return KQ_ERR_ARG;
     if (out_dtype != KQ_DT_F16 && out_dtype != KQ_DT_BF16 && out_dtype != KQ_DT_F32) return KQ_ERR_ARG;
     if (!logits && !idx) return KQ_ERR_ARG;
-    if (out && !weights && !logits) return KQ_ERR_ARG;
-    if (!out && !out_per_k) return KQ_ERR_ARG;
+    if ((out || out_rows) && !weights && !logits) return KQ_ERR_ARG;
+    if (!out && !out_per_k && !out_rows) return KQ_ERR_ARG;
     if (logits && t->d.num_experts > 1024) return KQ_ERR_UNSUPPORTED;
     if (t->d.num_experts > GROUP_MAX_E) return KQ_ERR_UNSUPPORTED;
     if (t->d.hidden % 512 || t->d.inter % 512) return KQ_ERR_UNSUPPORTED;  // whole 512-wide super-tiles
@@ -1036,7 +1090,7 @@ extern "C" int kq_moe_prefill(const kq_table* t, int layer, const void* x, int x
     // combine / per-k outputs
     dim3 grid((H / 4 + 255) / 256, T);
     return launch_dep(combine_kernel, grid, dim3(256), 0, s, (const float*)ys, (const int32_t*)inv_pos,
-                      (const float*)w_use, T, K, H, out, out_per_k, out_dtype, residual) == cudaSuccess
+                      (const float*)w_use, T, K, H, out, out_per_k, out_dtype, residual, out_rows) == cudaSuccess
                ? KQ_OK
                : KQ_ERR_CUDA;
 }

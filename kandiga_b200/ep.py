@@ -282,10 +282,17 @@ class PeerExpertParallelMoE:
 
     placements: one ExpertPlacement for every layer, or a list indexed by layer.
     table: this rank's ExpertTable whose layer l holds placements[l].experts_of(rank)
-    in local order (extra experts after them, e.g. a shared expert, are allowed)."""
+    in local order (extra experts after them, e.g. a shared expert, are allowed).
+    shared_id: local id of a shared expert held by every rank, run as one more
+    slot of each token's row on its own rank (the exchange then has top_k + 1
+    slots); forward() takes its per-token gate as `shared_gate`."""
 
-    def __init__(self, placements, rank: int, top_k: int, table, exchange: PeerExchange):
+    def __init__(self, placements, rank: int, top_k: int, table, exchange: PeerExchange,
+                 shared_id: Optional[int] = None):
         self.rank, self.k, self.table, self.ex = rank, top_k, table, exchange
+        self.shared_id = shared_id
+        if exchange.top_k != top_k + (0 if shared_id is None else 1):
+            raise ValueError("the exchange's slots must be top_k (+ 1 with a shared expert)")
         self.lib = N.load()
         self._pl = placements
         self._maps = {}
@@ -311,12 +318,15 @@ class PeerExpertParallelMoE:
         return idx.to(torch.int32).contiguous(), weights.to(torch.float32).contiguous()
 
     # the five steps (forward issues them in order; the one-GPU emulation interleaves ranks)
-    def dispatch(self, layer, x, idx, w):
+    def dispatch(self, layer, x, idx, w, shared_gate=None):
         owner, local, E = self.maps(layer, x.device)
         if x.dtype != self.ex.dtype:
             raise ValueError("x must be in the exchange dtype")
-        N.check(self.lib.kq_ep_dispatch(self.ex.handle, _ptr(x), _ptr(idx), _ptr(w), x.shape[0], _ptr(owner),
-                                        _ptr(local), E, _stream()), "kq_ep_dispatch")
+        if (shared_gate is None) != (self.shared_id is None):
+            raise ValueError("shared_gate goes with a shared_id")
+        N.check(self.lib.kq_ep_dispatch(self.ex.handle, _ptr(x), _ptr(idx), _ptr(w), x.shape[0], self.k, _ptr(owner),
+                                        _ptr(local), E, self.shared_id if self.shared_id is not None else -1,
+                                        _ptr(shared_gate), _stream()), "kq_ep_dispatch")
 
     def receive(self):
         N.check(self.lib.kq_ep_receive(self.ex.handle, None, None, None, None, _stream()), "kq_ep_receive")
@@ -338,30 +348,36 @@ class PeerExpertParallelMoE:
         return out
 
     def forward(self, layer, x, logits=None, idx=None, weights=None, residual=None, shared=None, gate=None,
-                out_dtype=None, out=None):
-        """out [T, H] = residual + routed MoE of x + gate * shared, for this rank's tokens."""
+                out_dtype=None, out=None, shared_gate=None):
+        """out [T, H] = residual + routed MoE of x (+ shared_gate * shared expert of x
+        when the object has a shared_id) + gate * shared, for this rank's tokens."""
         T = x.shape[0]
         idx, w = self.route(logits, idx, weights)
         out_dtype = out_dtype or x.dtype
         if out is None:
             out = torch.empty(T, self.ex.hidden, dtype=out_dtype, device=x.device)
         owner, local, E = self.maps(layer, x.device)
-        N.check(self.lib.kq_ep_moe(self.ex.handle, self.table.handle, layer, _ptr(x), T, _ptr(idx), _ptr(w), E,
-                                   _ptr(owner), _ptr(local), _ptr(residual),
+        if (shared_gate is None) != (self.shared_id is None):
+            raise ValueError("shared_gate goes with a shared_id")
+        N.check(self.lib.kq_ep_moe(self.ex.handle, self.table.handle, layer, _ptr(x), T, _ptr(idx), _ptr(w), self.k,
+                                   E, _ptr(owner), _ptr(local),
+                                   self.shared_id if self.shared_id is not None else -1, _ptr(shared_gate),
+                                   _ptr(residual),
                                    _DT[residual.dtype] if residual is not None else 0, _ptr(shared),
                                    _DT[shared.dtype] if shared is not None else 0, _ptr(gate), _ptr(out),
                                    _DT[out.dtype], _ptr(self.ws), self.ws.numel(), _stream()), "kq_ep_moe")
         return out
 
 
-def emulate_ranks(moes, layer, xs, routes, residuals=None, shareds=None, gates=None, out_dtype=torch.float32):
+def emulate_ranks(moes, layer, xs, routes, residuals=None, shareds=None, gates=None, out_dtype=torch.float32,
+                  shared_gates=None):
     """Run one layer of n emulated ranks (PeerExpertParallelMoE objects joined by
     PeerExchange.connect_local) on one GPU and one stream: every dispatch, then
     every receive + compute, then every return, then every combine, so each
     wait finds its flags already set.  routes[r] = (idx, weights)."""
     n = len(moes)
     for r in range(n):
-        moes[r].dispatch(layer, xs[r], *routes[r])
+        moes[r].dispatch(layer, xs[r], *routes[r], shared_gate=None if shared_gates is None else shared_gates[r])
     for r in range(n):
         moes[r].receive()
         moes[r].compute(layer)

@@ -186,3 +186,39 @@ def test_wait_that_nobody_satisfies_times_out(gpu):
     assert dt < 5.0
     exs[0].clear_status()
     assert exs[0].status()[0] == 0
+
+
+@pytest.mark.parametrize("world,Ts", [(2, [24, 9]), (3, [5, 16, 0])])
+def test_shared_expert_as_own_rank_slot(gpu, world, Ts):
+    """A shared expert held by every rank (the last expert of each rank's table)
+    runs as slot K of the token's row on its own rank, weighted by its gate:
+    out = res + sum_k w_k y_k + gate * y_shared, against the oracle with the
+    shared expert as assignment K + 1."""
+    from kandiga_b200.ep import (ExpertPlacement, PeerExchange, PeerExpertParallelMoE, emulate_ranks,
+                                 zipf_bias)
+    E, H, I, K = 12, 1024, 512, 3
+    full = get_layer(3, H, I, E + 1, "f16", seed=85)  # expert E is the shared one
+    pl = ExpertPlacement.balanced(np.exp(zipf_bias(E, 1.1, 5)), world)
+    tabs, moes, exs = [], [], []
+    for r in range(world):
+        ids = np.concatenate([pl.experts_of(r), [E]])
+        sub = O.ExpertLayer(full.bits, H, I, [m[ids] for m in full.w], [m[ids] for m in full.s],
+                            [m[ids] for m in full.b], full.sb_dtype, full.act)
+        tabs.append(make_table(sub))
+        exs.append(PeerExchange(r, world, max(Ts), H, K + 1))
+    PeerExchange.connect_local(exs)
+    for r in range(world):
+        moes.append(PeerExpertParallelMoE(pl, r, K, tabs[r], exs[r], shared_id=len(pl.experts_of(r))))
+    data = [inputs(T, H, E, K, 40 + r) for r, T in enumerate(Ts)]
+    gates = [torch.rand(T, device="cuda") for T in Ts]
+    res = [torch.randn(T, H, device="cuda") for T in Ts]
+    outs = emulate_ranks(moes, 0, [d[0] for d in data], [(d[1], d[2]) for d in data], residuals=res,
+                         out_dtype=torch.float32, shared_gates=gates)
+    for r in range(world):
+        assert exs[r].status()[0] == 0 and tabs[r].status() == 0
+        if Ts[r] == 0:
+            continue
+        idx = np.concatenate([data[r][1].cpu().numpy(), np.full((Ts[r], 1), E, np.int32)], 1)
+        w = np.concatenate([data[r][2].cpu().numpy(), gates[r].cpu().numpy()[:, None]], 1)
+        want = O.combine(full.moe(data[r][0].float().cpu().numpy(), idx), w, None)
+        assert rel_l2((outs[r] - res[r]).cpu().numpy(), want) < RTOL_L2
