@@ -96,14 +96,38 @@ struct Engine {
     size_t dout_bytes = 0;
     int32_t* didx = nullptr;
     size_t didx_bytes = 0;
-    uint32_t* hstatus = nullptr;  // pinned host word the device status is copied into
-    // Single-token calls: pinned staging [x: H*4 | ids: kMaxExperts*4 | out: kMaxExperts*H*4]
-    // and one instantiated CUDA graph per (layer, K, x dtype, out dtype) doing
-    // copy in -> decode kernels -> copy out -> status copy + clear.  The graphs
-    // hold the device buffers' addresses, so any reallocation drops them.
+    uint32_t* hstatus = nullptr;  // pinned, mapped host word the device status is copied into
+    uint32_t* hstatus_d = nullptr;  // its device address
+    // Single-token calls: pinned, mapped staging [x: H*4 | ids: kMaxExperts*4 |
+    // out: kMaxExperts*H*4] and one instantiated CUDA graph per (layer, K, x
+    // dtype, out dtype): a stage-in kernel (x and ids from the mapped stage to
+    // the device), the decode kernels, a stage-out kernel (outputs and the
+    // status word straight into the mapped stage, status cleared).  Kernels
+    // instead of copy-engine nodes: each copy node costs microseconds of
+    // copy-engine latency, which dominated the call.  The graphs hold the
+    // device buffers' addresses, so any reallocation drops them.
     uint8_t* hstage = nullptr;
+    uint8_t* hstage_d = nullptr;  // its device address
     std::map<uint64_t, cudaGraphExec_t> graphs;
 };
+
+// x (n16 16-byte units) and K ids from the mapped host stage to the device.
+__global__ void stage_in_kernel(const uint4* __restrict__ hx, uint4* __restrict__ dx, int n16,
+                                const int32_t* __restrict__ hidx, int32_t* __restrict__ didx, int K) {
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) dx[i] = hx[i];
+    if (threadIdx.x < K) didx[threadIdx.x] = hidx[threadIdx.x];
+}
+
+// outputs (n16 16-byte units) into the mapped host stage; the device status
+// word into its mapped host word, then cleared for the next call.
+__global__ void stage_out_kernel(const uint4* __restrict__ dout, uint4* __restrict__ hout, int n16,
+                                 uint32_t* ws_status, uint32_t* hstatus) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += gridDim.x * blockDim.x) hout[i] = dout[i];
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        *hstatus = *ws_status;
+        *ws_status = 0u;
+    }
+}
 
 void drop_graphs(Engine* e) {
     for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
@@ -136,17 +160,25 @@ size_t ws_need(const Engine* e, int T, int K) {
 
 bool ensure(Engine* e, int T, int K) {
     const int H = e->info.hidden;
-    if (!e->hstatus && cudaHostAlloc(reinterpret_cast<void**>(&e->hstatus), 4, cudaHostAllocDefault) != cudaSuccess) {
-        cudaGetLastError();
-        e->hstatus = nullptr;
-        return false;
+    if (!e->hstatus) {
+        if (cudaHostAlloc(reinterpret_cast<void**>(&e->hstatus), 4, cudaHostAllocMapped) != cudaSuccess ||
+            cudaHostGetDevicePointer(reinterpret_cast<void**>(&e->hstatus_d), e->hstatus, 0) != cudaSuccess) {
+            cudaGetLastError();
+            if (e->hstatus) cudaFreeHost(e->hstatus);
+            e->hstatus = nullptr;
+            return false;
+        }
     }
-    if (!e->hstage && cudaHostAlloc(reinterpret_cast<void**>(&e->hstage),
-                                    (size_t)H * 4 + kMaxExperts * 4 + (size_t)kMaxExperts * H * 4,
-                                    cudaHostAllocDefault) != cudaSuccess) {
-        cudaGetLastError();
-        e->hstage = nullptr;
-        return false;
+    if (!e->hstage) {
+        if (cudaHostAlloc(reinterpret_cast<void**>(&e->hstage),
+                          (size_t)H * 4 + kMaxExperts * 4 + (size_t)kMaxExperts * H * 4,
+                          cudaHostAllocMapped) != cudaSuccess ||
+            cudaHostGetDevicePointer(reinterpret_cast<void**>(&e->hstage_d), e->hstage, 0) != cudaSuccess) {
+            cudaGetLastError();
+            if (e->hstage) cudaFreeHost(e->hstage);
+            e->hstage = nullptr;
+            return false;
+        }
     }
     if (e->dx_bytes < (size_t)T * H * 4 || e->dout_bytes < (size_t)T * K * H * 4 ||
         e->didx_bytes < (size_t)T * K * 4 || T > e->ws_tokens || e->ws_bytes < ws_need(e, T, K))
@@ -273,13 +305,19 @@ int run_one(Engine* e, int layer, const void* x, int x_dtype, const int32_t* idx
             fprintf(stderr, "[kandiga] ERROR: graph capture failed for layer %d\n", layer);
             return -1;
         }
-        bool ok = cudaMemcpyAsync(e->dx, hx, xb, cudaMemcpyHostToDevice, s) == cudaSuccess &&
-                  cudaMemcpyAsync(e->didx, hidx, (size_t)K * 4, cudaMemcpyHostToDevice, s) == cudaSuccess;
+        const uint8_t* hx_d = e->hstage_d;
+        const int32_t* hidx_d = reinterpret_cast<const int32_t*>(e->hstage_d + (size_t)H * 4);
+        uint8_t* hout_d = e->hstage_d + (size_t)H * 4 + kMaxExperts * 4;
+        stage_in_kernel<<<1, 256, 0, s>>>(reinterpret_cast<const uint4*>(hx_d), static_cast<uint4*>(e->dx),
+                                          (int)(xb / 16), hidx_d, e->didx, K);
+        bool ok = cudaGetLastError() == cudaSuccess;
         ok = ok && kq_moe_decode(e->table, layer, e->dx, x_dtype, 1, nullptr, e->didx, nullptr, K, e->dout, nullptr,
                                  out_dtype, nullptr, e->ws, e->ws_bytes, s) == KQ_OK;
-        ok = ok && cudaMemcpyAsync(hout, e->dout, ob, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
-             cudaMemcpyAsync(e->hstatus, e->ws, 4, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
-             cudaMemsetAsync(e->ws, 0, 4, s) == cudaSuccess;
+        if (ok) {
+            stage_out_kernel<<<16, 256, 0, s>>>(static_cast<const uint4*>(e->dout), reinterpret_cast<uint4*>(hout_d),
+                                                (int)(ob / 16), static_cast<uint32_t*>(e->ws), e->hstatus_d);
+            ok = cudaGetLastError() == cudaSuccess;
+        }
         const bool ended = cudaStreamEndCapture(s, &graph) == cudaSuccess;
         cudaGraphExec_t exec = nullptr;
         ok = ok && ended && graph && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
