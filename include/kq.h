@@ -292,12 +292,17 @@ int kq_moe_decode(const kq_table* t, int layer, const void* x, int x_dtype, int 
  * reference.  Scratch is one fixed 8 MiB array inside libkq.so, held by every
  * GPU that loads the library until exit; calls needing more are rejected with
  * KQ_ERR_WORKSPACE.  The first call on a device resolves the array's device
- * address (cudaGetSymbolAddress) and must come before any stream capture.  All
- * calls share the array: overlapping calls on the GPU race.  Allocates nothing;
- * device status bits are not reported.  Arguments as kq_moe_decode. */
+ * address (cudaGetSymbolAddress) and must come before any stream capture; the
+ * stream must belong to the current device (KQ_ERR_ARG otherwise), and a
+ * context reset (cudaDeviceReset) invalidates the cached address.  All calls
+ * share the array: overlapping calls on the GPU race.  Allocates nothing.
+ * Arguments as kq_moe_decode. */
 int kq_moe_decode_static(const kq_table* t, int layer, const void* x, int x_dtype, int T,
                          const float* logits, int32_t* idx, float* weights, int K, void* out_per_k,
                          void* out, int out_dtype, const void* residual, void* stream);
+/* Device status bits (KQ_DEV_*) left by the last kq_moe_decode_static call on
+ * the current device; reads and clears the word (synchronises `stream`). */
+int kq_moe_decode_static_status(uint32_t* status_out, void* stream);
 
 /* Routed-expert decode of n independent single-token items in one persistent
  * launch: item j is row j of x, routed by row j of logits (or idx/weights as

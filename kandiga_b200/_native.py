@@ -103,6 +103,7 @@ SIGNATURES = {
                                     c_void_p, c_size_t, c_void_p]),
     "kq_moe_decode_static": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                      c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "kq_moe_decode_static_status": (c_int, [c_u32p, c_void_p]),
     "kq_qmat_create": (c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_void_p)]),
     "kq_qmat_destroy": (c_int, [c_void_p]),
     "kq_qmat_load_mlx": (c_int, [c_void_p, ctypes.POINTER(kq_mlx_matrix), ctypes.POINTER(kq_mlx_matrix),

@@ -4,7 +4,11 @@ hosts without a device allocator).  Its scratch is a fixed array inside libkq.so
 
 Checked through the C ABI against kq_moe_decode with a caller workspace, on two
 calls in a row with different shapes (the second call must not see the first
-call's leftovers).  This file is collected last on purpose."""
+call's leftovers).  This file is collected last (its name sorts after every
+other test file): the entry point is the most recent addition, so a run that
+stops at the first failure has already run the whole established suite, and
+it exercises the shared static array after other kernels have run in the
+same process.  It also passes run alone in a fresh process."""
 import ctypes
 
 import numpy as np
@@ -67,3 +71,33 @@ def test_static_decode_rejects_oversize(gpu):
     rc = lib.kq_moe_decode_static(t.handle, 0, ctypes.c_void_p(1), N.DT_F16, 1024, None, ctypes.c_void_p(1), None,
                                   16, ctypes.c_void_p(1), None, N.DT_F16, None, None)
     assert rc == 7  # KQ_ERR_WORKSPACE, before any device work
+
+
+def test_static_decode_status_reports_bad_expert(gpu):
+    """An expert id outside the table, passed as input routing, latches
+    KQ_DEV_BAD_EXPERT; kq_moe_decode_static_status reports it and clears it."""
+    from kandiga_b200 import _native as N
+    from kandiga_b200.experts import ExpertTable
+    lib = N.load()
+    E, H, I, K = 8, 2048, 512, 2
+    layer = O.ExpertLayer.random(3, H, I, E, seed=32, sb_dtype="f16")
+    t = ExpertTable(1, E, H, I, 3, "f16")
+    t.load_mlx(0, *[(torch.from_numpy(layer.w[m].reshape(E, layer.w[m].shape[1], -1)).cuda(),
+                     torch.from_numpy(layer.s[m].view(np.int16)).cuda(),
+                     torch.from_numpy(layer.b[m].view(np.int16)).cuda()) for m in range(3)])
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda a: ctypes.c_void_p(a.data_ptr())  # noqa: E731
+    x = torch.randn(1, H, device="cuda").half()
+    idx = torch.tensor([[1, 99]], dtype=torch.int32, device="cuda")
+    w = torch.tensor([[0.5, 0.5]], dtype=torch.float32, device="cuda")
+    out = torch.empty(1, H, dtype=torch.float32, device="cuda")
+    st = ctypes.c_uint32(0)
+    assert lib.kq_moe_decode_static(t.handle, 0, p(x), N.DT_F16, 1, None, p(idx), p(w), K, None, p(out),
+                                    N.DT_F32, None, stream) == 0
+    assert lib.kq_moe_decode_static_status(ctypes.byref(st), stream) == 0
+    assert st.value & N.DEV_BAD_EXPERT
+    assert lib.kq_moe_decode_static_status(ctypes.byref(st), stream) == 0 and st.value == 0  # cleared
+    idx = torch.tensor([[1, 3]], dtype=torch.int32, device="cuda")
+    assert lib.kq_moe_decode_static(t.handle, 0, p(x), N.DT_F16, 1, None, p(idx), p(w), K, None, p(out),
+                                    N.DT_F32, None, stream) == 0
+    assert lib.kq_moe_decode_static_status(ctypes.byref(st), stream) == 0 and st.value == 0
