@@ -490,8 +490,13 @@ int kq_tq_reserve(kq_tq_cache* c, int capacity, void* stream);
 /* Compress T new tokens of keys and values ([batch][heads][T][head_dim] in
  * dtype KQ_DT_*, device) onto the end of the cache: rotate, uniform 3-bit
  * quantize per vector, residual, QJL sign sketch (kandiga/kv_compress.py:59-92,
- * 120-150).  KQ_ERR_CAPACITY if the tokens do not fit. */
+ * 120-150).  KQ_ERR_CAPACITY if the tokens do not fit.  Storage width 128 (head_dim
+ * 65..128): the two D x D products run on the tensor cores (tcgen05, fp16 with
+ * two limbs per operand, ~22 bits); width 64: fp32 FMA chains. */
 int kq_tq_append(kq_tq_cache* c, const void* keys, const void* values, int dtype, int T, void* stream);
+/* Device status bits (KQ_DEV_WAIT_TIMEOUT) latched by the cache's append
+ * kernels (synchronises `stream`). */
+int kq_tq_status(const kq_tq_cache* c, uint32_t* status_out, void* stream);
 /* Reconstruct all cached keys (which = 0) or values (1) as fp16
  * [batch][heads][seq_len][head_dim] (kandiga/kv_compress.py:94-118, 152-168). */
 int kq_tq_dequant(const kq_tq_cache* c, int which, void* out_f16, void* stream);

@@ -125,6 +125,7 @@ SIGNATURES = {
     "kq_tq_destroy": (c_int, [c_void_p]),
     "kq_tq_seq_len": (c_int, [c_void_p]),
     "kq_tq_storage_dim": (c_int, [c_void_p]),
+    "kq_tq_status": (c_int, [c_void_p, c_u32p, c_void_p]),
     "kq_tq_capacity": (c_int, [c_void_p]),
     "kq_tq_reserve": (c_int, [c_void_p, c_int, c_void_p]),
     "kq_tq_append": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),

@@ -101,6 +101,8 @@ struct kq_tq_cache {
     uint8_t* packed[2] = {nullptr, nullptr};  // K, V: [B][H][cap][D/2], nibble = code | sign << 3
     float* scale[2] = {nullptr, nullptr};     // [B][H][cap] (+ 16 floats of tail padding)
     float* zero[2] = {nullptr, nullptr};
+    uint32_t* status = nullptr;      // device word: KQ_DEV_* bits latched by the append kernels
+    uint8_t* tc_ops = nullptr;       // width 128: R^T and P^T as fp16 limb pairs, swizzled (4 x 32 KB)
 };
 
 struct kq_tq3_mat {

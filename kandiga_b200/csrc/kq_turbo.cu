@@ -8,7 +8,10 @@
 //                      in shared memory, 8 vectors per warp share every R/P
 //                      load), per-vector min/max, 3-bit codes, residual,
 //                      residual P, signs; packed as one nibble per element
-//                      (code << 1 | sign) into a preallocated cache.
+//                      (code << 1 | sign) into a preallocated cache.  Used for
+//                      storage width 64 and for small appends.
+//   tq_append_tc_kernel the same for bulk appends at width 128, the two products
+//                      on the tensor cores (see below).
 //   tq_dequant_kernel  the reference's reconstruction ((q s + z) +- s/4) R^T
 //                      -> fp16, for the `keys` / `values` accessors.
 //   tq_attend_kernel   single-query attention straight on the codes, split
@@ -38,6 +41,7 @@
 
 #include "kq_internal.h"
 #include "kq_common.cuh"
+#include "kq_tc.cuh"
 
 namespace kq {
 
@@ -57,6 +61,8 @@ struct TqVecParams {
     float* zero[2];
     __half* out;  // dequant output [B][H][len][D]
     int which;    // dequant: 0 = K, 1 = V
+    uint32_t* status;
+    const uint8_t* tc_ops;  // tensor-core append: the B operand images
 };
 
 __device__ __forceinline__ float warp_min(float v) {
@@ -184,6 +190,237 @@ __global__ void __launch_bounds__(TQ_WARPS * 32, 1) tq_append_kernel(TqVecParams
         }
         __syncwarp();
     }
+}
+
+// ---- append on the tensor cores (storage width 128) -----------------------------------------
+//
+// One CTA of 128 threads per tile of 128 vectors (persistent over tiles).  The
+// two D x D products run as tcgen05 MMAs in fp16 with two limbs per operand:
+// v = v_hi + v_lo (v_hi = fp16(v), v_lo = fp16(v - v_hi)), likewise M, and
+// v M ~ v_hi M_hi + v_hi M_lo + v_lo M_hi (the dropped v_lo M_lo is ~2^-22 of
+// the product), accumulated in fp32 in tensor memory: about 22 bits, so a code
+// or a sign differs from an fp32 evaluation only where a value sits on a
+// rounding boundary.  R^T and P^T (B operands: B[n][k] = M[k][n]) sit in shared
+// memory as fp16 limb pairs for the whole launch; the A stage holds the tile's
+// inputs, then its residuals.  Thread i owns vector i of the tile (TMEM lane i)
+// and does the quantisation with the same explicitly rounded operations as
+// tq_append_kernel.
+constexpr int TQTC_THREADS = 128;
+constexpr int TQTC_D = 128;
+constexpr int TQTC_OP = TQTC_D * TQTC_D * 2;  // one 128 x 128 fp16 operand (two 64-wide K blocks)
+
+__host__ __device__ constexpr size_t tq_tc_smem() { return 1024 + (size_t)6 * TQTC_OP; }
+
+// element (r, k) of a 128 x 128 fp16 operand stored as two swizzled [128 x 64] K blocks
+__device__ __forceinline__ uint32_t tq_op_offset(int r, int k) {
+    return (uint32_t)((k >> 6) * (TQTC_D * 128)) + tc::sw128_offset(r, k & 63);
+}
+
+
+// 8 consecutive values (k0 % 8 == 0) of row r as fp16 hi / lo limbs: one 16-byte store each
+__device__ __forceinline__ void split_store8(uint8_t* hi, uint8_t* lo, int r, int k0, const float* v) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2 hh = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+        const float2 hf = __half22float2(hh);
+        const __half2 ll = __floats2half2_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y);
+        h[i] = *reinterpret_cast<const uint32_t*>(&hh);
+        l[i] = *reinterpret_cast<const uint32_t*>(&ll);
+    }
+    *reinterpret_cast<uint4*>(hi + tq_op_offset(r, k0)) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(lo + tq_op_offset(r, k0)) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// The four B operand images (R^T hi, R^T lo, P^T hi, P^T lo; each 128 x 128 fp16
+// in the swizzled two-block layout), built once per cache.
+__global__ void tq_tc_ops_kernel(const float* __restrict__ RT, const float* __restrict__ P, uint8_t* ops) {
+    const int n = blockIdx.x, k0 = threadIdx.x * 8;  // 128 blocks x 16 threads
+    float r[8], q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        r[i] = RT[(size_t)n * TQTC_D + k0 + i];       // R^T[n][k] = R[k][n]
+        q[i] = P[(size_t)(k0 + i) * TQTC_D + n];     // P^T[n][k] = P[k][n]
+    }
+    split_store8(ops, ops + TQTC_OP, n, k0, r);
+    split_store8(ops + 2 * TQTC_OP, ops + 3 * TQTC_OP, n, k0, q);
+}
+
+// D[lane][n] (+)= sum_k A[lane][k] B[n][k] with the three limb products, one thread issuing
+__device__ __forceinline__ void limb_mma(uint32_t d_tmem, const uint8_t* a_hi, const uint8_t* a_lo,
+                                         const uint8_t* b_hi, const uint8_t* b_lo) {
+    constexpr uint32_t idesc = tc::idesc_f16(128, TQTC_D, false);
+#pragma unroll
+    for (int kc = 0; kc < 2; ++kc) {
+        const uint32_t off = (uint32_t)kc * (TQTC_D * 128);
+        const uint64_t ah = tc::smem_desc_sw128(a_hi + off), al = tc::smem_desc_sw128(a_lo + off);
+        const uint64_t bh = tc::smem_desc_sw128(b_hi + off), bl = tc::smem_desc_sw128(b_lo + off);
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const uint32_t o = 32u * s;
+            tc::mma_f16_ss(d_tmem, tc::desc_advance(ah, o), tc::desc_advance(bh, o), idesc, kc > 0 || s > 0);
+            tc::mma_f16_ss(d_tmem, tc::desc_advance(ah, o), tc::desc_advance(bl, o), idesc, true);
+            tc::mma_f16_ss(d_tmem, tc::desc_advance(al, o), tc::desc_advance(bh, o), idesc, true);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(TQTC_THREADS, 1) tq_append_tc_kernel(TqVecParams p) {
+    extern __shared__ uint8_t tqtc_raw[];
+    uint8_t* sm = tqtc_raw + ((1024u - ((uint32_t)__cvta_generic_to_shared(tqtc_raw) & 1023u)) & 1023u);
+    uint8_t* sRh = sm;  // R^T limbs
+    uint8_t* sRl = sm + TQTC_OP;
+    uint8_t* sPh = sm + 2 * TQTC_OP;  // P^T limbs
+    uint8_t* sPl = sm + 3 * TQTC_OP;
+    uint8_t* sAh = sm + 4 * TQTC_OP;  // inputs, then residuals
+    uint8_t* sAl = sm + 5 * TQTC_OP;
+    __shared__ uint64_t bar;
+    __shared__ uint32_t tmem_slot;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    if (warp == 0) {
+        tc::tmem_alloc(&tmem_slot, 256);
+        tc::tmem_relinquish();
+    }
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();  // the barrier is initialised
+    // the B operand images, once per launch: four 32 KB bulk copies on one mbarrier
+    if (tid == 0) {
+        mbar_expect_tx(&bar, 4 * TQTC_OP);
+        const uint64_t pol = policy_evict_first();
+        for (int i = 0; i < 4; ++i) bulk_g2s(sm + (size_t)i * TQTC_OP, p.tc_ops + (size_t)i * TQTC_OP, TQTC_OP, &bar, pol);
+    }
+    mbar_wait(&bar, 0, p.status);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const long per = (long)p.B * p.H * p.T;
+    const long nvec = 2 * per;
+    const long ntiles = (nvec + 127) / 128;
+    uint32_t phase = 1;  // phase 0 was the operand copy
+    for (long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const long vi = tile * 128 + tid;
+        const bool live = vi < nvec;
+        const int which = live && vi >= per ? 1 : 0;
+        const long r = vi - which * per;  // (b H + h) T + t
+        // stage this thread's vector (zeros past head_dim and past the last vector),
+        // 8 values per step; 16-byte loads when the row allows them
+        {
+            const void* src = which ? p.src[1] : p.src[0];
+            const size_t base = live ? (size_t)r * p.Dr : 0;
+            const int esz = p.dtype == KQ_DT_F32 ? 4 : 2;
+            const bool vec = live && p.Dr == TQTC_D && p.dtype != KQ_DT_F32 &&
+                             ((reinterpret_cast<uintptr_t>(src) + base * esz) & 15) == 0;
+#pragma unroll 2
+            for (int k0 = 0; k0 < TQTC_D; k0 += 8) {
+                float v[8];
+                if (vec) {
+                    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(src) + (base + k0) * 2);
+                    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 f = p.dtype == KQ_DT_F16
+                                             ? __half22float2(*reinterpret_cast<const __half2*>(&w[i]))
+                                             : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+                        v[2 * i] = f.x;
+                        v[2 * i + 1] = f.y;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        v[i] = live && k0 + i < p.Dr ? load_as_float(src, p.dtype, base + k0 + i) : 0.f;
+                }
+                split_store8(sAh, sAl, tid, k0, v);
+            }
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            tc::fence_after_sync();
+            limb_mma(tmem, sAh, sAl, sRh, sRl);  // rotated = x R  -> columns [0, 128)
+            tc::mma_commit(&bar);
+        }
+        mbar_wait(&bar, phase, p.status);
+        phase ^= 1u;
+        tc::fence_after_sync();
+        // min / max over the head_dim real dimensions
+        float mn = INFINITY, mx = -INFINITY;
+        for (int c0 = 0; c0 < TQTC_D; c0 += 16) {
+            uint32_t a[16];
+            tc::tmem_ld16(tmem + lane_base + (uint32_t)c0, a);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (c0 + j < p.Dr) {
+                    mn = fminf(mn, __uint_as_float(a[j]));
+                    mx = fmaxf(mx, __uint_as_float(a[j]));
+                }
+        }
+        float scale = __fdiv_rn(__fsub_rn(mx, mn), 7.f);
+        if (scale == 0.f) scale = 1.f;
+        // codes and residuals (the residual overwrites the staged input)
+        uint32_t cw[TQTC_D / 8];
+#pragma unroll
+        for (int c0 = 0; c0 < TQTC_D; c0 += 16) {
+            uint32_t a[16];
+            tc::tmem_ld16(tmem + lane_base + (uint32_t)c0, a);
+            tc::tmem_ld_wait();
+            uint32_t w0 = 0, w1 = 0;
+            float res[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const float v = __uint_as_float(a[j]);
+                float q = rintf(__fdiv_rn(__fsub_rn(v, mn), scale));
+                q = fminf(fmaxf(q, 0.f), 7.f);
+                const float deq = __fadd_rn(__fmul_rn(q, scale), mn);
+                res[j] = __fsub_rn(v, deq);
+                if (j < 8) w0 |= (uint32_t)q << (4 * j + 1);
+                else w1 |= (uint32_t)q << (4 * (j - 8) + 1);
+            }
+            split_store8(sAh, sAl, tid, c0, res);
+            split_store8(sAh, sAl, tid, c0 + 8, res + 8);
+            cw[c0 / 8] = w0;
+            cw[c0 / 8 + 1] = w1;
+        }
+        tc::fence_before_sync();
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            tc::fence_after_sync();
+            limb_mma(tmem + 128, sAh, sAl, sPh, sPl);  // residual P -> columns [128, 256)
+            tc::mma_commit(&bar);
+        }
+        mbar_wait(&bar, phase, p.status);
+        phase ^= 1u;
+        tc::fence_after_sync();
+#pragma unroll
+        for (int c0 = 0; c0 < TQTC_D; c0 += 16) {
+            uint32_t a[16];
+            tc::tmem_ld16(tmem + lane_base + 128u + (uint32_t)c0, a);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (__uint_as_float(a[j]) > 0.f) cw[(c0 + j) / 8] |= 1u << (4 * ((c0 + j) & 7));
+        }
+        if (live) {
+            const size_t slot = (size_t)(r / p.T) * p.cap + p.len + (size_t)(r % p.T);
+            uint4* dst = reinterpret_cast<uint4*>((which ? p.packed[1] : p.packed[0]) + slot * (TQTC_D / 2));
+#pragma unroll
+            for (int i = 0; i < TQTC_D / 32; ++i) dst[i] = make_uint4(cw[4 * i], cw[4 * i + 1], cw[4 * i + 2], cw[4 * i + 3]);
+            (which ? p.scale[1] : p.scale[0])[slot] = scale;
+            (which ? p.zero[1] : p.zero[0])[slot] = mn;
+        }
+        tc::fence_before_sync();
+        __syncthreads();  // the A stage and the accumulators are free for the next tile
+        tc::fence_after_sync();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tmem, 256);
 }
 
 template <int D>
@@ -627,6 +864,16 @@ static cudaError_t launch_append(const TqVecParams& p, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+static cudaError_t launch_append_tc(const TqVecParams& p, cudaStream_t s) {
+    static int configured[64] = {0};
+    cudaError_t e = smem_attr_once(tq_append_tc_kernel, tq_tc_smem(), configured);
+    if (e != cudaSuccess) return e;
+    const long ntiles = (2L * p.B * p.H * p.T + 127) / 128;
+    const int grid = (int)std::min<long>(ntiles, (long)sm_count());
+    tq_append_tc_kernel<<<grid, TQTC_THREADS, tq_tc_smem(), s>>>(p);
+    return cudaGetLastError();
+}
+
 template <int D>
 static cudaError_t launch_dequant(const TqVecParams& p, cudaStream_t s) {
     static int configured[64] = {0};
@@ -673,10 +920,12 @@ extern "C" int kq_tq_create(int head_dim, int num_heads, int batch, int capacity
     capacity = round_cap(capacity);
     const size_t mb = (size_t)head_dim * head_dim * 4;
     if (cudaMalloc(&c->R, mb) != cudaSuccess || cudaMalloc(&c->RT, mb) != cudaSuccess ||
-        cudaMalloc(&c->P, mb) != cudaSuccess || !alloc_planes(c, capacity, c->packed, c->scale, c->zero)) {
+        cudaMalloc(&c->P, mb) != cudaSuccess || cudaMalloc(&c->status, 4) != cudaSuccess ||
+        cudaMemset(c->status, 0, 4) != cudaSuccess || !alloc_planes(c, capacity, c->packed, c->scale, c->zero)) {
         cudaFree(c->R);
         cudaFree(c->RT);
         cudaFree(c->P);
+        cudaFree(c->status);
         delete c;
         return KQ_ERR_ALLOC;
     }
@@ -705,6 +954,18 @@ extern "C" int kq_tq_create(int head_dim, int num_heads, int batch, int capacity
         kq_tq_destroy(c);
         return KQ_ERR_CUDA;
     }
+    if (head_dim == TQTC_D) {  // the tensor-core append's operand images
+        if (cudaMalloc(&c->tc_ops, 4 * (size_t)TQTC_OP) != cudaSuccess) {
+            c->tc_ops = nullptr;
+            kq_tq_destroy(c);
+            return KQ_ERR_ALLOC;
+        }
+        tq_tc_ops_kernel<<<TQTC_D, TQTC_D / 8>>>(c->RT, c->P, c->tc_ops);
+        if (cudaGetLastError() != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+            kq_tq_destroy(c);
+            return KQ_ERR_CUDA;
+        }
+    }
     *out = c;
     return KQ_OK;
 }
@@ -715,7 +976,18 @@ extern "C" int kq_tq_destroy(kq_tq_cache* c) {
     cudaFree(c->R);
     cudaFree(c->RT);
     cudaFree(c->P);
+    cudaFree(c->status);
+    cudaFree(c->tc_ops);
     delete c;
+    return KQ_OK;
+}
+
+extern "C" int kq_tq_status(const kq_tq_cache* c, uint32_t* status_out, void* stream) {
+    if (!c || !status_out) return KQ_ERR_ARG;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpyAsync(status_out, c->status, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return KQ_ERR_CUDA;
     return KQ_OK;
 }
 
@@ -780,6 +1052,7 @@ extern "C" int kq_tq_append(kq_tq_cache* c, const void* keys, const void* values
     p.len = c->len;
     p.Dr = c->Dr;
     p.R = c->R;
+    p.RT = c->RT;  // the tensor-core path stages R^T as its B operand
     p.P = c->P;
     for (int w = 0; w < 2; ++w) {
         p.packed[w] = c->packed[w];
@@ -787,7 +1060,13 @@ extern "C" int kq_tq_append(kq_tq_cache* c, const void* keys, const void* values
         p.zero[w] = c->zero[w];
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const cudaError_t e = c->D == 128 ? launch_append<128>(p, s) : launch_append<64>(p, s);
+    p.status = c->status;
+    p.tc_ops = c->tc_ops;
+    // Below 2048 vectors (a decode step's few tokens) the FMA kernel's shorter
+    // start-up wins; bulk appends go to the tensor cores.
+    const long nvec = 2L * c->B * c->H * T;
+    const cudaError_t e = c->D == 128 ? (nvec >= 2048 ? launch_append_tc(p, s) : launch_append<128>(p, s))
+                                      : launch_append<64>(p, s);
     if (e != cudaSuccess) return KQ_ERR_CUDA;
     c->len += T;
     return KQ_OK;
