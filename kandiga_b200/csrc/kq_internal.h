@@ -84,6 +84,25 @@ cudaError_t raise_smem_limit(const void* kernel, size_t bytes);
 int load_bkex_dir(const char* packed_dir, int num_layers, cudaStream_t s, kq_table** out, BkexInfo* info,
                   int extra_experts = 0);
 
+// Launch `kern` as a programmatic dependent of the kernel before it on the
+// stream: it may start before that kernel ends and must call
+// griddepcontrol.wait (pdl_wait) before touching what that kernel writes.
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch_dep(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                     Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // Workspace carve-up for kq_moe_* (offsets in bytes, 256-aligned).
 struct MoeWs {
     size_t status, idx, w, act, amax, total;

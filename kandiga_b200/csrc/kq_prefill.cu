@@ -906,24 +906,6 @@ static bool make_kq_tmap(CUtensorMap* m, const void* layer, size_t layer_bytes, 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Launch as a programmatic dependent of the previous work on the stream: the
-// kernel is scheduled while its predecessor drains and waits (griddepcontrol)
-// for it to complete before it reads or writes global memory.
-template <typename... KArgs, typename... Args>
-static cudaError_t launch_dep(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
-                              Args... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, args...);
-}
 
 template <int BITS, int SB_DT>
 static cudaError_t launch_tc_t(const TcParams& p, const CUtensorMap (&tm)[4], const CUtensorMap& tkq, cudaStream_t s,

@@ -541,6 +541,7 @@ __global__ void __launch_bounds__(256) tq_rotate_q_kernel(TqAttParams p) {
     const int qh = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
     const int j = tid % D, half = tid / D;
     const int Hq = p.H * p.G;
+    pdl_launch_dependents();  // the attend kernel may start its copies now
     const size_t qoff = ((size_t)b * Hq + qh) * p.Dr;
     if (tid < D) qs[tid] = tid < p.Dr ? load_as_float(p.q, p.q_dtype, qoff + tid) : 0.f;
     __syncthreads();
@@ -621,6 +622,8 @@ __global__ void __launch_bounds__(TQ_ATT_THREADS) tq_attend_kernel(TqAttParams p
         bulk_g2s(vsc, p.scale[1] + row, fbytes, bar, pol);
         bulk_g2s(vze, p.zero[1] + row, fbytes, bar, pol);
     }
+    pdl_wait();  // q R is complete and visible (the chunk's copies are already in flight)
+    pdl_launch_dependents();
     for (int i = tid; i < G * (D + 1); i += TQ_ATT_THREADS)
         qr[i] = p.qrot[((size_t)b * Hq + (size_t)h * G) * (D + 1) + i];
     __syncthreads();
@@ -732,6 +735,7 @@ __global__ void __launch_bounds__(256) tq_combine_kernel(TqAttParams p) {
     const int qh = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int Hq = p.H * p.G;
     const float* part = p.part + ((size_t)b * Hq + qh) * p.nchunk * (D + 2);
+    pdl_wait();  // every chunk's partials are complete and visible
     float M = -INFINITY;
     for (int c = tid; c < p.nchunk; c += 256) M = fmaxf(M, part[(size_t)c * (D + 2) + D]);
     M = warp_max(M);
@@ -893,10 +897,14 @@ static cudaError_t launch_attend(const TqAttParams& p, dim3 grid, dim3 cgrid, cu
     const size_t smem = tq_att_smem<D>(TQ_MAXG);
     cudaError_t e = smem_attr_once(tq_attend_kernel<D>, smem, configured);
     if (e != cudaSuccess) return e;
+    // rotate-q -> attend -> combine as programmatic dependents: each kernel
+    // starts (the attend CTAs issue their chunk copies) while its predecessor
+    // finishes, and waits for it before reading its output
     tq_rotate_q_kernel<D><<<cgrid, 256, 0, s>>>(p);
-    tq_attend_kernel<D><<<grid, TQ_ATT_THREADS, tq_att_smem<D>(p.G), s>>>(p);
-    tq_combine_kernel<D><<<cgrid, 256, 0, s>>>(p);
-    return cudaGetLastError();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if ((e = launch_dep(tq_attend_kernel<D>, grid, dim3(TQ_ATT_THREADS), tq_att_smem<D>(p.G), s, p)) != cudaSuccess)
+        return e;
+    return launch_dep(tq_combine_kernel<D>, cgrid, dim3(256), (size_t)0, s, p);
 }
 
 }  // namespace kq
