@@ -791,11 +791,31 @@ __global__ void combine_kernel(const float* __restrict__ ys, const int32_t* __re
             }
         }
         if (out) {
+            float v[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                float v = acc[j];
-                if (residual) v = load_as_float(residual, out_dtype, (size_t)t * H + h + j) + v;
-                store_from_float(out, out_dtype, orow + h + j, v);
+            for (int j = 0; j < 4; ++j)
+                v[j] = residual ? load_as_float(residual, out_dtype, (size_t)t * H + h + j) + acc[j] : acc[j];
+            const size_t esz = out_dtype == KQ_DT_F32 ? 4 : 2;
+            const uintptr_t addr = reinterpret_cast<uintptr_t>(out) + (orow + h) * esz;
+            if (addr & (4 * esz - 1)) {  // a caller's buffer at an odd element offset
+#pragma unroll
+                for (int j = 0; j < 4; ++j) store_from_float(out, out_dtype, orow + h + j, v[j]);
+            } else if (out_dtype == KQ_DT_F32) {
+                *reinterpret_cast<float4*>(static_cast<float*>(out) + orow + h) = make_float4(v[0], v[1], v[2], v[3]);
+            } else {
+                // the four values in one 8-byte store (rows written to another GPU cross
+                // NVLink as whole sectors rather than as 2-byte pieces)
+                uint32_t w0, w1;
+                if (out_dtype == KQ_DT_F16) {
+                    const __half2 a = __floats2half2_rn(v[0], v[1]), b = __floats2half2_rn(v[2], v[3]);
+                    w0 = *reinterpret_cast<const uint32_t*>(&a);
+                    w1 = *reinterpret_cast<const uint32_t*>(&b);
+                } else {
+                    const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+                    w0 = *reinterpret_cast<const uint32_t*>(&a);
+                    w1 = *reinterpret_cast<const uint32_t*>(&b);
+                }
+                *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + orow + h) = make_uint2(w0, w1);
             }
         }
     }
