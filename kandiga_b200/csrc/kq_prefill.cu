@@ -765,15 +765,20 @@ __global__ void act_fixup_kernel(const uint32_t* __restrict__ act_flag, const in
 __global__ void combine_kernel(const float* __restrict__ ys, const int32_t* __restrict__ inv_pos,
                                const float* __restrict__ w, int T, int K, int H, void* out, void* out_per_k,
                                int out_dtype, const void* residual, void* const* __restrict__ out_rows) {
-    const int t = blockIdx.y;
     const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
     pdl_wait();  // the down projection is complete and visible
-    size_t orow = (size_t)t * H;
-    if (out_rows) {  // uniform over the CTA: one row per blockIdx.y
-        out = t < T ? out_rows[t] : nullptr;
-        orow = 0;
-    }
-    if (t < T && h < H && (out || out_per_k)) {
+    bool wrote = false;
+    // rows blockIdx.y, + gridDim.y, ... (one row a CTA unless the rows go to
+    // other GPUs: then a CTA takes several and fences once)
+    for (int t = blockIdx.y; t < T; t += gridDim.y) {
+        void* o = out;
+        size_t orow = (size_t)t * H;
+        if (out_rows) {  // uniform over the CTA
+            o = out_rows[t];
+            orow = 0;
+        }
+        if (h >= H || !(o || out_per_k)) continue;
+        wrote |= o != nullptr;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int k = 0; k < K; ++k) {
             const int pos = inv_pos[(size_t)t * K + k];
@@ -784,24 +789,24 @@ __global__ void combine_kernel(const float* __restrict__ ys, const int32_t* __re
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
                     store_from_float(out_per_k, out_dtype, ((size_t)t * K + k) * H + h + j, y[j]);
-            if (out) {
+            if (o) {
                 const float wk = w[(size_t)t * K + k];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) acc[j] += y[j] * wk;
             }
         }
-        if (out) {
+        if (o) {
             float v[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j)
                 v[j] = residual ? load_as_float(residual, out_dtype, (size_t)t * H + h + j) + acc[j] : acc[j];
             const size_t esz = out_dtype == KQ_DT_F32 ? 4 : 2;
-            const uintptr_t addr = reinterpret_cast<uintptr_t>(out) + (orow + h) * esz;
+            const uintptr_t addr = reinterpret_cast<uintptr_t>(o) + (orow + h) * esz;
             if (addr & (4 * esz - 1)) {  // a caller's buffer at an odd element offset
 #pragma unroll
-                for (int j = 0; j < 4; ++j) store_from_float(out, out_dtype, orow + h + j, v[j]);
+                for (int j = 0; j < 4; ++j) store_from_float(o, out_dtype, orow + h + j, v[j]);
             } else if (out_dtype == KQ_DT_F32) {
-                *reinterpret_cast<float4*>(static_cast<float*>(out) + orow + h) = make_float4(v[0], v[1], v[2], v[3]);
+                *reinterpret_cast<float4*>(static_cast<float*>(o) + orow + h) = make_float4(v[0], v[1], v[2], v[3]);
             } else {
                 // the four values in one 8-byte store (rows written to another GPU cross
                 // NVLink as whole sectors rather than as 2-byte pieces)
@@ -815,13 +820,13 @@ __global__ void combine_kernel(const float* __restrict__ ys, const int32_t* __re
                     w0 = *reinterpret_cast<const uint32_t*>(&a);
                     w1 = *reinterpret_cast<const uint32_t*>(&b);
                 }
-                *reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + orow + h) = make_uint2(w0, w1);
+                *reinterpret_cast<uint2*>(static_cast<uint16_t*>(o) + orow + h) = make_uint2(w0, w1);
             }
         }
     }
-    if (out_rows) {  // no thread of the CTA has returned above
-        __syncthreads();
-        if (threadIdx.x == 0 && out) __threadfence_system();
+    if (out_rows) {  // every thread of the CTA reaches this point
+        const int any = __syncthreads_or(wrote ? 1 : 0);
+        if (threadIdx.x == 0 && any) __threadfence_system();
     }
 }
 
@@ -1089,8 +1094,9 @@ int kq::moe_prefill_ex(const kq_table* t, int layer, const void* x, int x_dtype,
     p.mat_off = t->gateup_bytes;
     p.n_mt = H / 128;
     if (int rc = gemm(act_s, I)) return rc;
-    // combine / per-k outputs
-    dim3 grid((H / 4 + 255) / 256, T);
+    // combine / per-k outputs (rows going to other GPUs: at most 128 CTA rows, so
+    // a CTA fences once after several rows)
+    dim3 grid((H / 4 + 255) / 256, out_rows ? std::min(T, 128) : T);
     return launch_dep(combine_kernel, grid, dim3(256), 0, s, (const float*)ys, (const int32_t*)inv_pos,
                       (const float*)w_use, T, K, H, out, out_per_k, out_dtype, residual, out_rows) == cudaSuccess
                ? KQ_OK
