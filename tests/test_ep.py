@@ -127,3 +127,75 @@ def test_balanced_placement_properties():
     for r in range(8):
         ids = pl.experts_of(r)
         assert np.array_equal(pl.local[ids], np.arange(len(ids)))
+
+
+class _FakeEpLib:
+    """Stand-in for the five libkq calls PeerExchange makes on the host side
+    (the real ones allocate and map device memory)."""
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.connected = None
+
+    def kq_ep_create(self, rank, world, max_tokens, hidden, top_k, dtype, out):
+        out._obj.value = 1000 + rank
+        return 0
+
+    def kq_ep_ipc_handle(self, h, buf):
+        import ctypes
+        ctypes.memmove(buf, bytes([h.value - 1000]) * 64, 64)
+        return 0
+
+    def kq_ep_connect(self, h, blob):
+        self.connected = bytes(blob)
+        return 0
+
+    def kq_ep_destroy(self, h):
+        pass
+
+
+def peer_worker(rank, world, port, q):
+    import kandiga_b200._native as N
+    from kandiga_b200 import ep as EP
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        fake = _FakeEpLib(rank)
+        N.load = lambda *a, **k: fake  # the exchange object binds whatever load() returns
+        ex = EP.PeerExchange(rank, world, 16, 1024, 4)
+        ex.connect()
+        q.put((rank, fake.connected))
+        ex.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_peer_exchange_handles_in_rank_order(world):
+    """PeerExchange.connect gathers every rank's 64-byte IPC handle over the
+    process group and passes them to kq_ep_connect in rank order."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=peer_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    want = b"".join(bytes([r]) * 64 for r in range(world))
+    assert all(got[r] == want for r in range(world))
+
+
+def test_peer_moe_checks_slot_count():
+    """The exchange's slots must be top_k, or top_k + 1 with a shared expert."""
+    from kandiga_b200 import ep as EP
+
+    class Ex:
+        top_k = 8
+        handle = None
+
+    with pytest.raises(ValueError):
+        EP.PeerExpertParallelMoE(EP.ExpertPlacement.contiguous(8, 1), 0, 8, None, Ex(), shared_id=8)
