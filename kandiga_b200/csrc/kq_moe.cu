@@ -131,28 +131,46 @@ __device__ __forceinline__ float block_stage_x(const GemvParams& p, int vec, int
 
 // ---- qunit_kernel: gate/up and dense matrices ---------------------------------------------
 
-template <int BITS, int NW, int NBUF>
+// Tile slots of a CTA: NBUF per warp, reused round-robin, one mbarrier each;
+// or, with PA ("prefetch all"), one per tile of the CTA's RT row tiles in the
+// matrix's own order, filled by one bulk copy per row tile (its nst tiles are
+// contiguous) issued before the programmatic-dependent-launch wait, one
+// mbarrier per row tile.  A copy engine completes a few bulk copies per
+// microsecond per SM whatever their size, so whole rows (18-64 KB) instead of
+// 3.5 KB tiles keep it off the critical path.
+template <int NW, int NBUF, int RT, bool PA>
+__host__ __device__ constexpr int qunit_slots(int nst) {
+    return PA ? RT * nst : NW * NBUF;
+}
+template <int NW, int NBUF, int RT, bool PA>
+__host__ __device__ constexpr int qunit_bars(int nst) {
+    return PA ? RT : NW * NBUF;
+}
+
+template <int BITS, int NW, int NBUF, int RT = 1, bool PA = false>
 __host__ __device__ constexpr size_t qunit_smem(int nst) {
-    return align_up((size_t)NW * NBUF * TileT<BITS>::BYTES, 128) +     // tiles
+    return align_up((size_t)qunit_slots<NW, NBUF, RT, PA>(nst) * TileT<BITS>::BYTES, 128) +  // tiles
            align_up((size_t)nst * TILE_COLS * 2, 128) +                  // xs
            align_up((size_t)nst * TILE_GROUPS * 8, 128) +                // cx
            align_up((size_t)NW * 32 * 8, 128) +                          // warp partials
-           align_up((size_t)NW * NBUF * 8, 128) +                        // mbarriers
+           align_up((size_t)qunit_bars<NW, NBUF, RT, PA>(nst) * 8, 128) +   // mbarriers
            256;                                                           // scratch
 }
 
 // RT > 1 (dense matrices only): RT row tiles per CTA, NW / RT warps each,
-// sharing one staged input.
-template <int BITS, int SB_DT, int NW, int NBUF, int RT = 1>
+// sharing one staged input.  PA (dense matrices only): every tile of the CTA
+// has its own slot, so no copy is issued after the wait.
+template <int BITS, int SB_DT, int NW, int NBUF, int RT = 1, bool PA = false>
 __global__ void __launch_bounds__(NW * 32) qunit_kernel(const GemvParams p) {
     constexpr int WPG = NW / RT;  // warps per row tile
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int TB = TileT<BITS>::BYTES;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int npad = p.nst * TILE_COLS, ng = npad / GS;
+    const int nslot = qunit_slots<NW, NBUF, RT, PA>(p.nst), nbar = qunit_bars<NW, NBUF, RT, PA>(p.nst);
     uint8_t* sp = smem;
     uint8_t* tiles = sp;
-    sp += align_up((size_t)NW * NBUF * TB, 128);
+    sp += align_up((size_t)nslot * TB, 128);
     __half* xs = reinterpret_cast<__half*>(sp);
     sp += align_up((size_t)npad * 2, 128);
     float2* cx = reinterpret_cast<float2*>(sp);
@@ -160,7 +178,7 @@ __global__ void __launch_bounds__(NW * 32) qunit_kernel(const GemvParams p) {
     float2* red = reinterpret_cast<float2*>(sp);
     sp += align_up((size_t)NW * 32 * 8, 128);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sp);
-    sp += align_up((size_t)NW * NBUF * 8, 128);
+    sp += align_up((size_t)nbar * 8, 128);
     float* scratch = reinterpret_cast<float*>(sp);   // 2*NW floats
     int* s_e = reinterpret_cast<int*>(sp + 192);     // expert id of this unit
 
@@ -174,10 +192,8 @@ __global__ void __launch_bounds__(NW * 32) qunit_kernel(const GemvParams p) {
     const int rt = (u % nrtc) * RT + grp;    // this warp's row tile
     const bool rt_ok = rt < p.nrt;
     const int t = tk / p.K, k = tk % p.K;
-    uint8_t* my_tiles = tiles + (size_t)warp * NBUF * TB;
-    uint64_t* my_bars = bars + warp * NBUF;
     if (tid == 0) {  // every warp's barriers, so warp 0 may issue copies for all of them
-        for (int b = 0; b < NW * NBUF; ++b) mbar_init(&bars[b], 1);
+        for (int b = 0; b < nbar; ++b) mbar_init(&bars[b], 1);
         fence_mbar_init();
     }
     __syncthreads();
@@ -188,13 +204,24 @@ __global__ void __launch_bounds__(NW * 32) qunit_kernel(const GemvParams p) {
         return wl < p.nst ? (p.nst - 1 - wl) / WPG + 1 : 0;
     };
     const int ntl = ntiles_of(warp);
+    // slot of warp w's i-th tile (column tile w % WPG + i * WPG of its row tile)
+    auto slot_of = [&](int w, int i) {
+        return PA ? (w / WPG) * p.nst + w % WPG + i * WPG : w * NBUF + i % NBUF;
+    };
     const uint64_t pol = policy_evict_first();
-    auto issue_for = [&](int w, int i, const uint8_t* mb) {
-        const int st = w % WPG + i * WPG, slot = i % NBUF;
+    auto issue_for = [&](int w, int i, const uint8_t* mb) {  // per-warp ring (not PA)
+        const int st = w % WPG + i * WPG, slot = slot_of(w, i);
         const int rtw = (u % nrtc) * RT + w / WPG;
-        uint64_t* bar = bars + w * NBUF + slot;
+        uint64_t* bar = bars + slot;
         mbar_expect_tx(bar, TB);
-        bulk_g2s(tiles + ((size_t)w * NBUF + slot) * TB, mb + ((size_t)rtw * p.nst + st) * TB, TB, bar, pol);
+        bulk_g2s(tiles + (size_t)slot * TB, mb + ((size_t)rtw * p.nst + st) * TB, TB, bar, pol);
+    };
+    auto issue_row = [&](int g, const uint8_t* mb) {  // PA: row tile g of the CTA, all its tiles
+        const int rtw = (u % nrtc) * RT + g;
+        if (rtw >= p.nrt) return;
+        const uint32_t bytes = (uint32_t)p.nst * TB;
+        mbar_expect_tx(&bars[g], bytes);
+        bulk_g2s(tiles + (size_t)g * p.nst * TB, mb + (size_t)rtw * p.nst * TB, bytes, &bars[g], pol);
     };
 
     bool valid = true;
@@ -221,8 +248,12 @@ __global__ void __launch_bounds__(NW * 32) qunit_kernel(const GemvParams p) {
             if (lane == 0) {
                 *s_e = e;
                 const uint8_t* mb = mbase + (size_t)((unsigned)e < (unsigned)p.E ? e : 0) * p.expert_bytes;
-                for (int w = 0; w < NW; ++w)
-                    for (int i = 0; i < NBUF && i < ntiles_of(w); ++i) issue_for(w, i, mb);
+                if constexpr (PA) {
+                    for (int g = 0; g < RT; ++g) issue_row(g, mb);
+                } else {
+                    for (int w = 0; w < NW; ++w)
+                        for (int i = 0; i < NBUF && i < ntiles_of(w); ++i) issue_for(w, i, mb);
+                }
             }
         } else {
             const float iv = block_stage_x<BITS>(p, t, npad, xs, cx, scratch, 32, (NW - 1) * 32);
@@ -238,8 +269,13 @@ __global__ void __launch_bounds__(NW * 32) qunit_kernel(const GemvParams p) {
         }
         mbase += (size_t)e * p.expert_bytes;
     } else {
-        if (lane == 0)  // dense weights do not depend on earlier work: fetch before the wait
-            for (int i = 0; i < NBUF && i < ntl; ++i) issue_for(warp, i, mbase);
+        if (lane == 0) {  // dense weights do not depend on earlier work: fetch before the wait
+            if constexpr (PA) {
+                if (wg == 0) issue_row(grp, mbase);
+            } else {
+                for (int i = 0; i < NBUF && i < ntl; ++i) issue_for(warp, i, mbase);
+            }
+        }
         pdl_wait();
         pdl_launch_dependents();
         inv = block_stage_x<BITS>(p, tk, npad, xs, cx, scratch, 0, NW * 32);
@@ -247,13 +283,14 @@ __global__ void __launch_bounds__(NW * 32) qunit_kernel(const GemvParams p) {
     }
 
     float y0 = 0.f, y1 = 0.f;
+    if (PA && ntl > 0) mbar_wait(&bars[grp], 0u, p.status);
     for (int i = 0; i < ntl; ++i) {
-        const int slot = i % NBUF;
-        mbar_wait(&my_bars[slot], (uint32_t)((i / NBUF) & 1), p.status);
+        const int slot = slot_of(warp, i);
+        if (!PA) mbar_wait(&bars[slot], (uint32_t)((i / NBUF) & 1), p.status);
         TileRegs<BITS> R;
-        tile_load<BITS>(my_tiles + (size_t)slot * TB, R);
+        tile_load<BITS>(tiles + (size_t)slot * TB, R);
         __syncwarp();
-        if (lane == 0 && i + NBUF < ntl) {
+        if (!PA && lane == 0 && i + NBUF < ntl) {
             fence_proxy_async_smem();
             issue_for(warp, i + NBUF, mbase);
         }
@@ -472,10 +509,10 @@ static cudaError_t launch_down_t(const GemvParams& p, cudaStream_t s) {
 #define KQ_WIDE_MIN_NST 8  // column tiles from which a matrix gets wide CTAs
 #endif
 
-template <int BITS, int SB_DT, int NW, int NBUF, int RT = 1>
+template <int BITS, int SB_DT, int NW, int NBUF, int RT = 1, bool PA = false>
 static cudaError_t launch_dense_nw(const GemvParams& p, cudaStream_t s) {
-    auto kern = qunit_kernel<BITS, SB_DT, NW, NBUF, RT>;
-    const size_t smem = qunit_smem<BITS, NW, NBUF>(p.nst);
+    auto kern = qunit_kernel<BITS, SB_DT, NW, NBUF, RT, PA>;
+    const size_t smem = qunit_smem<BITS, NW, NBUF, RT, PA>(p.nst);
     cudaError_t err = smem_attr(kern, smem, nullptr);
     if (err != cudaSuccess) return err;
     const long units = (long)p.T * p.K * ((p.nrt + RT - 1) / RT);
@@ -489,11 +526,31 @@ static cudaError_t launch_dense_nw(const GemvParams& p, cudaStream_t s) {
 #define KQ_SHORT_NBUF 1
 #endif
 
-// Long rows (K >= 4096) with few row tiles (one wave at two CTAs per SM) get
-// 16 warps per CTA: each thread stages and multiplies a quarter as much.
+#ifndef KQ_DENSE_PA
+#define KQ_DENSE_PA 1
+#endif
+#ifndef KQ_PA_NW
+#define KQ_PA_NW 16
+#endif
+constexpr size_t PA_MAX_TILE_BYTES = 100 * 1024;  // tile slots of one CTA in prefetch-all mode
+
+// Prefetch-all (a matrix row of at most PA_MAX_TILE_BYTES): every tile of a
+// CTA is in flight before the wait, so after the previous launch completes
+// only the input staging and the arithmetic remain.  RT is the smallest of 1,
+// 2, 4 that fits the launch in one wave at two CTAs per SM.
+// Otherwise: long rows (K >= 4096) with few row tiles (one wave at two CTAs per
+// SM) get 16 warps per CTA: each thread stages and multiplies a quarter as much.
 template <int BITS, int SB_DT>
 static cudaError_t launch_dense_t(const GemvParams& p, cudaStream_t s) {
     const long units = (long)p.T * p.K * p.nrt;
+    const size_t row_bytes = (size_t)p.nst * TileT<BITS>::BYTES;
+    if (KQ_DENSE_PA && row_bytes <= PA_MAX_TILE_BYTES) {
+        if (units <= 2L * 148 || 2 * row_bytes > PA_MAX_TILE_BYTES)
+            return launch_dense_nw<BITS, SB_DT, KQ_PA_NW, 1, 1, true>(p, s);
+        if (units <= 4L * 148 || 4 * row_bytes > PA_MAX_TILE_BYTES)
+            return launch_dense_nw<BITS, SB_DT, KQ_PA_NW, 1, 2, true>(p, s);
+        return launch_dense_nw<BITS, SB_DT, KQ_PA_NW, 1, 4, true>(p, s);
+    }
     if (p.nst >= KQ_WIDE_MIN_NST && units <= 2L * 148) return launch_dense_nw<BITS, SB_DT, 16, 1>(p, s);
     if (KQ_SHORT_RT > 1 && p.nst < KQ_WIDE_MIN_NST && units > 2L * 148)
         return launch_dense_nw<BITS, SB_DT, 4 * KQ_SHORT_RT, KQ_SHORT_NBUF, KQ_SHORT_RT>(p, s);

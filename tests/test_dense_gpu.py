@@ -30,16 +30,19 @@ def qmat_from(bits, rows, cols, seed, sb="f16", pair=False):
     return q, mats
 
 
-@pytest.mark.parametrize("bits,rows,cols", [(3, 512, 2560), (4, 256, 2048), (3, 2560, 9216), (3, 4096, 2560)])
-def test_dense_gemv_matches_oracle(gpu, bits, rows, cols):
+@pytest.mark.parametrize("bits,rows,cols,T", [(3, 512, 2560, 2), (4, 256, 2048, 2), (3, 2560, 9216, 2),
+                                              (3, 4096, 2560, 2), (3, 6144, 2560, 2), (4, 4112, 2048, 3)])
+def test_dense_gemv_matches_oracle(gpu, bits, rows, cols, T):
+    """Launch shapes with 1, 2 and 4 row tiles per CTA; 4112 rows (257 row
+    tiles) leave the last CTA of each token one row tile."""
     q, mats = qmat_from(bits, rows, cols, seed=rows + cols)
     p, s, b = mats[0]
     w, ss, bb = q.unpack_mlx(0)
     assert np.array_equal(w.cpu().numpy().reshape(-1), p.view(np.uint8).reshape(-1))
     assert np.array_equal(ss.cpu().numpy().view(np.uint16), s)
-    x = np.random.RandomState(1).randn(2, cols).astype(np.float16)
+    x = np.random.RandomState(1).randn(T, cols).astype(np.float16)
     y = q(torch.from_numpy(x).cuda(), out_dtype=torch.float32).cpu().numpy()
-    for t in range(2):
+    for t in range(T):
         ref = O.matvec(bits, p, s, b, x[t].astype(np.float32), "f16")
         assert rel_l2(y[t], ref) < 2e-3
 
