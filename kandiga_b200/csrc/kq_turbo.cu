@@ -500,7 +500,7 @@ __global__ void tq_export_kernel(const uint8_t* __restrict__ packed, const float
 // placed in the mantissa under the exponent of 1.0 (no int-to-float convert).
 __device__ __forceinline__ float nib_1p(uint32_t w, int k) {
     const uint32_t b = k <= 4 ? (w << (19 - 4 * k)) : (w >> (4 * k - 19));
-    return __uint_as_float((b & 0x00780000u) | 0x3F800000u);
+    return __uint_as_float(and_or(b, 0x00780000u, 0x3F800000u));  // one lop3, not an AND and an OR
 }
 
 #ifndef KQ_TQ_ATT_THREADS
