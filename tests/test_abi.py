@@ -68,6 +68,14 @@ def test_argument_validation_without_device(lib):
     assert lib.bakan_cpu_expert_mlp_f16(None, 0, None, None, 8, None) == -1
 
 
+def test_integration_guide_lists_every_entry_point():
+    """INTEGRATION.md's appendix gives the ctypes signature of every bound entry point."""
+    from kandiga_b200 import _native
+    guide = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    missing = [n for n in _native.SIGNATURES if f"\n{n}: " not in guide]
+    assert not missing, missing
+
+
 def test_product_package_does_not_import_oracle():
     for py in glob.glob(os.path.join(ROOT, "kandiga_b200", "**", "*.py"), recursive=True):
         src = open(py).read()
