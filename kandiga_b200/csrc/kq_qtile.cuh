@@ -97,10 +97,9 @@ __device__ __forceinline__ uint32_t pair_of(const uint32_t* wd, const uint32_t* 
             return and_or(src, mask, magic2(k));
         } else {
             constexpr int b = (J - 30) * 3;
-            uint32_t v = ((wd[b] >> 15) & 0x00010001u) | magic2(0);
-            v |= (wd[b + 1] >> 14) & 0x00020002u;
-            v |= (wd[b + 2] >> 13) & 0x00040004u;
-            return v;
+            uint32_t v = and_or(wd[b] >> 15, 0x00010001u, magic2(0));
+            v = and_or(wd[b + 1] >> 14, 0x00020002u, v);
+            return and_or(wd[b + 2] >> 13, 0x00040004u, v);
         }
     } else {
         constexpr int w = J / 4, s = J % 4;
